@@ -1,0 +1,132 @@
+/*
+ * kokoro_b200.h -- C ABI of the B200-native Kokoro-82M batched ragged forward.
+ *
+ * This boundary replaces the reference crate's GPU layer: the Rust side keeps `Engine`
+ * (src/engine.rs) and binds these symbols in place of `Gpu::new` + `GpuKokoro::with_gpu`
+ * (src/gpu.rs:81-105, :685-724) and `GpuKokoro::forward_batch` (src/gpu_batch.rs:179-421).
+ * Plain pointers and sizes only; no C++ or CUDA types cross it.
+ *
+ * Conventions (mirroring the reference's contract, src/gpu_batch.rs:14-24, src/engine.rs:190-241):
+ *  - Status codes instead of panics; kk_last_error() gives the message of the last failure.
+ *  - An engine is bound to one CUDA device and one stream and is NOT thread-safe: use one
+ *    handle per GPU per host thread (the reference runs one GPU thread, src/cli.rs:625).
+ *  - Host buffers belong to the caller. Device memory comes from a per-engine arena that grows
+ *    on demand and is reused across calls; an allocation failure returns KK_ERR_OOM so the
+ *    caller's split-the-batch-in-half policy (src/engine.rs:229-234) still works.
+ *  - Results are per item, in input order.
+ */
+#ifndef KOKORO_B200_H
+#define KOKORO_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#if defined(__GNUC__)
+#define KK_API __attribute__((visibility("default")))
+#else
+#define KK_API
+#endif
+
+typedef enum {
+  KK_OK = 0,
+  KK_ERR_INVALID_ARG = 1, /* bad shapes / ids / speed (src/gpu_batch.rs:183-187) */
+  KK_ERR_OOM = 2,         /* device or pinned-host allocation failed */
+  KK_ERR_CUDA = 3,        /* any other CUDA runtime error */
+  KK_ERR_TIMEOUT = 4,     /* a bounded in-kernel wait (LSTM step barrier) gave up */
+  KK_ERR_IO = 5           /* weight file missing, unreadable or malformed */
+} kk_status;
+
+typedef enum {
+  KK_PRECISION_FP32 = 0, /* fp32 everywhere (SIMT FFMA); the parity path */
+  KK_PRECISION_BF16 = 1  /* bf16 tensor-core (tcgen05) convs and GEMMs, fp32 accumulation */
+} kk_precision;
+
+typedef struct kk_engine kk_engine;
+
+/* Model constants (src/model.rs:12-19, src/vocoder.rs:8-11). */
+#define KK_STYLE_DIM 128
+#define KK_REF_S_DIM 256
+#define KK_MAX_DUR 50
+#define KK_CONTEXT_LEN 512
+#define KK_SAMPLE_RATE 24000
+#define KK_SAMPLES_PER_FRAME 600
+#define KK_HARMONICS 9
+
+/*
+ * kk_create -- load a safetensors checkpoint (the reference's layout: raw state-dict names,
+ * weight_norm as weight_v/weight_g, AdaIN affine optional) onto CUDA device `cuda_ordinal`.
+ * Replaces Gpu::new (src/gpu.rs:81) + Weights::load (src/weights.rs:14) +
+ * Kokoro::from_weights (src/model.rs:122) + GpuKokoro::with_gpu (src/gpu.rs:685).
+ */
+KK_API kk_status kk_create(const char* safetensors_path, int cuda_ordinal, int precision, kk_engine** out);
+
+/* Release every device and host resource of the engine. NULL is a no-op. */
+KK_API void kk_destroy(kk_engine* e);
+
+/* Message of the last failure on this engine (or of the last kk_create when e is NULL). */
+KK_API const char* kk_last_error(const kk_engine* e);
+
+/* Engine identity string (part of the reference's resume keys, src/engine.rs:109-111). */
+KK_API const char* kk_identity(const kk_engine* e);
+
+/*
+ * kk_forward_batch -- the batched ragged forward (GpuKokoro::forward_batch,
+ * src/gpu_batch.rs:179; BatchItem src/gpu_batch.rs:19-24).
+ *
+ *  ids, ids_len   token ids of all items concatenated, pads included; ids_len[i] in [2, 512]
+ *  ref_s          [n_items][256] style vectors (128 decoder + 128 prosody)
+ *  speed          [n_items], finite and > 0
+ *  seeds          [n_items] counter-noise seeds (ItemNoise::Counter), NULL = all zero
+ *  noise          NULL, or replayed sine-noise draws (ItemNoise::Fixed) for every item,
+ *                 concatenated, 600 * 9 * N_b floats per item; requires forced_dur
+ *  forced_dur     NULL, or per-token durations (>= 0, each item's sum >= 1), laid out like ids;
+ *                 replaces the predicted durations (vocoder comparison mode)
+ *  dur_out        [sum ids_len] durations used (predicted or forced), like ids; may be NULL
+ *  n_samples_out  [n_items] audio length of each item, 600 * sum(dur); may be NULL
+ *
+ * The audio stays in the engine until the next forward call: read it with kk_fetch_audio.
+ */
+KK_API kk_status kk_forward_batch(kk_engine* e, int n_items, const int64_t* ids, const int32_t* ids_len,
+                           const float* ref_s, const float* speed, const uint64_t* seeds,
+                           const float* noise, const int64_t* forced_dur, int64_t* dur_out,
+                           int64_t* n_samples_out);
+
+/* Copy item `item`'s audio of the last forward into `dst` (capacity `cap` floats). */
+KK_API kk_status kk_fetch_audio(kk_engine* e, int item, float* dst, int64_t cap);
+
+/*
+ * kk_decode_batch -- decoder + iSTFTNet generator only (the reference's
+ * `decoder(asr, F0, N, ref_s[:, :128])`, src/gpu_batch.rs:299-420) on a ragged batch.
+ *
+ *  n_frames   [n_items] N_b frames per item (>= 1)
+ *  asr        [sum N_b][512] aligned text features, time-major, items concatenated
+ *  f0, n      [sum 2 N_b] F0 and N curves
+ *  s_dec      [n_items][128] decoder styles
+ *  seeds      [n_items] counter-noise seeds, NULL = all zero; noise: NULL or replayed draws
+ *  audio_out  [sum 600 N_b] samples, items concatenated; may be NULL (audio kept on device)
+ */
+KK_API kk_status kk_decode_batch(kk_engine* e, int n_items, const int32_t* n_frames, const float* asr,
+                          const float* f0, const float* n, const float* s_dec,
+                          const uint64_t* seeds, const float* noise, float* audio_out);
+
+/* Options (benchmark / diagnostics). */
+typedef enum {
+  KK_OPT_KEEP_AUDIO_ON_DEVICE = 1, /* 1: forward leaves audio on the device (no D2H) */
+  KK_OPT_SYNC_EACH_STAGE = 2       /* 1: synchronise after each stage (error localisation) */
+} kk_option;
+KK_API kk_status kk_set_option(kk_engine* e, int option, int64_t value);
+
+/* Bytes of device memory the engine currently holds (weights + arena). */
+KK_API int64_t kk_device_bytes(const kk_engine* e);
+
+/* Number of kernel launches issued by the engine since creation (counted on the host). */
+KK_API int64_t kk_launch_count(const kk_engine* e);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* KOKORO_B200_H */

@@ -1,0 +1,1309 @@
+// kokoro-b200 engine: weight hydration, per-engine device arena, and the batched ragged forward
+// behind the C ABI of include/kokoro_b200.h.
+//
+// The forward follows GpuKokoro::forward_batch (src/gpu_batch.rs:179-421) stage by stage, with
+// one B200-first change of representation: every activation is time-major ([rows][channels]),
+// so a convolution tap is a row offset, a linear layer is a 1-tap convolution, a channel concat
+// is a column range of one buffer, and the transposes of the reference disappear.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+#include <memory>
+#include <numeric>
+#include <string>
+#include <vector>
+
+#include "../../include/kokoro_b200.h"
+#include "kk_common.cuh"
+#include "kk_launch.h"
+#include "kk_tc.h"
+#include "kk_weights.h"
+
+namespace kk {
+
+#define KK_CUDA(expr)                                                                         \
+  do {                                                                                        \
+    cudaError_t _e = (expr);                                                                  \
+    if (_e != cudaSuccess) {                                                                  \
+      throw ::kk::KKError(_e == cudaErrorMemoryAllocation ? KK_ERR_OOM : KK_ERR_CUDA,               \
+                    std::string(#expr) + ": " + cudaGetErrorString(_e));                      \
+    }                                                                                         \
+  } while (0)
+
+#define KK_REQUIRE(cond, msg)                                   \
+  do {                                                          \
+    if (!(cond)) throw ::kk::KKError(KK_ERR_INVALID_ARG, (msg));      \
+  } while (0)
+
+// ------------------------------------------------------------------------------ device arena
+
+// Bump allocator over a chain of cudaMalloc'd blocks, kept across calls; mark/rewind give
+// stack-like reuse inside a forward (safe because all work is ordered on one stream).
+class Arena {
+ public:
+  ~Arena() { release(); }
+  void release() {
+    for (auto& b : blocks_) cudaFree(b.p);
+    blocks_.clear();
+    cur_ = 0;
+  }
+  void* alloc(size_t bytes) {
+    bytes = (bytes + 255) & ~size_t(255);
+    if (bytes == 0) bytes = 256;
+    while (cur_ < blocks_.size()) {
+      Block& b = blocks_[cur_];
+      if (b.used + bytes <= b.cap) {
+        void* p = b.p + b.used;
+        b.used += bytes;
+        return p;
+      }
+      cur_++;
+    }
+    size_t last = blocks_.empty() ? 0 : blocks_.back().cap;
+    size_t cap = std::max({bytes, 2 * last, size_t(256) << 20});
+    char* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, cap);
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      cap = bytes;
+      e = cudaMalloc(&p, cap);
+      if (e != cudaSuccess) {
+        cudaGetLastError();
+        throw KKError(KK_ERR_OOM, "device arena: cannot allocate " + std::to_string(bytes >> 20) + " MiB");
+      }
+    }
+    blocks_.push_back({p, cap, bytes});
+    cur_ = blocks_.size() - 1;
+    return p;
+  }
+  template <class T>
+  T* get(size_t n) {
+    return static_cast<T*>(alloc(n * sizeof(T)));
+  }
+  struct Mark {
+    size_t blk, used;
+  };
+  Mark mark() const { return {cur_, cur_ < blocks_.size() ? blocks_[cur_].used : 0}; }
+  void rewind(Mark m) {
+    for (size_t i = m.blk + 1; i < blocks_.size(); i++) blocks_[i].used = 0;
+    if (m.blk < blocks_.size()) blocks_[m.blk].used = m.used;
+    cur_ = m.blk;
+  }
+  void reset() {
+    for (auto& b : blocks_) b.used = 0;
+    cur_ = 0;
+  }
+  size_t bytes() const {
+    size_t s = 0;
+    for (auto& b : blocks_) s += b.cap;
+    return s;
+  }
+
+ private:
+  struct Block {
+    char* p;
+    size_t cap, used;
+  };
+  std::vector<Block> blocks_;
+  size_t cur_ = 0;
+};
+
+// Pinned host staging for the uploads and downloads of one call (reset per call).
+class PinnedArena {
+ public:
+  ~PinnedArena() {
+    for (auto& b : blocks_) cudaFreeHost(b.p);
+  }
+  void* alloc(size_t bytes) {
+    bytes = (bytes + 63) & ~size_t(63);
+    for (; cur_ < blocks_.size(); cur_++) {
+      if (blocks_[cur_].used + bytes <= blocks_[cur_].cap) {
+        void* p = blocks_[cur_].p + blocks_[cur_].used;
+        blocks_[cur_].used += bytes;
+        return p;
+      }
+    }
+    size_t cap = std::max(bytes, size_t(64) << 20);
+    char* p = nullptr;
+    if (cudaHostAlloc(&p, cap, cudaHostAllocDefault) != cudaSuccess) {
+      cudaGetLastError();
+      throw KKError(KK_ERR_OOM, "pinned host staging: cannot allocate " + std::to_string(cap >> 20) + " MiB");
+    }
+    blocks_.push_back({p, cap, bytes});
+    cur_ = blocks_.size() - 1;
+    return p;
+  }
+  void reset() {
+    for (auto& b : blocks_) b.used = 0;
+    cur_ = 0;
+  }
+
+ private:
+  struct Block {
+    char* p;
+    size_t cap, used;
+  };
+  std::vector<Block> blocks_;
+  size_t cur_ = 0;
+};
+
+// ------------------------------------------------------------------------------ model
+
+struct Conv {
+  int cin = 0, cout = 0, K = 1, dil = 1, pad = 0, stride = 1;
+  float* w = nullptr;  // fp32 [K][cin][cout]
+  float* b = nullptr;
+  TcWeights tc;        // bf16 tcgen05 operand layout (BF16 precision only)
+};
+struct AdaIN {
+  float* nw = nullptr;
+  float* nb = nullptr;
+  int off = 0;  // column offset of this layer's gamma|beta in the fused per-item fc output
+  int c = 0;
+};
+struct ResBlk {
+  int din = 0, dout = 0;
+  bool up = false, has_sc = false;
+  Conv c1, c2, sc;
+  AdaIN n1, n2;
+  float* pool_w = nullptr;
+  float* pool_b = nullptr;
+};
+struct SnakeBlk {
+  int c = 0, k = 0;
+  Conv c1[3], c2[3];
+  AdaIN a1[3], a2[3];
+  float* al1[3];
+  float* al2[3];
+};
+struct Lstm {
+  Conv ih;  // both directions: cout = 2 * 4H (W_ih fwd | W_ih reverse), bias b_ih
+  float* whh = nullptr;
+  float* bhh = nullptr;
+};
+
+struct Model {
+  float *word, *pos, *tt0, *emb_g, *emb_b;
+  Conv map_in, qkv, dense, ffn, ffn_out;
+  float *attn_g, *attn_b, *full_g, *full_b;
+  Conv bert_enc;
+  Lstm dur_lstm[3];
+  int adaln_off[3];
+  Lstm pred_lstm, shared, te_lstm;
+  Conv dur_proj;
+  ResBlk f0[3], nn[3];
+  Conv f0_proj, n_proj;
+  float* te_emb;
+  Conv te_cnn[3];
+  float *te_g[3], *te_b[3];
+  ResBlk enc, dec[4];
+  float *f0conv_w, *nconv_w;
+  float f0conv_b, nconv_b;
+  Conv asr_res;
+  float* lw;
+  float lb;
+  Conv noise0, noise1, ups[2], post;
+  SnakeBlk noise_res[2], rb[6];
+  Conv fc_dec, fc_pro;  // all AdaIN / AdaLN style projections fused: cin 128, cout = sum of 2C
+};
+
+static const int DILS[3] = {1, 3, 5};
+
+struct Engine {
+  int dev = 0;
+  int precision = KK_PRECISION_FP32;
+  cudaStream_t st = nullptr;
+  Model m{};
+  std::vector<void*> wallocs;
+  size_t wbytes = 0;
+  Arena ar;
+  PinnedArena pin;
+  std::string err;
+  std::string ident;
+  bool keep_audio_dev = false, sync_each = false;
+  long long launches = 0;
+  int* err_flag = nullptr;
+  bool tc_ok = false;
+  // results of the last forward
+  float* audio_host = nullptr;
+  size_t audio_host_cap = 0;
+  std::vector<long long> out_off, out_len;
+
+  ~Engine();
+  // -- load
+  float* up(const std::vector<float>& v);
+  Conv conv_from(const std::vector<float>& w, const float* bias_h, int cin, int cout, int K, int dil, int pad,
+                 int stride);
+  Conv load_conv(const Checkpoint& ck, const std::string& p, int cin, int cout, int K, int dil, int pad, int stride,
+                 bool bias);
+  Conv load_linear(const Checkpoint& ck, const std::string& p, int din, int dout, bool bias = true);
+  AdaIN load_adain(const Checkpoint& ck, const std::string& p, int c, std::vector<float>& fcw, std::vector<float>& fcb);
+  ResBlk load_resblk(const Checkpoint& ck, const std::string& p, int din, int dout, bool up, std::vector<float>& fcw,
+                     std::vector<float>& fcb);
+  SnakeBlk load_snake(const Checkpoint& ck, const std::string& p, int c, int k, std::vector<float>& fcw,
+                      std::vector<float>& fcb);
+  Lstm load_lstm(const Checkpoint& ck, const std::string& p, int din);
+  void load(const Checkpoint& ck);
+  // -- forward helpers
+  template <class T>
+  T* upload(const T* h, size_t n);
+  void check(cudaError_t e, const char* what);
+  void dump(const char* name, const void* p, long long rows, int cols, int ld);
+  void stage_sync(const char* what);
+  ConvArgs ca(const Conv& c);
+  void run_conv(const Conv& c, ConvArgs& a);
+  void stats(const float* x, int ldx, int C, const Dom& d, const ItemTab* items, int B, int max_len, float** mean,
+             float** rstd);
+  void adain_args(ConvArgs& a, const AdaIN& n, const float* mean, const float* rstd, const float* gb, int ldgb, int mode,
+                  float slope, const float* alpha);
+  void resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, const Dom& dout, float* y, int ldy,
+              const float* gb, int ldgb, const ItemTab* items, int B, int max_n);
+  void snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d, const float* gb, int ldgb,
+             const ItemTab* items, int B, int max_n);
+  void lstm(const Lstm& L, const float* x, int ldx, int rows, const std::vector<int>& start,
+            const std::vector<int>& len, float* out, int ldo);
+  void linear(const Conv& c, const float* x, int ldx, int rows, float* y, int ldy, int out_mode = OUT_STORE,
+              const float* sc = nullptr, int ldsc = 0);
+  float* decode_core(int B, const std::vector<ItemTab>& items_h, const ItemTab* items, const int* col_item_n, int LN,
+                     float* xcat0, float* f0, float* nc, const float* gb_dec, int ldgb, const uint64_t* seeds_d,
+                     const float* noise_d, const long long* noise_off_d);
+  void finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h);
+  void forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
+               const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
+               int64_t* nsamp_out);
+  void decode(int B, const int32_t* n_frames, const float* asr, const float* f0, const float* n, const float* s_dec,
+              const uint64_t* seeds, const float* noise, float* audio_out);
+};
+
+Engine::~Engine() {
+  if (dev >= 0) cudaSetDevice(dev);
+  if (st) cudaStreamSynchronize(st);
+  for (void* p : wallocs) cudaFree(p);
+  ar.release();
+  if (audio_host) cudaFreeHost(audio_host);
+  if (st) cudaStreamDestroy(st);
+}
+
+float* Engine::up(const std::vector<float>& v) {
+  float* p = nullptr;
+  KK_CUDA(cudaMalloc(&p, std::max<size_t>(v.size(), 1) * sizeof(float)));
+  wallocs.push_back(p);
+  wbytes += v.size() * sizeof(float);
+  KK_CUDA(cudaMemcpy(p, v.data(), v.size() * sizeof(float), cudaMemcpyHostToDevice));
+  return p;
+}
+
+// w: torch layout [cout][cin][K] -> fp32 [K][cin][cout] (+ the bf16 tcgen05 layout in BF16 mode)
+Conv Engine::conv_from(const std::vector<float>& w, const float* bias_h, int cin, int cout, int K, int dil, int pad,
+                       int stride) {
+  Conv c;
+  c.cin = cin, c.cout = cout, c.K = K, c.dil = dil, c.pad = pad, c.stride = stride;
+  std::vector<float> t((size_t)K * cin * cout);
+  for (int co = 0; co < cout; co++)
+    for (int ci = 0; ci < cin; ci++)
+      for (int k = 0; k < K; k++) t[((size_t)k * cin + ci) * cout + co] = w[((size_t)co * cin + ci) * K + k];
+  c.w = up(t);
+  if (bias_h) c.b = up(std::vector<float>(bias_h, bias_h + cout));
+  if (precision == KK_PRECISION_BF16 && tc_ok) {
+    KK_CUDA(tc_make_weights(w.data(), cin, cout, K, &c.tc));
+    wallocs.push_back(c.tc.w);
+    wbytes += c.tc.bytes;
+  }
+  return c;
+}
+
+Conv Engine::load_conv(const Checkpoint& ck, const std::string& p, int cin, int cout, int K, int dil, int pad,
+                       int stride, bool bias) {
+  std::vector<float> w = ck.conv_weight(p, {cout, cin, K});
+  std::vector<float> b;
+  if (bias) b = ck.get(p + ".bias", {cout});
+  return conv_from(w, bias ? b.data() : nullptr, cin, cout, K, dil, pad, stride);
+}
+
+Conv Engine::load_linear(const Checkpoint& ck, const std::string& p, int din, int dout, bool bias) {
+  std::vector<float> w = ck.get(p + ".weight", {dout, din});
+  std::vector<float> b;
+  if (bias) b = ck.get(p + ".bias", {dout});
+  return conv_from(w, bias ? b.data() : nullptr, din, dout, 1, 1, 0, 1);
+}
+
+// AdaIN1d (src/nn.rs:87-100): affine defaults, and fc rows appended to the fused projection.
+AdaIN Engine::load_adain(const Checkpoint& ck, const std::string& p, int c, std::vector<float>& fcw,
+                         std::vector<float>& fcb) {
+  AdaIN a;
+  a.c = c;
+  a.nw = up(ck.norm_affine(p + ".norm.weight", c, 1.0f));
+  a.nb = up(ck.norm_affine(p + ".norm.bias", c, 0.0f));
+  std::vector<float> w = ck.get(p + ".fc.weight", {2 * c, STYLE});
+  std::vector<float> b = ck.get(p + ".fc.bias", {2 * c});
+  a.off = (int)fcb.size();
+  fcw.insert(fcw.end(), w.begin(), w.end());
+  fcb.insert(fcb.end(), b.begin(), b.end());
+  return a;
+}
+
+// AdainResBlk1d (src/nn.rs:103-141)
+ResBlk Engine::load_resblk(const Checkpoint& ck, const std::string& p, int din, int dout, bool upb,
+                           std::vector<float>& fcw, std::vector<float>& fcb) {
+  ResBlk r;
+  r.din = din, r.dout = dout, r.up = upb;
+  r.c1 = load_conv(ck, p + ".conv1", din, dout, 3, 1, 1, 1, true);
+  r.c2 = load_conv(ck, p + ".conv2", dout, dout, 3, 1, 1, 1, true);
+  r.n1 = load_adain(ck, p + ".norm1", din, fcw, fcb);
+  r.n2 = load_adain(ck, p + ".norm2", dout, fcw, fcb);
+  r.has_sc = din != dout;
+  if (r.has_sc) r.sc = load_conv(ck, p + ".conv1x1", din, dout, 1, 1, 0, 1, false);
+  if (upb) {
+    r.pool_w = up(ck.conv_weight(p + ".pool", {din, 1, 3}));
+    r.pool_b = up(ck.get(p + ".pool.bias", {din}));
+  }
+  if (r.up && !r.has_sc) throw KKError(KK_ERR_IO, p + ": upsampling block without a 1x1 shortcut");
+  return r;
+}
+
+// AdaINResBlock1 (src/nn.rs:143-166)
+SnakeBlk Engine::load_snake(const Checkpoint& ck, const std::string& p, int c, int k, std::vector<float>& fcw,
+                            std::vector<float>& fcb) {
+  SnakeBlk s;
+  s.c = c, s.k = k;
+  for (int i = 0; i < 3; i++) {
+    int d = DILS[i];
+    s.c1[i] = load_conv(ck, p + ".convs1." + std::to_string(i), c, c, k, d, (k * d - d) / 2, 1, true);
+    s.c2[i] = load_conv(ck, p + ".convs2." + std::to_string(i), c, c, k, 1, (k - 1) / 2, 1, true);
+  }
+  for (int i = 0; i < 3; i++) s.a1[i] = load_adain(ck, p + ".adain1." + std::to_string(i), c, fcw, fcb);
+  for (int i = 0; i < 3; i++) s.a2[i] = load_adain(ck, p + ".adain2." + std::to_string(i), c, fcw, fcb);
+  for (int i = 0; i < 3; i++) s.al1[i] = up(ck.get(p + ".alpha1." + std::to_string(i), {1, c, 1}));
+  for (int i = 0; i < 3; i++) s.al2[i] = up(ck.get(p + ".alpha2." + std::to_string(i), {1, c, 1}));
+  return s;
+}
+
+// BiLSTM (src/nn.rs:170-189): W_ih of both directions stacked into one 1-tap conv (cout 2048).
+Lstm Engine::load_lstm(const Checkpoint& ck, const std::string& p, int din) {
+  const int H = 256;
+  Lstm l;
+  std::vector<float> wih, bih, whh, bhh;
+  for (const char* sfx : {"", "_reverse"}) {
+    auto a = ck.get(p + ".weight_ih_l0" + sfx, {4 * H, din});
+    auto b = ck.get(p + ".bias_ih_l0" + sfx, {4 * H});
+    auto c = ck.get(p + ".weight_hh_l0" + sfx, {4 * H, H});
+    auto d = ck.get(p + ".bias_hh_l0" + sfx, {4 * H});
+    wih.insert(wih.end(), a.begin(), a.end());
+    bih.insert(bih.end(), b.begin(), b.end());
+    whh.insert(whh.end(), c.begin(), c.end());
+    bhh.insert(bhh.end(), d.begin(), d.end());
+  }
+  l.ih = conv_from(wih, bih.data(), din, 8 * H, 1, 1, 0, 1);
+  l.whh = up(whh);
+  l.bhh = up(bhh);
+  return l;
+}
+
+// ConvTranspose1d(cin, cout, K, stride s, pad p) as a polyphase 3-tap convolution over the input
+// rows (pad 1): output row s*q + j, channel co, is column j*cout + co of input row q, with
+// W'[m][ci][j*cout + co] = W_T[ci][co][s*(1 - m) + j + p] when that tap index lies in [0, K).
+static void convT_polyphase(const std::vector<float>& wT, const std::vector<float>& b, int cin, int cout, int K, int s,
+                            int p, std::vector<float>& w_out, std::vector<float>& b_out) {
+  const int cp = s * cout;
+  w_out.assign((size_t)cp * cin * 3, 0.0f);  // torch layout [cp][cin][3]
+  for (int m = 0; m < 3; m++)
+    for (int j = 0; j < s; j++) {
+      int k = s * (1 - m) + j + p;
+      if (k < 0 || k >= K) continue;
+      for (int ci = 0; ci < cin; ci++)
+        for (int co = 0; co < cout; co++)
+          w_out[((size_t)(j * cout + co) * cin + ci) * 3 + m] = wT[((size_t)ci * cout + co) * K + k];
+    }
+  b_out.resize(cp);
+  for (int j = 0; j < s; j++)
+    for (int co = 0; co < cout; co++) b_out[j * cout + co] = b[co];
+}
+
+void Engine::load(const Checkpoint& ck) {
+  const std::string L = "bert.encoder.albert_layer_groups.0.albert_layers.0";
+  std::vector<float> fdw, fdb, fpw, fpb;  // fused style projections: decoder (s_dec), prosody (s_pro)
+  // ---- ALBERT (src/albert.rs:36-64)
+  m.word = up(ck.get("bert.embeddings.word_embeddings.weight", {178, 128}));
+  m.pos = up(ck.get("bert.embeddings.position_embeddings.weight", {512, 128}));
+  {
+    auto tt = ck.get("bert.embeddings.token_type_embeddings.weight", {2, 128});
+    tt.resize(128);
+    m.tt0 = up(tt);
+  }
+  m.emb_g = up(ck.get("bert.embeddings.LayerNorm.weight", {128}));
+  m.emb_b = up(ck.get("bert.embeddings.LayerNorm.bias", {128}));
+  m.map_in = load_linear(ck, "bert.encoder.embedding_hidden_mapping_in", 128, 768);
+  {
+    std::vector<float> w, b;
+    for (const char* n : {"query", "key", "value"}) {
+      auto a = ck.get(L + ".attention." + n + ".weight", {768, 768});
+      auto c = ck.get(L + ".attention." + n + ".bias", {768});
+      w.insert(w.end(), a.begin(), a.end());
+      b.insert(b.end(), c.begin(), c.end());
+    }
+    m.qkv = conv_from(w, b.data(), 768, 2304, 1, 1, 0, 1);
+  }
+  m.dense = load_linear(ck, L + ".attention.dense", 768, 768);
+  m.attn_g = up(ck.get(L + ".attention.LayerNorm.weight", {768}));
+  m.attn_b = up(ck.get(L + ".attention.LayerNorm.bias", {768}));
+  m.ffn = load_linear(ck, L + ".ffn", 768, 2048);
+  m.ffn_out = load_linear(ck, L + ".ffn_output", 2048, 768);
+  m.full_g = up(ck.get(L + ".full_layer_layer_norm.weight", {768}));
+  m.full_b = up(ck.get(L + ".full_layer_layer_norm.bias", {768}));
+  m.bert_enc = load_linear(ck, "bert_encoder", 768, 512);
+  // ---- predictor (src/model.rs:60-86)
+  for (int i = 0; i < 3; i++) {
+    m.dur_lstm[i] = load_lstm(ck, "predictor.text_encoder.lstms." + std::to_string(2 * i), 640);
+    auto w = ck.get("predictor.text_encoder.lstms." + std::to_string(2 * i + 1) + ".fc.weight", {1024, 128});
+    auto b = ck.get("predictor.text_encoder.lstms." + std::to_string(2 * i + 1) + ".fc.bias", {1024});
+    m.adaln_off[i] = (int)fpb.size();
+    fpw.insert(fpw.end(), w.begin(), w.end());
+    fpb.insert(fpb.end(), b.begin(), b.end());
+  }
+  m.pred_lstm = load_lstm(ck, "predictor.lstm", 640);
+  m.dur_proj = load_linear(ck, "predictor.duration_proj.linear_layer", 512, 50);
+  m.shared = load_lstm(ck, "predictor.shared", 640);
+  const char* names[2] = {"F0", "N"};
+  for (int s = 0; s < 2; s++) {
+    ResBlk* blk = s == 0 ? m.f0 : m.nn;
+    std::string p = std::string("predictor.") + names[s];
+    blk[0] = load_resblk(ck, p + ".0", 512, 512, false, fpw, fpb);
+    blk[1] = load_resblk(ck, p + ".1", 512, 256, true, fpw, fpb);
+    blk[2] = load_resblk(ck, p + ".2", 256, 256, false, fpw, fpb);
+  }
+  m.f0_proj = load_conv(ck, "predictor.F0_proj", 256, 1, 1, 1, 0, 1, true);
+  m.n_proj = load_conv(ck, "predictor.N_proj", 256, 1, 1, 1, 0, 1, true);
+  // ---- text encoder (src/model.rs:29-44)
+  m.te_emb = up(ck.get("text_encoder.embedding.weight", {178, 512}));
+  for (int i = 0; i < 3; i++) {
+    std::string p = "text_encoder.cnn." + std::to_string(i);
+    m.te_cnn[i] = load_conv(ck, p + ".0", 512, 512, 5, 1, 2, 1, true);
+    m.te_g[i] = up(ck.get(p + ".1.gamma", {512}));
+    m.te_b[i] = up(ck.get(p + ".1.beta", {512}));
+  }
+  m.te_lstm = load_lstm(ck, "text_encoder.lstm", 512);
+  // ---- decoder (src/vocoder.rs:98-111)
+  m.enc = load_resblk(ck, "decoder.encode", 514, 1024, false, fdw, fdb);
+  for (int i = 0; i < 4; i++)
+    m.dec[i] = load_resblk(ck, "decoder.decode." + std::to_string(i), 1090, i < 3 ? 1024 : 512, i == 3, fdw, fdb);
+  {
+    auto w = ck.conv_weight("decoder.F0_conv", {1, 1, 3});
+    m.f0conv_w = up(w);
+    m.f0conv_b = ck.get("decoder.F0_conv.bias", {1})[0];
+    auto w2 = ck.conv_weight("decoder.N_conv", {1, 1, 3});
+    m.nconv_w = up(w2);
+    m.nconv_b = ck.get("decoder.N_conv.bias", {1})[0];
+  }
+  m.asr_res = load_conv(ck, "decoder.asr_res.0", 512, 64, 1, 1, 0, 1, true);
+  // ---- generator (src/vocoder.rs:54-80)
+  const std::string g = "decoder.generator";
+  m.lw = up(ck.get(g + ".m_source.l_linear.weight", {1, 9}));
+  m.lb = ck.get(g + ".m_source.l_linear.bias", {1})[0];
+  m.noise0 = load_conv(ck, g + ".noise_convs.0", 22, 256, 12, 1, 3, 6, true);
+  m.noise1 = load_conv(ck, g + ".noise_convs.1", 22, 128, 1, 1, 0, 1, true);
+  m.noise_res[0] = load_snake(ck, g + ".noise_res.0", 256, 7, fdw, fdb);
+  m.noise_res[1] = load_snake(ck, g + ".noise_res.1", 128, 11, fdw, fdb);
+  const int ups_cfg[2][5] = {{512, 256, 20, 10, 5}, {256, 128, 12, 6, 3}};
+  for (int i = 0; i < 2; i++) {
+    const int ci = ups_cfg[i][0], co = ups_cfg[i][1], K = ups_cfg[i][2], s = ups_cfg[i][3], p = ups_cfg[i][4];
+    std::string pre = g + ".ups." + std::to_string(i);
+    auto wT = ck.conv_weight(pre, {ci, co, K});
+    auto b = ck.get(pre + ".bias", {co});
+    std::vector<float> wp, bp;
+    convT_polyphase(wT, b, ci, co, K, s, p, wp, bp);
+    m.ups[i] = conv_from(wp, bp.data(), ci, s * co, 3, 1, 1, 1);
+  }
+  const int ks[3] = {3, 7, 11};
+  for (int i = 0; i < 2; i++)
+    for (int j = 0; j < 3; j++)
+      m.rb[i * 3 + j] = load_snake(ck, g + ".resblocks." + std::to_string(i * 3 + j), 512 >> (i + 1), ks[j], fdw, fdb);
+  m.post = load_conv(ck, g + ".conv_post", 128, 22, 7, 1, 3, 1, true);
+  // fused style projections
+  m.fc_dec = conv_from(fdw, fdb.data(), 128, (int)fdb.size(), 1, 1, 0, 1);
+  m.fc_pro = conv_from(fpw, fpb.data(), 128, (int)fpb.size(), 1, 1, 0, 1);
+  KK_CUDA(upload_stft_constants(st));
+  KK_CUDA(cudaStreamSynchronize(st));
+}
+
+// ------------------------------------------------------------------------------ forward helpers
+
+template <class T>
+T* Engine::upload(const T* h, size_t n) {
+  T* d = ar.get<T>(std::max<size_t>(n, 1));
+  if (n == 0) return d;
+  void* s = pin.alloc(n * sizeof(T));
+  memcpy(s, h, n * sizeof(T));
+  KK_CUDA(cudaMemcpyAsync(d, s, n * sizeof(T), cudaMemcpyHostToDevice, st));
+  return d;
+}
+
+void Engine::check(cudaError_t e, const char* what) {
+  launches++;
+  if (e != cudaSuccess) throw KKError(e == cudaErrorMemoryAllocation ? KK_ERR_OOM : KK_ERR_CUDA,
+                                      std::string(what) + ": " + cudaGetErrorString(e));
+  if (sync_each) {
+    cudaError_t s = cudaStreamSynchronize(st);
+    if (s != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string(what) + " (sync): " + cudaGetErrorString(s));
+  }
+}
+
+// Diagnostic stage dump: with KK_DEBUG_DUMP_DIR set, copy a [rows][ld] f32 buffer to the host
+// and write <dir>/<name>.f32 plus <name>.shape ("rows cols ld").
+void Engine::dump(const char* name, const void* p, long long rows, int cols, int ld) {
+  const char* dir = getenv("KK_DEBUG_DUMP_DIR");
+  if (!dir || !*dir) return;
+  KK_CUDA(cudaStreamSynchronize(st));
+  std::vector<float> h((size_t)rows * ld);
+  KK_CUDA(cudaMemcpy(h.data(), p, h.size() * sizeof(float), cudaMemcpyDeviceToHost));
+  std::string base = std::string(dir) + "/" + name;
+  FILE* f = fopen((base + ".f32").c_str(), "wb");
+  if (f) {
+    fwrite(h.data(), sizeof(float), h.size(), f);
+    fclose(f);
+  }
+  f = fopen((base + ".shape").c_str(), "w");
+  if (f) {
+    fprintf(f, "%lld %d %d\n", rows, cols, ld);
+    fclose(f);
+  }
+}
+
+void Engine::stage_sync(const char* what) {
+  if (!sync_each) return;
+  cudaError_t s = cudaStreamSynchronize(st);
+  if (s != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(s));
+}
+
+ConvArgs Engine::ca(const Conv& c) {
+  ConvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.w = c.w, a.bias = c.b, a.cin = c.cin, a.cout = c.cout, a.K = c.K, a.dil = c.dil, a.pad = c.pad,
+  a.stride = c.stride;
+  a.in_mode = IN_NOMASK;
+  a.out_mode = OUT_STORE;
+  a.oscale = 1.0f;
+  return a;
+}
+
+void Engine::run_conv(const Conv& c, ConvArgs& a) {
+  if (precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc)) {
+    check(tc_conv(a, c.tc, st), "conv(tcgen05)");
+  } else {
+    check(launch_conv_simt(a, st), "conv(simt)");
+  }
+}
+
+void Engine::linear(const Conv& c, const float* x, int ldx, int rows, float* y, int ldy, int out_mode, const float* sc,
+                    int ldsc) {
+  ConvArgs a = ca(c);
+  a.x = x, a.ldx = ldx, a.L_in = rows, a.y = y, a.ldy = ldy, a.L_out = rows, a.out_mode = out_mode, a.sc = sc,
+  a.ldsc = ldsc;
+  run_conv(c, a);
+}
+
+void Engine::stats(const float* x, int ldx, int C, const Dom& d, const ItemTab* items, int B, int max_len, float** mean,
+                   float** rstd) {
+  *mean = ar.get<float>((size_t)B * C);
+  *rstd = ar.get<float>((size_t)B * C);
+  double* part = ar.get<double>((size_t)2 * B * C);
+  check(launch_stats(x, ldx, C, items, B, d.scale == 0 ? 1 : d.scale, d.plus1, max_len, part, *mean, *rstd, st),
+        "stats");
+}
+
+void Engine::adain_args(ConvArgs& a, const AdaIN& n, const float* mean, const float* rstd, const float* gb, int ldgb,
+                        int mode, float slope, const float* alpha) {
+  a.in_mode = mode;
+  a.mean = mean, a.rstd = rstd, a.nw = n.nw, a.nb = n.nb, a.gb = gb + n.off, a.ldgb = ldgb, a.slope = slope,
+  a.alpha = alpha;
+}
+
+// AdainResBlk1d (src/gpu_batch.rs:103-135): y = (conv2(act(AdaIN2(conv1(pool?(act(AdaIN1(x))))))) + sc) / sqrt(2)
+void Engine::resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, const Dom& dout, float* y, int ldy,
+                    const float* gb, int ldgb, const ItemTab* items, int B, int max_n) {
+  auto mk = ar.mark();
+  const int scale_in = din.scale, scale_out = dout.scale;
+  float *m1, *r1, *m2, *r2;
+  stats(x, ldx, R.din, din, items, B, max_n * scale_in, &m1, &r1);
+  float* h = ar.get<float>((size_t)dout.L * R.dout);
+  ConvArgs a = ca(R.c1);
+  if (R.up) {
+    float* p = ar.get<float>((size_t)dout.L * R.din);
+    ConvArgs pro = ca(R.c1);
+    pro.x = x, pro.ldx = ldx, pro.cin = R.din, pro.din = din;
+    adain_args(pro, R.n1, m1, r1, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
+    check(launch_adain_pool(x, R.din, din.L, pro, R.pool_w, R.pool_b, p, st), "adain_pool");
+    a.x = p, a.ldx = R.din, a.in_mode = IN_MASK, a.din = dout, a.L_in = dout.L;
+  } else {
+    a.x = x, a.ldx = ldx, a.din = din, a.L_in = din.L;
+    adain_args(a, R.n1, m1, r1, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
+  }
+  a.y = h, a.ldy = R.dout, a.L_out = dout.L;
+  run_conv(R.c1, a);
+  stats(h, R.dout, R.dout, dout, items, B, max_n * scale_out, &m2, &r2);
+  const float* sc = x;
+  int ldsc = ldx;
+  if (R.has_sc) {
+    float* s = ar.get<float>((size_t)dout.L * R.dout);
+    ConvArgs c = ca(R.sc);
+    c.x = x, c.ldx = ldx, c.in_mode = IN_MASK, c.in_up2 = R.up ? 1 : 0, c.din = dout, c.L_in = dout.L;
+    c.y = s, c.ldy = R.dout, c.L_out = dout.L;
+    run_conv(R.sc, c);
+    sc = s, ldsc = R.dout;
+  }
+  ConvArgs b2 = ca(R.c2);
+  b2.x = h, b2.ldx = R.dout, b2.din = dout, b2.L_in = dout.L;
+  adain_args(b2, R.n2, m2, r2, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
+  b2.y = y, b2.ldy = ldy, b2.L_out = dout.L, b2.out_mode = OUT_PLUS, b2.sc = sc, b2.ldsc = ldsc;
+  b2.oscale = 1.0f / sqrtf(2.0f);
+  run_conv(R.c2, b2);
+  ar.rewind(mk);
+}
+
+// AdaINResBlock1 with Snake (src/gpu_batch.rs:137-154): out = x_in + sum_i conv2_i(snake(AdaIN(conv1_i(snake(AdaIN(.))))))
+void Engine::snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d, const float* gb, int ldgb,
+                   const ItemTab* items, int B, int max_n) {
+  auto mk = ar.mark();
+  const int C = S.c;
+  float* h = ar.get<float>((size_t)d.L * C);
+  const float* cur = xin;
+  const int max_len = max_n * d.scale + d.plus1;
+  for (int i = 0; i < 3; i++) {
+    float *m1, *r1, *m2, *r2;
+    stats(cur, C, C, d, items, B, max_len, &m1, &r1);
+    ConvArgs a = ca(S.c1[i]);
+    a.x = cur, a.ldx = C, a.din = d, a.L_in = d.L, a.y = h, a.ldy = C, a.L_out = d.L;
+    adain_args(a, S.a1[i], m1, r1, gb, ldgb, IN_ADAIN_SNAKE, 0.0f, S.al1[i]);
+    run_conv(S.c1[i], a);
+    stats(h, C, C, d, items, B, max_len, &m2, &r2);
+    ConvArgs b = ca(S.c2[i]);
+    b.x = h, b.ldx = C, b.din = d, b.L_in = d.L, b.y = out, b.ldy = C, b.L_out = d.L;
+    adain_args(b, S.a2[i], m2, r2, gb, ldgb, IN_ADAIN_SNAKE, 0.0f, S.al2[i]);
+    if (i == 0) {
+      b.out_mode = OUT_PLUS, b.sc = xin, b.ldsc = C;
+    } else {
+      b.out_mode = OUT_ADD;
+    }
+    run_conv(S.c2[i], b);
+    cur = out;
+  }
+  ar.rewind(mk);
+}
+
+// One BiLSTM over row spans (src/gpu_batch.rs:157-175): gx = W_ih x + b_ih for both directions in
+// one 1-tap conv, then the persistent recurrence.
+void Engine::lstm(const Lstm& L, const float* x, int ldx, int rows, const std::vector<int>& start,
+                  const std::vector<int>& len, float* out, int ldo) {
+  auto mk = ar.mark();
+  const int B = (int)start.size();
+  float* gx = ar.get<float>((size_t)rows * 2048);
+  linear(L.ih, x, ldx, rows, gx, 2048);
+  std::vector<int> order(B);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len[a] > len[b]; });
+  const int Tmax = B ? len[order[0]] : 0;
+  std::vector<int> act(std::max(Tmax, 1), 0);
+  for (int s = 0, k = B; s < Tmax; s++) {
+    while (k > 0 && len[order[k - 1]] <= s) k--;
+    act[s] = k;
+  }
+  LstmArgs a;
+  a.gx = gx, a.ldgx = 2048, a.whh = L.whh, a.bhh = L.bhh, a.out = out, a.ldo = ldo;
+  a.start = upload(start.data(), B);
+  a.len = upload(len.data(), B);
+  a.order = upload(order.data(), B);
+  a.act = upload(act.data(), act.size());
+  a.B = B, a.Tmax = Tmax;
+  a.hbuf = ar.get<float>((size_t)4 * B * 256);
+  a.cst = ar.get<float>((size_t)2 * B * 256);
+  a.bar = ar.get<unsigned>(2);
+  a.err = err_flag;
+  check(launch_lstm(a, st), "lstm");
+  ar.rewind(mk);
+}
+
+// Decoder + generator on the frame layout (src/gpu_batch.rs:299-420). xcat0 [LN][514] holds asr
+// in columns 0..511; f0 / nc are the 2N curves. Returns the audio buffer [600 LN].
+float* Engine::decode_core(int B, const std::vector<ItemTab>& items_h, const ItemTab* items, const int* col_item_n,
+                           int LN, float* xcat0, float* f0, float* nc, const float* gb_dec, int ldgb,
+                           const uint64_t* seeds_d, const float* noise_d, const long long* noise_off_d) {
+  int max_n = 0;
+  for (auto& it : items_h) max_n = std::max(max_n, it.n);
+  const Dom dN{col_item_n, LN, 1, 0, LN};
+  const Dom d2{col_item_n, LN, 2, 0, 2 * LN};
+  const Dom d20{col_item_n, LN, 20, 0, 20 * LN};
+  const Dom d120{col_item_n, LN, 120, 1, 120 * LN + 1};
+  const int L2 = 2 * LN, L20 = 20 * LN, L120 = 120 * LN + 1;
+  // ---- decoder (pre-generator)
+  float* catA = ar.get<float>((size_t)LN * 1090);
+  float* catB = ar.get<float>((size_t)LN * 1090);
+  CurveConv wf{m.f0conv_w, m.f0conv_b}, wn{m.nconv_w, m.nconv_b};
+  check(launch_curve_conv(f0, nc, d2, LN, wf, wn, xcat0, 514, 512, catA, 1090, 1088, catB, 1090, 1088, st),
+        "curve_conv");
+  {
+    ConvArgs a = ca(m.asr_res);
+    a.x = xcat0, a.ldx = 514, a.in_mode = IN_MASK, a.din = dN, a.L_in = LN;
+    a.y = catA + 1024, a.ldy = 1090, a.L_out = LN;
+    run_conv(m.asr_res, a);
+    check(launch_copy_cols(catA, 1090, 1024, catB, 1090, 1024, LN, 64, st), "copy_cols");
+  }
+  dump("xcat0", xcat0, LN, 514, 514);
+  resblk(m.enc, xcat0, 514, dN, dN, catA, 1090, gb_dec, ldgb, items, B, max_n);
+  dump("enc", catA, LN, 1090, 1090);
+  resblk(m.dec[0], catA, 1090, dN, dN, catB, 1090, gb_dec, ldgb, items, B, max_n);
+  resblk(m.dec[1], catB, 1090, dN, dN, catA, 1090, gb_dec, ldgb, items, B, max_n);
+  resblk(m.dec[2], catA, 1090, dN, dN, catB, 1090, gb_dec, ldgb, items, B, max_n);
+  float* xd = ar.get<float>((size_t)L2 * 512);
+  resblk(m.dec[3], catB, 1090, dN, d2, xd, 512, gb_dec, ldgb, items, B, max_n);
+  dump("xd", xd, L2, 512, 512);
+  stage_sync("decoder");
+  // ---- harmonic source + STFT (one launch each for the whole batch)
+  float* pp = ar.get<float>((size_t)9 * L2);
+  check(launch_sine_phase(f0, L2, items, B, pp, st), "sine_phase");
+  float* har = ar.get<float>((size_t)600 * LN);
+  check(launch_har_source(f0, pp, L2, items, col_item_n, LN, seeds_d, noise_d, noise_off_d, m.lw, m.lb, har, st),
+        "har_source");
+  float* spec = ar.get<float>((size_t)L120 * 22);
+  check(launch_stft(har, items, d120, spec, 22, st), "stft");
+  dump("har", har, 600LL * LN, 1, 1);
+  dump("spec", spec, L120, 22, 22);
+  stage_sync("source");
+  // ---- generator stage 0 (2N -> 20N, C 256)
+  float* y0 = ar.get<float>((size_t)L20 * 256);
+  float* x1 = ar.get<float>((size_t)L20 * 256);
+  {
+    auto mk = ar.mark();
+    float* xs = ar.get<float>((size_t)L20 * 256);
+    float* xsr = ar.get<float>((size_t)L20 * 256);
+    ConvArgs a = ca(m.noise0);
+    a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256, a.L_out = L20;
+    run_conv(m.noise0, a);
+    snake(m.noise_res[0], xs, xsr, d20, gb_dec, ldgb, items, B, max_n);
+    ConvArgs u = ca(m.ups[0]);
+    u.x = xd, u.ldx = 512, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d2, u.L_in = L2;
+    u.y = y0, u.ldy = 2560, u.L_out = L2, u.out_mode = OUT_PLUS, u.sc = xsr, u.ldsc = 2560;
+    run_conv(m.ups[0], u);
+    dump("xs0", xs, L20, 256, 256);
+    dump("xsr0", xsr, L20, 256, 256);
+    dump("y0", y0, L20, 256, 256);
+    ar.rewind(mk);
+    float* r[3];
+    for (int j = 0; j < 3; j++) {
+      r[j] = ar.get<float>((size_t)L20 * 256);
+      snake(m.rb[j], y0, r[j], d20, gb_dec, ldgb, items, B, max_n);
+    }
+    check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
+    dump("r0_0", r[0], L20, 256, 256);
+    dump("x1", x1, L20, 256, 256);
+    ar.rewind(mk);
+  }
+  stage_sync("generator stage 0");
+  // ---- generator stage 1 (20N -> 120N + 1, C 128)
+  float* y1 = ar.get<float>((size_t)L120 * 128);
+  float* x2 = ar.get<float>((size_t)L120 * 128);
+  {
+    auto mk = ar.mark();
+    float* xs = ar.get<float>((size_t)L120 * 128);
+    float* xsr = ar.get<float>((size_t)L120 * 128);
+    ConvArgs a = ca(m.noise1);
+    a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 128, a.L_out = L120;
+    run_conv(m.noise1, a);
+    snake(m.noise_res[1], xs, xsr, d120, gb_dec, ldgb, items, B, max_n);
+    float* u1 = xs;  // noise-conv output no longer needed
+    ConvArgs u = ca(m.ups[1]);
+    u.x = x1, u.ldx = 256, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d20, u.L_in = L20;
+    u.y = u1, u.ldy = 768, u.L_out = L20;
+    run_conv(m.ups[1], u);
+    check(launch_reflect_add(u1, xsr, 128, items, d120, y1, st), "reflect_add");
+    dump("xsr1", xsr, L120, 128, 128);
+    dump("y1", y1, L120, 128, 128);
+    ar.rewind(mk);
+    float* r[3];
+    for (int j = 0; j < 3; j++) {
+      r[j] = ar.get<float>((size_t)L120 * 128);
+      snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n);
+    }
+    check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
+    dump("x2", x2, L120, 128, 128);
+    ar.rewind(mk);
+  }
+  stage_sync("generator stage 1");
+  // ---- conv_post + iSTFT
+  float* post = ar.get<float>((size_t)L120 * 22);
+  {
+    ConvArgs a = ca(m.post);
+    a.x = x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
+    a.y = post, a.ldy = 22, a.L_out = L120;
+    run_conv(m.post, a);
+  }
+  float* audio = ar.get<float>((size_t)600 * LN);
+  check(launch_istft(post, 22, items, d120, col_item_n, LN, audio, st), "istft");
+  dump("post", post, L120, 22, 22);
+  dump("audio", audio, 600LL * LN, 1, 1);
+  stage_sync("istft");
+  return audio;
+}
+
+void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h) {
+  const size_t n = (size_t)600 * LN;
+  out_off.clear();
+  out_len.clear();
+  for (auto& it : items_h) {
+    out_off.push_back(600LL * it.a);
+    out_len.push_back(600LL * it.n);
+  }
+  int errh = 0;
+  if (!keep_audio_dev) {
+    if (audio_host_cap < n) {
+      if (audio_host) cudaFreeHost(audio_host);
+      audio_host = nullptr;
+      audio_host_cap = 0;
+      if (cudaHostAlloc(&audio_host, n * sizeof(float), cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        audio_host = nullptr;
+        throw KKError(KK_ERR_OOM, "pinned audio buffer");
+      }
+      audio_host_cap = n;
+    }
+    KK_CUDA(cudaMemcpyAsync(audio_host, audio_d, n * sizeof(float), cudaMemcpyDeviceToHost, st));
+  }
+  int* eh = (int*)pin.alloc(sizeof(int));
+  KK_CUDA(cudaMemcpyAsync(eh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+  KK_CUDA(cudaStreamSynchronize(st));
+  errh = *eh;
+  if (errh) throw KKError(KK_ERR_TIMEOUT, "an LSTM step barrier timed out");
+}
+
+void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
+                     const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
+                     int64_t* nsamp_out) {
+  KK_REQUIRE(B > 0, "empty batch");
+  KK_REQUIRE(ids && ids_len && ref_s && speed, "null input pointer");
+  KK_REQUIRE(!(noise && !forced), "replayed noise requires forced durations");
+  long long total_ids = 0;
+  for (int b = 0; b < B; b++) {
+    KK_REQUIRE(ids_len[b] >= 2 && ids_len[b] <= 512, "input_ids length outside [2, 512]");
+    KK_REQUIRE(std::isfinite(speed[b]) && speed[b] > 0.0f, "speed must be positive and finite");
+    total_ids += ids_len[b];
+  }
+  for (long long i = 0; i < total_ids; i++) KK_REQUIRE(ids[i] >= 0 && ids[i] < 178, "token id out of range");
+  if (forced) {
+    long long o = 0;
+    for (int b = 0; b < B; b++) {
+      long long s = 0;
+      for (int i = 0; i < ids_len[b]; i++) {
+        KK_REQUIRE(forced[o + i] >= 0 && forced[o + i] <= (1 << 20), "forced duration out of range");
+        s += forced[o + i];
+      }
+      KK_REQUIRE(s >= 1, "forced durations of an item sum to zero");
+      o += ids_len[b];
+    }
+  }
+  KK_CUDA(cudaSetDevice(dev));
+  ar.reset();
+  pin.reset();
+  KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
+  // ---- token layout (src/gpu_batch.rs:189-213)
+  std::vector<ItemTab> items_h(B);
+  int LT = 0;
+  for (int b = 0; b < B; b++) {
+    items_h[b] = {LT, ids_len[b], 0, 0};
+    LT += ids_len[b] + GAP_T;
+  }
+  std::vector<int> row_item_h(LT, -1), ids_h(LT, 0);
+  {
+    long long o = 0;
+    for (int b = 0; b < B; b++) {
+      for (int i = 0; i < ids_len[b]; i++) {
+        row_item_h[items_h[b].tok_start + i] = b;
+        ids_h[items_h[b].tok_start + i] = (int)ids[o + i];
+      }
+      o += ids_len[b];
+    }
+  }
+  std::vector<float> sdec_h((size_t)B * 128), spro_h((size_t)B * 128);
+  for (int b = 0; b < B; b++) {
+    memcpy(&sdec_h[(size_t)b * 128], ref_s + (size_t)b * 256, 128 * sizeof(float));
+    memcpy(&spro_h[(size_t)b * 128], ref_s + (size_t)b * 256 + 128, 128 * sizeof(float));
+  }
+  int* ids_d = upload(ids_h.data(), LT);
+  int* row_item_d = upload(row_item_h.data(), LT);
+  ItemTab* items_d = upload(items_h.data(), B);
+  float* sdec_d = upload(sdec_h.data(), sdec_h.size());
+  float* spro_d = upload(spro_h.data(), spro_h.size());
+  float* speed_d = upload(speed, B);
+  const Dom dT{row_item_d, 0, 0, 0, LT};
+  std::vector<int> tstart(B), tlen(B);
+  for (int b = 0; b < B; b++) tstart[b] = items_h[b].tok_start, tlen[b] = items_h[b].tok_len;
+  // ---- fused style projections (every AdaIN / AdaLN gamma|beta of the batch)
+  const int wdec = m.fc_dec.cout, wpro = m.fc_pro.cout;
+  float* gb_dec = ar.get<float>((size_t)B * wdec);
+  float* gb_pro = ar.get<float>((size_t)B * wpro);
+  linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
+  linear(m.fc_pro, spro_d, 128, B, gb_pro, wpro);
+  // ---- ALBERT (src/gpu_batch.rs:423-455)
+  float* x640 = ar.get<float>((size_t)LT * 640);
+  {
+    auto mk = ar.mark();
+    float* emb = ar.get<float>((size_t)LT * 128);
+    check(launch_albert_embed(ids_d, row_item_d, items_d, LT, m.word, m.pos, m.tt0, m.emb_g, m.emb_b, emb, st),
+          "albert_embed");
+    float* h = ar.get<float>((size_t)LT * 768);
+    float* qkv = ar.get<float>((size_t)LT * 2304);
+    float* ctx = ar.get<float>((size_t)LT * 768);
+    float* a = ar.get<float>((size_t)LT * 768);
+    float* f = ar.get<float>((size_t)LT * 2048);
+    linear(m.map_in, emb, 128, LT, h, 768);
+    int max_t = 0;
+    for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
+    for (int layer = 0; layer < 12; layer++) {
+      linear(m.qkv, h, 768, LT, qkv, 2304);
+      check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
+      linear(m.dense, ctx, 768, LT, a, 768, OUT_PLUS, h, 768);
+      check(launch_ln_rows(a, 768, LT, 768, m.attn_g, m.attn_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, a,
+                           768, st),
+            "ln");
+      linear(m.ffn, a, 768, LT, f, 2048, OUT_GELU);
+      linear(m.ffn_out, f, 2048, LT, h, 768, OUT_PLUS, a, 768);
+      check(launch_ln_rows(h, 768, LT, 768, m.full_g, m.full_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, h,
+                           768, st),
+            "ln");
+    }
+    // bert_encoder -> d_en, then [d_en | s_pro] (src/gpu_batch.rs:223-231)
+    linear(m.bert_enc, h, 768, LT, x640, 640);
+    check(launch_cat_style(row_item_d, LT, 512, spro_d, 128, x640, 640, st), "cat_style");
+    dump("bert", h, LT, 768, 768);
+    dump("d_en", x640, LT, 640, 640);
+    ar.rewind(mk);
+  }
+  stage_sync("albert");
+  // ---- duration encoder + predictor LSTM + duration logits (src/gpu_batch.rs:224-248)
+  int* dur_d = ar.get<int>(LT);
+  float* q_d = ar.get<float>(LT);
+  {
+    auto mk = ar.mark();
+    float* hl = ar.get<float>((size_t)LT * 512);
+    for (int i = 0; i < 3; i++) {
+      lstm(m.dur_lstm[i], x640, 640, LT, tstart, tlen, hl, 512);
+      check(launch_ln_rows(hl, 512, LT, 512, nullptr, nullptr, 1e-5f, 2, 0.0f, row_item_d, gb_pro + m.adaln_off[i],
+                           wpro, spro_d, 128, x640, 640, st),
+            "adaln");
+    }
+    lstm(m.pred_lstm, x640, 640, LT, tstart, tlen, hl, 512);
+    float* logits = ar.get<float>((size_t)LT * 50);
+    linear(m.dur_proj, hl, 512, LT, logits, 50);
+    check(launch_durations(logits, 50, row_item_d, speed_d, LT, dur_d, q_d, st), "durations");
+    dump("x640", x640, LT, 640, 640);
+    dump("logits", logits, LT, 50, 50);
+    ar.rewind(mk);
+  }
+  // ---- durations to the host: the one mid-forward synchronisation (src/gpu_batch.rs:243-248)
+  std::vector<int> dur_h(LT, 0);
+  if (forced) {
+    long long o = 0;
+    for (int b = 0; b < B; b++) {
+      for (int i = 0; i < ids_len[b]; i++) dur_h[items_h[b].tok_start + i] = (int)forced[o + i];
+      o += ids_len[b];
+    }
+  } else {
+    int* dh = (int*)pin.alloc(sizeof(int) * LT);
+    int* eh = (int*)pin.alloc(sizeof(int));
+    KK_CUDA(cudaMemcpyAsync(dh, dur_d, sizeof(int) * LT, cudaMemcpyDeviceToHost, st));
+    KK_CUDA(cudaMemcpyAsync(eh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+    KK_CUDA(cudaStreamSynchronize(st));
+    if (*eh) throw KKError(KK_ERR_TIMEOUT, "an LSTM step barrier timed out");
+    memcpy(dur_h.data(), dh, sizeof(int) * LT);
+  }
+  if (dur_out) {
+    long long o = 0;
+    for (int b = 0; b < B; b++) {
+      for (int i = 0; i < ids_len[b]; i++) dur_out[o + i] = dur_h[items_h[b].tok_start + i];
+      o += ids_len[b];
+    }
+  }
+  // ---- frame layout (src/gpu_batch.rs:250-279)
+  int LN = 0;
+  for (int b = 0; b < B; b++) {
+    long long n = 0;
+    for (int i = 0; i < ids_len[b]; i++) n += dur_h[items_h[b].tok_start + i];
+    KK_REQUIRE(n >= 1 && n < (1 << 22), "item frame count out of range");
+    items_h[b].a = LN;
+    items_h[b].n = (int)n;
+    LN += (int)n + GAP_N;
+  }
+  if (nsamp_out)
+    for (int b = 0; b < B; b++) nsamp_out[b] = 600LL * items_h[b].n;
+  std::vector<int> col_item_h(LN, -1), src_row_h(LN, -1);
+  for (int b = 0; b < B; b++) {
+    int f = items_h[b].a;
+    for (int i = 0; i < ids_len[b]; i++)
+      for (int k = 0; k < dur_h[items_h[b].tok_start + i]; k++) {
+        col_item_h[f] = b;
+        src_row_h[f] = items_h[b].tok_start + i;
+        f++;
+      }
+  }
+  items_d = upload(items_h.data(), B);
+  int* col_item_d = upload(col_item_h.data(), LN);
+  int* src_row_d = upload(src_row_h.data(), LN);
+  const Dom dN{col_item_d, LN, 1, 0, LN};
+  const Dom d2{col_item_d, LN, 2, 0, 2 * LN};
+  std::vector<int> fstart(B), flen(B);
+  int max_n = 0;
+  for (int b = 0; b < B; b++) fstart[b] = items_h[b].a, flen[b] = items_h[b].n, max_n = std::max(max_n, flen[b]);
+  // ---- F0 / N predictor (src/gpu_batch.rs:281-292)
+  float* f0 = ar.get<float>((size_t)2 * LN);
+  float* nc = ar.get<float>((size_t)2 * LN);
+  {
+    auto mk = ar.mark();
+    float* en = ar.get<float>((size_t)LN * 640);
+    check(launch_gather_rows(x640, 640, src_row_d, LN, 640, en, 640, st), "gather_rows");
+    float* sh = ar.get<float>((size_t)LN * 512);
+    lstm(m.shared, en, 640, LN, fstart, flen, sh, 512);
+    dump("sh", sh, LN, 512, 512);
+    float* h1 = ar.get<float>((size_t)LN * 512);
+    float* h2 = ar.get<float>((size_t)2 * LN * 256);
+    float* h3 = ar.get<float>((size_t)2 * LN * 256);
+    for (int s = 0; s < 2; s++) {
+      const ResBlk* blk = s == 0 ? m.f0 : m.nn;
+      resblk(blk[0], sh, 512, dN, dN, h1, 512, gb_pro, wpro, items_d, B, max_n);
+      resblk(blk[1], h1, 512, dN, d2, h2, 256, gb_pro, wpro, items_d, B, max_n);
+      resblk(blk[2], h2, 256, d2, d2, h3, 256, gb_pro, wpro, items_d, B, max_n);
+      const Conv& proj = s == 0 ? m.f0_proj : m.n_proj;
+      ConvArgs a = ca(proj);
+      a.x = h3, a.ldx = 256, a.in_mode = IN_MASK, a.din = d2, a.L_in = 2 * LN;
+      a.y = s == 0 ? f0 : nc, a.ldy = 1, a.L_out = 2 * LN;
+      run_conv(proj, a);
+    }
+    ar.rewind(mk);
+  }
+  dump("f0", f0, 2LL * LN, 1, 1);
+  dump("nc", nc, 2LL * LN, 1, 1);
+  stage_sync("f0n");
+  // ---- text encoder (src/gpu_batch.rs:457-481) and alignment of its output (asr)
+  float* xcat0 = ar.get<float>((size_t)LN * 514);
+  {
+    auto mk = ar.mark();
+    float* e = ar.get<float>((size_t)LT * 512);
+    float* y = ar.get<float>((size_t)LT * 512);
+    check(launch_embed_rows(ids_d, row_item_d, LT, m.te_emb, 512, e, st), "embed");
+    float* cur = e;
+    float* nxt = y;
+    for (int i = 0; i < 3; i++) {
+      ConvArgs a = ca(m.te_cnn[i]);
+      a.x = cur, a.ldx = 512, a.in_mode = IN_MASK, a.din = dT, a.L_in = LT, a.y = nxt, a.ldy = 512, a.L_out = LT;
+      run_conv(m.te_cnn[i], a);
+      check(launch_ln_rows(nxt, 512, LT, 512, m.te_g[i], m.te_b[i], 1e-5f, 1, 0.2f, nullptr, nullptr, 0, nullptr, 0,
+                           nxt, 512, st),
+            "ln");
+      std::swap(cur, nxt);
+    }
+    float* t_en = nxt;
+    lstm(m.te_lstm, cur, 512, LT, tstart, tlen, t_en, 512);
+    check(launch_gather_rows(t_en, 512, src_row_d, LN, 512, xcat0, 514, st), "gather_rows");
+    ar.rewind(mk);
+  }
+  stage_sync("text encoder");
+  // ---- noise inputs
+  uint64_t* seeds_d = nullptr;
+  if (seeds) seeds_d = upload(seeds, B);
+  float* noise_d = nullptr;
+  long long* noise_off_d = nullptr;
+  if (noise) {
+    std::vector<long long> off(B);
+    long long tot = 0;
+    for (int b = 0; b < B; b++) off[b] = tot, tot += 600LL * 9 * items_h[b].n;
+    noise_d = upload(noise, (size_t)tot);
+    noise_off_d = upload(off.data(), B);
+  }
+  float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
+                             noise_off_d);
+  finish_audio(audio, LN, items_h);
+}
+
+void Engine::decode(int B, const int32_t* n_frames, const float* asr, const float* f0_in, const float* n_in,
+                    const float* s_dec, const uint64_t* seeds, const float* noise, float* audio_out) {
+  KK_REQUIRE(B > 0, "empty batch");
+  KK_REQUIRE(n_frames && asr && f0_in && n_in && s_dec, "null input pointer");
+  std::vector<ItemTab> items_h(B);
+  int LN = 0;
+  long long tot = 0;
+  for (int b = 0; b < B; b++) {
+    KK_REQUIRE(n_frames[b] >= 1 && n_frames[b] < (1 << 22), "frame count out of range");
+    items_h[b] = {0, 0, LN, n_frames[b]};
+    LN += n_frames[b] + GAP_N;
+    tot += n_frames[b];
+  }
+  KK_CUDA(cudaSetDevice(dev));
+  ar.reset();
+  pin.reset();
+  KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
+  std::vector<int> col_item_h(LN, -1), tab1(LN, -1), tab2(2 * LN, -1);
+  long long r = 0;
+  for (int b = 0; b < B; b++) {
+    for (int i = 0; i < items_h[b].n; i++) {
+      col_item_h[items_h[b].a + i] = b;
+      tab1[items_h[b].a + i] = (int)(r + i);
+    }
+    for (int i = 0; i < 2 * items_h[b].n; i++) tab2[2 * items_h[b].a + i] = (int)(2 * r + i);
+    r += items_h[b].n;
+  }
+  ItemTab* items_d = upload(items_h.data(), B);
+  int* col_item_d = upload(col_item_h.data(), LN);
+  int* tab1_d = upload(tab1.data(), LN);
+  int* tab2_d = upload(tab2.data(), 2 * LN);
+  float* asr_d = upload(asr, (size_t)tot * 512);
+  float* f0c_d = upload(f0_in, (size_t)2 * tot);
+  float* nc_d = upload(n_in, (size_t)2 * tot);
+  float* sdec_d = upload(s_dec, (size_t)B * 128);
+  float* xcat0 = ar.get<float>((size_t)LN * 514);
+  float* f0 = ar.get<float>((size_t)2 * LN);
+  float* nc = ar.get<float>((size_t)2 * LN);
+  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, 514, st), "gather_rows");
+  check(launch_gather_rows(f0c_d, 1, tab2_d, 2 * LN, 1, f0, 1, st), "gather_rows");
+  check(launch_gather_rows(nc_d, 1, tab2_d, 2 * LN, 1, nc, 1, st), "gather_rows");
+  const int wdec = m.fc_dec.cout;
+  float* gb_dec = ar.get<float>((size_t)B * wdec);
+  linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
+  uint64_t* seeds_d = seeds ? upload(seeds, B) : nullptr;
+  float* noise_d = nullptr;
+  long long* noise_off_d = nullptr;
+  if (noise) {
+    std::vector<long long> off(B);
+    long long t = 0;
+    for (int b = 0; b < B; b++) off[b] = t, t += 600LL * 9 * items_h[b].n;
+    noise_d = upload(noise, (size_t)t);
+    noise_off_d = upload(off.data(), B);
+  }
+  float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
+                             noise_off_d);
+  finish_audio(audio, LN, items_h);
+  if (audio_out && !keep_audio_dev) {
+    long long o = 0;
+    for (int b = 0; b < B; b++) {
+      memcpy(audio_out + o, audio_host + out_off[b], sizeof(float) * out_len[b]);
+      o += out_len[b];
+    }
+  }
+}
+
+}  // namespace kk
+
+// ------------------------------------------------------------------------------ C ABI
+
+struct kk_engine {
+  std::unique_ptr<kk::Engine> e;
+};
+
+static thread_local std::string g_create_error;
+
+template <class F>
+static kk_status guarded(kk_engine* h, F&& f) {
+  try {
+    f();
+    if (h) h->e->err.clear();
+    return KK_OK;
+  } catch (const kk::KKError& x) {
+    if (h) h->e->err = x.what();
+    else g_create_error = x.what();
+    return (kk_status)x.status;
+  } catch (const std::bad_alloc&) {
+    if (h) h->e->err = "host allocation failed";
+    else g_create_error = "host allocation failed";
+    return KK_ERR_OOM;
+  } catch (const std::exception& x) {
+    if (h) h->e->err = x.what();
+    else g_create_error = x.what();
+    return KK_ERR_CUDA;
+  }
+}
+
+extern "C" {
+
+kk_status kk_create(const char* path, int cuda_ordinal, int precision, kk_engine** out) {
+  if (!out || !path) {
+    g_create_error = "null argument";
+    return KK_ERR_INVALID_ARG;
+  }
+  *out = nullptr;
+  if (precision != KK_PRECISION_FP32 && precision != KK_PRECISION_BF16) {
+    g_create_error = "unknown precision";
+    return KK_ERR_INVALID_ARG;
+  }
+  std::unique_ptr<kk_engine> h(new kk_engine{std::unique_ptr<kk::Engine>(new kk::Engine())});
+  kk::Engine& e = *h->e;
+  kk_status s = guarded(nullptr, [&] {
+    int n = 0;
+    KK_CUDA(cudaGetDeviceCount(&n));
+    KK_REQUIRE(cuda_ordinal >= 0 && cuda_ordinal < n, "CUDA device ordinal out of range");
+    cudaDeviceProp prop;
+    KK_CUDA(cudaGetDeviceProperties(&prop, cuda_ordinal));
+    if (prop.major != 10)
+      throw kk::KKError(KK_ERR_CUDA, std::string("device ") + prop.name + " is not compute capability 10.x (sm_100a)");
+    e.dev = cuda_ordinal;
+    e.precision = precision;
+    KK_CUDA(cudaSetDevice(cuda_ordinal));
+    KK_CUDA(cudaStreamCreateWithFlags(&e.st, cudaStreamNonBlocking));
+    KK_CUDA(cudaMalloc(&e.err_flag, sizeof(int)));
+    e.wallocs.push_back(e.err_flag);
+    KK_CUDA(cudaMemset(e.err_flag, 0, sizeof(int)));
+    e.tc_ok = precision == KK_PRECISION_BF16 && kk::tc_available();
+    kk::Checkpoint ck(path);
+    e.load(ck);
+    e.ident = std::string("cuda-b200 ") + (precision == KK_PRECISION_BF16 ? "bf16" : "fp32") +
+              (e.tc_ok ? " tcgen05" : " simt");
+  });
+  if (s != KK_OK) return s;
+  *out = h.release();
+  return KK_OK;
+}
+
+void kk_destroy(kk_engine* h) { delete h; }
+
+const char* kk_last_error(const kk_engine* h) { return h ? h->e->err.c_str() : g_create_error.c_str(); }
+
+const char* kk_identity(const kk_engine* h) { return h ? h->e->ident.c_str() : ""; }
+
+kk_status kk_forward_batch(kk_engine* h, int n_items, const int64_t* ids, const int32_t* ids_len, const float* ref_s,
+                           const float* speed, const uint64_t* seeds, const float* noise, const int64_t* forced_dur,
+                           int64_t* dur_out, int64_t* n_samples_out) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    h->e->out_off.clear();
+    h->e->out_len.clear();
+    h->e->forward(n_items, ids, ids_len, ref_s, speed, seeds, noise, forced_dur, dur_out, n_samples_out);
+  });
+}
+
+kk_status kk_fetch_audio(kk_engine* h, int item, float* dst, int64_t cap) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    kk::Engine& e = *h->e;
+    KK_REQUIRE(item >= 0 && item < (int)e.out_off.size(), "item index out of range (no forward result)");
+    KK_REQUIRE(!e.keep_audio_dev, "audio was kept on the device (KK_OPT_KEEP_AUDIO_ON_DEVICE)");
+    KK_REQUIRE(dst && cap >= e.out_len[item], "destination too small");
+    memcpy(dst, e.audio_host + e.out_off[item], sizeof(float) * e.out_len[item]);
+  });
+}
+
+kk_status kk_decode_batch(kk_engine* h, int n_items, const int32_t* n_frames, const float* asr, const float* f0,
+                          const float* n, const float* s_dec, const uint64_t* seeds, const float* noise,
+                          float* audio_out) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] { h->e->decode(n_items, n_frames, asr, f0, n, s_dec, seeds, noise, audio_out); });
+}
+
+kk_status kk_set_option(kk_engine* h, int option, int64_t value) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    if (option == KK_OPT_KEEP_AUDIO_ON_DEVICE) h->e->keep_audio_dev = value != 0;
+    else if (option == KK_OPT_SYNC_EACH_STAGE) h->e->sync_each = value != 0;
+    else throw kk::KKError(KK_ERR_INVALID_ARG, "unknown option");
+  });
+}
+
+int64_t kk_device_bytes(const kk_engine* h) { return h ? (int64_t)(h->e->wbytes + h->e->ar.bytes()) : 0; }
+
+int64_t kk_launch_count(const kk_engine* h) { return h ? h->e->launches : 0; }
+
+}  // extern "C"

@@ -1,0 +1,847 @@
+// Memory-bound and latency-bound kernels of the kokoro-b200 forward: embeddings, row
+// LayerNorm / AdaLayerNorm, per-item attention (fp32), the persistent BiLSTM recurrence, AdaIN
+// statistics, the AdaIN+pool upsampler, duration rounding, the F0/N curve convolutions, the
+// harmonic source, STFT / iSTFT, and the small glue passes.
+//
+// Arithmetic that decides bit-level agreement with the reference is written out explicitly:
+// the SineGen phase path uses the reference's FMA placement and f64 accumulation
+// (kernels/kokoro.cu:188-254), durations use a sequential f32 sigmoid sum with
+// round-half-to-even (src/model.rs:90-99), STFT / iSTFT run their DFTs in f64 (:470-508).
+#include <math.h>
+#include "kk_common.cuh"
+#include "kk_launch.h"
+
+namespace kk {
+
+__constant__ double c_tw[440];  // [cos 11x20 | sin 11x20] of 2*pi*((k*n) % 20)/20 (src/gpu.rs:93-99)
+__constant__ float c_win[20];   // periodic Hann(20) (src/gpu.rs:101)
+
+static inline unsigned nblk(long n, int t) { return (unsigned)((n + t - 1) / t); }
+
+// Sum of a double over a block of `blockDim.x` (multiple of 32, <= 1024) threads.
+__device__ double block_sum_d(double v, double* sh) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_down_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    double r = l < nw ? sh[l] : 0.0;
+    for (int o = 16; o > 0; o >>= 1) r += __shfl_down_sync(0xffffffffu, r, o);
+    if (l == 0) sh[32] = r;
+  }
+  __syncthreads();
+  return sh[32];
+}
+
+// ------------------------------------------------------------------------------ token side
+
+__global__ void albert_embed_kernel(const int* ids, const int* row_item, const ItemTab* items, const float* word,
+                                    const float* pos, const float* tt0, const float* g, const float* bb,
+                                    float* out) {
+  __shared__ double sh[33];
+  const int r = blockIdx.x, j = threadIdx.x;  // 128 threads = EMB
+  const int b = row_item[r];
+  if (b < 0) {
+    out[(long)r * 128 + j] = 0.0f;
+    return;
+  }
+  const int i = r - items[b].tok_start;
+  const int id = ids[r];
+  const float v = __fadd_rn(__fadd_rn(word[id * 128 + j], tt0[j]), pos[i * 128 + j]);
+  const float mean = (float)(block_sum_d((double)v, sh) / 128.0);
+  const double c = (double)__fsub_rn(v, mean);
+  const float var = (float)(block_sum_d(c * c, sh) / 128.0);
+  const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(var, 1e-12f)));
+  float o = __fmul_rn(__fsub_rn(v, mean), inv);
+  o = __fadd_rn(__fmul_rn(o, g[j]), bb[j]);
+  out[(long)r * 128 + j] = o;
+}
+
+cudaError_t launch_albert_embed(const int* ids, const int* row_item, const ItemTab* items, int rows,
+                                const float* word, const float* pos, const float* tt0, const float* g,
+                                const float* b, float* out, cudaStream_t st) {
+  albert_embed_kernel<<<rows, 128, 0, st>>>(ids, row_item, items, word, pos, tt0, g, b, out);
+  return cudaGetLastError();
+}
+
+__global__ void gather_rows_kernel(const float* src, int lds, const int* tab, int rows, int d, float* out, int ldo) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= (long)rows * d) return;
+  int r = (int)(i / d), j = (int)(i % d);
+  int s = tab[r];
+  out[(long)r * ldo + j] = s < 0 ? 0.0f : src[(long)s * lds + j];
+}
+
+cudaError_t launch_gather_rows(const float* src, int lds, const int* tab, int rows, int d, float* out, int ldo,
+                               cudaStream_t st) {
+  long n = (long)rows * d;
+  if (n == 0) return cudaSuccess;
+  gather_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(src, lds, tab, rows, d, out, ldo);
+  return cudaGetLastError();
+}
+
+__global__ void embed_rows_kernel(const int* ids, const int* row_item, int rows, const float* table, int d, float* out) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= (long)rows * d) return;
+  int r = (int)(i / d), j = (int)(i % d);
+  out[i] = row_item[r] < 0 ? 0.0f : table[(long)ids[r] * d + j];
+}
+
+cudaError_t launch_embed_rows(const int* ids, const int* row_item, int rows, const float* table, int d, float* out,
+                              cudaStream_t st) {
+  long n = (long)rows * d;
+  embed_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(ids, row_item, rows, table, d, out);
+  return cudaGetLastError();
+}
+
+__global__ void ln_rows_kernel(const float* x, int ldx, int d, const float* g, const float* bb, float eps, int mode,
+                               float slope, const int* row_item, const float* gb, int ldgb, const float* style,
+                               int sdim, float* y, int ldy) {
+  __shared__ double sh[33];
+  const int r = blockIdx.x;
+  const float* row = x + (long)r * ldx;
+  float* yr = y + (long)r * ldy;
+  int item = 0;
+  if (mode == 2) {
+    item = row_item[r];
+    if (item < 0) {
+      for (int j = threadIdx.x; j < d + sdim; j += blockDim.x) yr[j] = 0.0f;
+      return;
+    }
+  }
+  double s = 0.0;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) s += (double)row[j];
+  const float mean = (float)(block_sum_d(s, sh) / (double)d);
+  double v = 0.0;
+  for (int j = threadIdx.x; j < d; j += blockDim.x) {
+    double c = (double)(row[j] - mean);
+    v += c * c;
+  }
+  const float inv = 1.0f / sqrtf((float)(block_sum_d(v, sh) / (double)d) + eps);
+  if (mode == 2) {
+    const float* gg = gb + (long)item * ldgb;
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float o = (row[j] - mean) * inv;
+      yr[j] = (1.0f + gg[j]) * o + gg[d + j];
+    }
+    for (int j = threadIdx.x; j < sdim; j += blockDim.x) yr[d + j] = style[(long)item * sdim + j];
+  } else {
+    for (int j = threadIdx.x; j < d; j += blockDim.x) {
+      float o = (row[j] - mean) * inv;
+      if (g) o = o * g[j];
+      if (bb) o = o + bb[j];
+      if (mode == 1) o = leaky(o, slope);
+      yr[j] = o;
+    }
+  }
+}
+
+cudaError_t launch_ln_rows(const float* x, int ldx, int rows, int d, const float* g, const float* b, float eps,
+                           int mode, float slope, const int* row_item, const float* gb, int ldgb,
+                           const float* style, int sdim, float* y, int ldy, cudaStream_t st) {
+  if (rows == 0) return cudaSuccess;
+  ln_rows_kernel<<<rows, 256, 0, st>>>(x, ldx, d, g, b, eps, mode, slope, row_item, gb, ldgb, style, sdim, y, ldy);
+  return cudaGetLastError();
+}
+
+__global__ void cat_style_kernel(const int* row_item, int rows, int d, const float* style, int sdim, float* y, int ldy) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  const int w = d + sdim;
+  if (i >= (long)rows * w) return;
+  int r = (int)(i / w), j = (int)(i % w);
+  int b = row_item[r];
+  if (b < 0) y[(long)r * ldy + j] = 0.0f;
+  else if (j >= d) y[(long)r * ldy + j] = style[(long)b * sdim + (j - d)];
+}
+
+cudaError_t launch_cat_style(const int* row_item, int rows, int d, const float* style, int sdim, float* y, int ldy,
+                             cudaStream_t st) {
+  long n = (long)rows * (d + sdim);
+  cat_style_kernel<<<nblk(n, 256), 256, 0, st>>>(row_item, rows, d, style, sdim, y, ldy);
+  return cudaGetLastError();
+}
+
+// Per-item 12-head attention, one thread per query row, keys/values staged 64 at a time,
+// online softmax over blocks of 16 keys. qkv row: [q(768) | k(768) | v(768)], head h at h*64.
+__global__ void __launch_bounds__(128) attention_f32_kernel(const float* qkv, int ld, const ItemTab* items,
+                                                            float* ctx, int ldc) {
+  __shared__ __align__(16) float Ks[64][64];
+  __shared__ __align__(16) float Vs[64][64];
+  const int b = blockIdx.x >> 2, qb = blockIdx.x & 3, h = blockIdx.y;
+  const ItemTab it = items[b];
+  const int T = it.tok_len;
+  if (qb * 128 >= T) return;
+  const int qi = qb * 128 + threadIdx.x;
+  const bool valid = qi < T;
+  float q[64], acc[64];
+  float m = -INFINITY, l = 0.0f;
+#pragma unroll
+  for (int d = 0; d < 64; d++) {
+    q[d] = valid ? qkv[(long)(it.tok_start + qi) * ld + h * 64 + d] : 0.0f;
+    acc[d] = 0.0f;
+  }
+  for (int kb = 0; kb < T; kb += 64) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < 64 * 64; i += 128) {
+      int j = i >> 6, d = i & 63, row = kb + j;
+      bool in = row < T;
+      long base = (long)(it.tok_start + row) * ld + h * 64 + d;
+      Ks[j][d] = in ? qkv[base + 768] : 0.0f;
+      Vs[j][d] = in ? qkv[base + 1536] : 0.0f;
+    }
+    __syncthreads();
+    if (!valid) continue;
+    const int nk = min(64, T - kb);
+    for (int j0 = 0; j0 < nk; j0 += 16) {
+      float s[16];
+      float mx = m;
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        const int j = j0 + jj;
+        float dot = 0.0f;
+        if (j < nk) {
+#pragma unroll
+          for (int d = 0; d < 64; d += 4) {
+            float4 kv = *reinterpret_cast<const float4*>(&Ks[j][d]);
+            dot = fmaf(q[d], kv.x, dot);
+            dot = fmaf(q[d + 1], kv.y, dot);
+            dot = fmaf(q[d + 2], kv.z, dot);
+            dot = fmaf(q[d + 3], kv.w, dot);
+          }
+          s[jj] = dot * 0.125f;
+        } else {
+          s[jj] = -INFINITY;
+        }
+        mx = fmaxf(mx, s[jj]);
+      }
+      if (mx > m) {
+        const float corr = expf(m - mx);
+        l *= corr;
+#pragma unroll
+        for (int d = 0; d < 64; d++) acc[d] *= corr;
+        m = mx;
+      }
+#pragma unroll
+      for (int jj = 0; jj < 16; jj++) {
+        const float p = expf(s[jj] - m);
+        l += p;
+        if (j0 + jj < nk) {
+#pragma unroll
+          for (int d = 0; d < 64; d += 4) {
+            float4 vv = *reinterpret_cast<const float4*>(&Vs[j0 + jj][d]);
+            acc[d] = fmaf(p, vv.x, acc[d]);
+            acc[d + 1] = fmaf(p, vv.y, acc[d + 1]);
+            acc[d + 2] = fmaf(p, vv.z, acc[d + 2]);
+            acc[d + 3] = fmaf(p, vv.w, acc[d + 3]);
+          }
+        }
+      }
+    }
+  }
+  if (valid) {
+    const float inv = 1.0f / l;
+    float* o = ctx + (long)(it.tok_start + qi) * ldc + h * 64;
+#pragma unroll
+    for (int d = 0; d < 64; d++) o[d] = acc[d] * inv;
+  }
+}
+
+cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* items, int B, int max_len, float* ctx,
+                                 int ldc, cudaStream_t st) {
+  (void)max_len;
+  dim3 grid(B * 4, 12);
+  attention_f32_kernel<<<grid, 128, 0, st>>>(qkv, ldqkv, items, ctx, ldc);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ LSTM
+
+constexpr int LH = 256;            // hidden units per direction
+constexpr int L_UNITS = 4;         // hidden units owned by one CTA (all four gates)
+constexpr int L_CTAS_PER_DIR = LH / L_UNITS;
+constexpr int L_KC = 32;           // k-chunk of the staged hidden state
+constexpr int L_IPC = 64;          // items per chunk (one per thread group of 4 units)
+constexpr unsigned long long L_TIMEOUT_NS = 2000000000ull;
+
+__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+// Bidirectional LSTM recurrence for all items of a batch (kernels/kokoro.cu:400-450 semantics:
+// gates = gx + (W_hh h + b_hh), order i, f, g, o). CTA (dir, unit block) keeps its 16 rows of
+// W_hh in shared memory for the whole sequence; thread (unit, item lane) owns one (item, unit)
+// and computes its four gates, so the cell update needs no exchange. One bounded step barrier
+// per direction: a wait longer than 2 s sets *err and every CTA returns.
+__global__ void __launch_bounds__(256) lstm_kernel(LstmArgs a) {
+  __shared__ float Ws[16][LH + 4];
+  __shared__ float Hs[L_IPC][L_KC + 1];
+  __shared__ int s_abort;
+  const int dir = blockIdx.x / L_CTAS_PER_DIR;
+  const int j0 = (blockIdx.x % L_CTAS_PER_DIR) * L_UNITS;
+  const int tid = threadIdx.x, jl = tid & 3, il = tid >> 2;
+  const int j = j0 + jl;
+  for (int i = tid; i < 16 * LH; i += 256) {
+    int r = i / LH, k = i % LH;
+    int g = r >> 2, u = r & 3;
+    Ws[r][k] = a.whh[((long)dir * 4 * LH + g * LH + j0 + u) * LH + k];
+  }
+  float bh[4];
+#pragma unroll
+  for (int g = 0; g < 4; g++) bh[g] = a.bhh[dir * 4 * LH + g * LH + j];
+  __syncthreads();
+  for (int s = 0; s < a.Tmax; s++) {
+    const int na = a.act[s];
+    const float* hp = a.hbuf + ((long)(s & 1) * 2 + dir) * (long)a.B * LH;
+    float* hn = a.hbuf + ((long)((s + 1) & 1) * 2 + dir) * (long)a.B * LH;
+    for (int ic = 0; ic < na; ic += L_IPC) {
+      const int rank = ic + il;
+      const bool valid = rank < na;
+      const int b = valid ? a.order[rank] : 0;
+      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+      for (int kc = 0; kc < LH; kc += L_KC) {
+        __syncthreads();
+        for (int i = tid; i < L_IPC * L_KC; i += 256) {
+          int ii = i / L_KC, kk = i % L_KC;
+          int rr = ic + ii;
+          Hs[ii][kk] = rr < na ? __ldcg(hp + (long)a.order[rr] * LH + kc + kk) : 0.0f;
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < L_KC; kk++) {
+          const float hv = Hs[il][kk];
+          acc[0] = fmaf(Ws[jl][kc + kk], hv, acc[0]);
+          acc[1] = fmaf(Ws[4 + jl][kc + kk], hv, acc[1]);
+          acc[2] = fmaf(Ws[8 + jl][kc + kk], hv, acc[2]);
+          acc[3] = fmaf(Ws[12 + jl][kc + kk], hv, acc[3]);
+        }
+      }
+      if (valid) {
+        const int T = a.len[b];
+        const int t = dir == 0 ? s : T - 1 - s;
+        const long row = (long)a.start[b] + t;
+        const float* gx = a.gx + row * a.ldgx + dir * 4 * LH;
+        const float gi = gx[j] + (acc[0] + bh[0]);
+        const float gf = gx[LH + j] + (acc[1] + bh[1]);
+        const float gg = gx[2 * LH + j] + (acc[2] + bh[2]);
+        const float go = gx[3 * LH + j] + (acc[3] + bh[3]);
+        const float ig = 1.0f / (1.0f + expf(-gi));
+        const float fg = 1.0f / (1.0f + expf(-gf));
+        const float cg = tanhf(gg);
+        const float og = 1.0f / (1.0f + expf(-go));
+        float* cp = a.cst + ((long)dir * a.B + b) * LH + j;
+        const float c = fg * (*cp) + ig * cg;
+        *cp = c;
+        const float h = og * tanhf(c);
+        hn[(long)b * LH + j] = h;
+        a.out[row * a.ldo + dir * LH + j] = h;
+      }
+    }
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence();
+      atomicAdd(a.bar + dir, 1u);
+      const unsigned target = (unsigned)(s + 1) * L_CTAS_PER_DIR;
+      const unsigned long long t0 = globaltimer_ns();
+      int ab = 0;
+      while (ld_acquire_u32(a.bar + dir) < target) {
+        if (*(volatile int*)a.err) {
+          ab = 1;
+          break;
+        }
+        if (globaltimer_ns() - t0 > L_TIMEOUT_NS) {
+          atomicExch(a.err, 1);
+          ab = 1;
+          break;
+        }
+        __nanosleep(64);
+      }
+      __threadfence();
+      s_abort = ab;
+    }
+    __syncthreads();
+    if (s_abort) return;
+  }
+}
+
+cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st) {
+  cudaError_t e;
+  if ((e = cudaMemsetAsync(a.hbuf, 0, sizeof(float) * 4L * a.B * LH, st)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(a.cst, 0, sizeof(float) * 2L * a.B * LH, st)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned) * 2, st)) != cudaSuccess) return e;
+  if (a.Tmax == 0) return cudaSuccess;
+  LstmArgs args = a;
+  void* params[] = {&args};
+  return cudaLaunchCooperativeKernel((const void*)lstm_kernel, dim3(2 * L_CTAS_PER_DIR), dim3(256), params, 0, st);
+}
+
+// ------------------------------------------------------------------------------ AdaIN statistics
+
+__global__ void stats_partial_kernel(const float* x, int ldx, int C, const ItemTab* items, int scale, int plus1,
+                                     int rs, double* part) {
+  __shared__ double sh[8][32][2];
+  const int b = blockIdx.x, c = blockIdx.y * 32 + (threadIdx.x & 31), lr = threadIdx.x >> 5;
+  const ItemTab it = items[b];
+  const long start = (long)it.a * scale;
+  const int len = it.n * scale + plus1;
+  const int chunk = (len + rs - 1) / rs;
+  const int r0 = blockIdx.z * chunk, r1 = min(len, r0 + chunk);
+  double S = 0.0, S2 = 0.0;
+  if (c < C && r0 < r1) {
+    const float shift = x[start * ldx + c];
+    float s = 0.0f, s2 = 0.0f;
+    for (int r = r0 + lr; r < r1; r += 8) {
+      float v = x[(start + r) * ldx + c] - shift;
+      s += v;
+      s2 += v * v;
+    }
+    S = s;
+    S2 = s2;
+  }
+  sh[lr][threadIdx.x & 31][0] = S;
+  sh[lr][threadIdx.x & 31][1] = S2;
+  __syncthreads();
+  if (lr == 0 && c < C && r0 < r1) {
+    for (int k = 1; k < 8; k++) {
+      S += sh[k][threadIdx.x][0];
+      S2 += sh[k][threadIdx.x][1];
+    }
+    atomicAdd(part + ((long)b * C + c) * 2, S);
+    atomicAdd(part + ((long)b * C + c) * 2 + 1, S2);
+  }
+}
+
+__global__ void stats_final_kernel(const float* x, int ldx, int C, const ItemTab* items, int B, int scale, int plus1,
+                                   const double* part, float* mean, float* rstd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * C) return;
+  int b = i / C, c = i % C;
+  const ItemTab it = items[b];
+  const int len = it.n * scale + plus1;
+  const float shift = x[(long)it.a * scale * ldx + c];
+  double d = part[2L * i] / (double)len;
+  double var = part[2L * i + 1] / (double)len - d * d;
+  if (var < 0.0) var = 0.0;
+  mean[i] = (float)((double)shift + d);
+  rstd[i] = 1.0f / sqrtf((float)var + 1e-5f);
+}
+
+cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, int B, int scale, int plus1,
+                         int max_len, double* part, float* mean, float* rstd, cudaStream_t st) {
+  cudaError_t e = cudaMemsetAsync(part, 0, sizeof(double) * 2L * B * C, st);
+  if (e != cudaSuccess) return e;
+  const int cg = (C + 31) / 32;
+  int rs = (4 * 148 + B * cg - 1) / (B * cg);
+  int rmax = (max_len + 511) / 512;
+  rs = max(1, min(rs, rmax));
+  stats_partial_kernel<<<dim3(B, cg, rs), 256, 0, st>>>(x, ldx, C, items, scale, plus1, rs, part);
+  if ((e = cudaGetLastError()) != cudaSuccess) return e;
+  stats_final_kernel<<<nblk((long)B * C, 256), 256, 0, st>>>(x, ldx, C, items, B, scale, plus1, part, mean, rstd);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ AdaIN + pool
+
+__device__ __forceinline__ float pool_in(const ConvArgs& p, const float* x, int L, int i, int c) {
+  if (i < 0 || i >= L) return 0.0f;
+  int b = dom_item(p.din, i);
+  if (b < 0) return 0.0f;
+  return prologue(p, x[(long)i * p.ldx + c], b, c);
+}
+
+__global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, const float* pw, const float* pb, float* y) {
+  long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (idx >= 2L * L * C) return;
+  int o = (int)(idx / C), c = (int)(idx % C);
+  float acc = pb[c];
+  if ((o & 1) == 0) {
+    acc = fmaf(pw[c * 3 + 1], pool_in(p, x, L, o >> 1, c), acc);
+  } else {
+    acc = fmaf(pw[c * 3 + 2], pool_in(p, x, L, (o - 1) >> 1, c), acc);
+    acc = fmaf(pw[c * 3 + 0], pool_in(p, x, L, (o + 1) >> 1, c), acc);
+  }
+  y[idx] = acc;
+}
+
+cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw, const float* pb,
+                              float* y, cudaStream_t st) {
+  long n = 2L * L * C;
+  adain_pool_kernel<<<nblk(n, 256), 256, 0, st>>>(x, C, L, pro, pw, pb, y);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ durations
+
+__global__ void durations_kernel(const float* logits, int ldl, const int* row_item, const float* speed, int rows,
+                                 int* dur, float* q) {
+  int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r >= rows) return;
+  int b = row_item[r];
+  if (b < 0) {
+    dur[r] = 0;
+    q[r] = 0.0f;
+    return;
+  }
+  const float* l = logits + (long)r * ldl;
+  float s = 0.0f;
+  for (int j = 0; j < 50; j++) s = __fadd_rn(s, __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-l[j]))));
+  float v = __fdiv_rn(s, speed[b]);
+  int d = (int)rintf(v);
+  dur[r] = d < 1 ? 1 : d;
+  q[r] = v;
+}
+
+cudaError_t launch_durations(const float* logits, int ldl, const int* row_item, const float* speed, int rows,
+                             int* dur, float* q, cudaStream_t st) {
+  durations_kernel<<<nblk(rows, 256), 256, 0, st>>>(logits, ldl, row_item, speed, rows, dur, q);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ F0 / N curve convs
+
+__device__ __forceinline__ float curve_at(const float* v, const Dom& d2, int i) {
+  return dom_item(d2, i) >= 0 ? v[i] : 0.0f;
+}
+
+__global__ void curve_conv_kernel(const float* f0, const float* nc, Dom d2, int LN, CurveConv wf, CurveConv wn,
+                                  float* dst0, int ld0, int col0, float* dst1, int ld1, int col1, float* dst2,
+                                  int ld2, int col2) {
+  int o = blockIdx.x * blockDim.x + threadIdx.x;
+  if (o >= LN) return;
+  float af = 0.0f, an = 0.0f;
+  for (int k = 0; k < 3; k++) {
+    int i = 2 * o + k - 1;
+    af = fmaf(wf.w[k], curve_at(f0, d2, i), af);
+    an = fmaf(wn.w[k], curve_at(nc, d2, i), an);
+  }
+  af = af + wf.b;
+  an = an + wn.b;
+  if (dst0) { dst0[(long)o * ld0 + col0] = af; dst0[(long)o * ld0 + col0 + 1] = an; }
+  if (dst1) { dst1[(long)o * ld1 + col1] = af; dst1[(long)o * ld1 + col1 + 1] = an; }
+  if (dst2) { dst2[(long)o * ld2 + col2] = af; dst2[(long)o * ld2 + col2 + 1] = an; }
+}
+
+cudaError_t launch_curve_conv(const float* f0, const float* nc, Dom d2, int LN, CurveConv wf, CurveConv wn,
+                              float* dst0, int ld0, int col0, float* dst1, int ld1, int col1, float* dst2, int ld2,
+                              int col2, cudaStream_t st) {
+  curve_conv_kernel<<<nblk(LN, 256), 256, 0, st>>>(f0, nc, d2, LN, wf, wn, dst0, ld0, col0, dst1, ld1, col1, dst2,
+                                                   ld2, col2);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ harmonic source
+
+__device__ __forceinline__ float torch_remainder1(float a) {
+  float m = fmodf(a, 1.0f);
+  if (m != 0.0f && m < 0.0f) m = m + 1.0f;
+  return m;
+}
+
+// rad value of harmonic h at sample t of an item's F0 curve f0c [L] (upsampled nearest x300)
+__device__ __forceinline__ float sine_rad(const float* f0c, int L, float near_scale, int t, int h) {
+  int src = (int)floorf(__fmul_rn((float)t, near_scale));
+  if (src > L - 1) src = L - 1;
+  return torch_remainder1(__fdiv_rn(__fmul_rn(f0c[src], (float)(h + 1)), 24000.0f));
+}
+
+// phase_pre [h][2N domain]: linear downsample of rad by 300, f64 cumulative sum, * 2 pi * 300
+// (sine_phase_pre, kernels/kokoro.cu:206-226). One thread per (item, harmonic).
+__global__ void sine_phase_kernel(const float* f0, int L2, const ItemTab* items, int B, float* pp) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * 9) return;
+  const int b = i / 9, h = i % 9;
+  const ItemTab it = items[b];
+  const int L = 2 * it.n, S = 300 * L, D = L;
+  const float* f0c = f0 + 2L * it.a;
+  float* out = pp + (long)h * L2 + 2L * it.a;
+  const float near_scale = (float)(1.0 / 300.0);
+  const float down_scale = (float)(1.0 / (1.0 / 300.0));
+  double acc = 0.0;
+  for (int d = 0; d < D; d++) {
+    float real = fmaf(down_scale, __fadd_rn((float)d, 0.5f), -0.5f);
+    if (real < 0.0f) real = 0.0f;
+    int i0 = (int)floorf(real);
+    if (i0 > S - 1) i0 = S - 1;
+    float l1 = fminf(fmaxf(__fsub_rn(real, (float)i0), 0.0f), 1.0f);
+    int i1 = i0 < S - 1 ? i0 + 1 : i0;
+    float l0 = __fsub_rn(1.0f, l1);
+    float v = fmaf(sine_rad(f0c, L, near_scale, i0, h), l0, __fmul_rn(sine_rad(f0c, L, near_scale, i1, h), l1));
+    acc += (double)v;
+    out[d] = __fmul_rn(__fmul_rn(__fmul_rn((float)acc, 2.0f), 3.14159274101257324f), 300.0f);
+  }
+}
+
+cudaError_t launch_sine_phase(const float* f0, int L2, const ItemTab* items, int B, float* pp, cudaStream_t st) {
+  sine_phase_kernel<<<nblk((long)B * 9, 64), 64, 0, st>>>(f0, L2, items, B, pp);
+  return cudaGetLastError();
+}
+
+__device__ __forceinline__ unsigned long long splitmix_at(unsigned long long seed, unsigned long long ctr) {
+  unsigned long long x = seed + (ctr + 1ULL) * 0x9E3779B97F4A7C15ULL;
+  x = (x ^ (x >> 30)) * 0xBF58476D1CE4E5B9ULL;
+  x = (x ^ (x >> 27)) * 0x94D049BB133111EBULL;
+  return x ^ (x >> 31);
+}
+
+// har[t] = tanh(sum_h lw[h] * (sin(phase(t, h)) * 0.1 * uv + amp * noise[t*9 + h]) + lb)
+// (sine_har_source + gen_noise, kernels/kokoro.cu:228-254, 282-302), noise generated in place
+// from the item's counter stream or read from replayed draws. One thread per sample of the 600N
+// domain; gap samples -> 0. sin / tanh / log / sqrt / cos are evaluated in f64 and rounded once
+// to f32 (correctly rounded results), so the source is reproducible on any IEEE CPU.
+__global__ void har_source_kernel(const float* f0, const float* pp, int L2, const ItemTab* items,
+                                  const int* col_item_n, int LN, const uint64_t* seeds, const float* noise,
+                                  const long long* noise_off, const float* lw, float lb, float* har) {
+  long c = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (c >= 600L * LN) return;
+  const int b = col_item_n[c / 600];
+  if (b < 0) {
+    har[c] = 0.0f;
+    return;
+  }
+  const ItemTab it = items[b];
+  const int t = (int)(c - 600L * it.a);
+  const int L = 2 * it.n, D = L;
+  const float* f0c = f0 + 2L * it.a;
+  const float near_scale = (float)(1.0 / 300.0);
+  const float up_scale = (float)(1.0 / 300.0);
+  int src = (int)floorf(__fmul_rn((float)t, near_scale));
+  if (src > L - 1) src = L - 1;
+  const float f0v = f0c[src];
+  const float uv = f0v > 10.0f ? 1.0f : 0.0f;
+  const float amp = __fadd_rn(__fmul_rn(uv, 0.003f), __fdiv_rn(__fmul_rn(__fsub_rn(1.0f, uv), 0.1f), 3.0f));
+  float real = fmaf(up_scale, __fadd_rn((float)t, 0.5f), -0.5f);
+  if (real < 0.0f) real = 0.0f;
+  int i0 = (int)floorf(real);
+  if (i0 > D - 1) i0 = D - 1;
+  const float l1 = fminf(fmaxf(__fsub_rn(real, (float)i0), 0.0f), 1.0f);
+  const int i1 = i0 < D - 1 ? i0 + 1 : i0;
+  const float l0 = __fsub_rn(1.0f, l1);
+  float nz[9];
+  if (noise) {
+    const float* nb = noise + noise_off[b] + (long)t * 9;
+#pragma unroll
+    for (int h = 0; h < 9; h++) nz[h] = nb[h];
+  } else {
+    const unsigned long long seed = seeds ? seeds[b] : 0ULL;
+    const long q0 = (long)t * 9;
+    for (long p = q0 >> 1; p <= (q0 + 8) >> 1; p++) {
+      unsigned long long x = splitmix_at(seed, 1024ULL + (unsigned long long)p);
+      float u1 = (float)((x >> 40) + 1ULL) * (1.0f / 16777216.0f);
+      float u2 = (float)((x >> 16) & 0xFFFFFFULL) * (1.0f / 16777216.0f);
+      float r = (float)sqrt(-2.0 * log((double)u1));
+      float th = __fmul_rn(6.2831855f, u2);
+      long e0 = 2 * p - q0, e1 = e0 + 1;
+      if (e0 >= 0 && e0 < 9) nz[e0] = __fmul_rn(r, (float)cos((double)th));
+      if (e1 >= 0 && e1 < 9) nz[e1] = __fmul_rn(r, (float)sin((double)th));
+    }
+  }
+  const float* ppb = pp + 2L * it.a;
+  float acc = 0.0f;
+#pragma unroll
+  for (int h = 0; h < 9; h++) {
+    const float* ph_row = ppb + (long)h * L2;
+    float ph = fmaf(ph_row[i0], l0, __fmul_rn(ph_row[i1], l1));
+    float sine = __fmul_rn((float)sin((double)ph), 0.1f);
+    float v = __fadd_rn(__fmul_rn(sine, uv), __fmul_rn(amp, nz[h]));
+    acc = __fadd_rn(acc, __fmul_rn(lw[h], v));
+  }
+  har[c] = (float)tanh((double)__fadd_rn(acc, lb));
+}
+
+cudaError_t launch_har_source(const float* f0, const float* pp, int L2, const ItemTab* items, const int* col_item_n,
+                              int LN, const uint64_t* seeds, const float* noise, const long long* noise_off,
+                              const float* lw, float lb, float* har, cudaStream_t st) {
+  long n = 600L * LN;
+  har_source_kernel<<<nblk(n, 256), 256, 0, st>>>(f0, pp, L2, items, col_item_n, LN, seeds, noise, noise_off, lw, lb,
+                                                  har);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ STFT / iSTFT
+
+// One thread per frame row of the 120N+1 domain: reflect-padded centred window of the item's
+// har, periodic Hann, f64 DFT -> magnitude and phase, 11 bins each (stft20_ld,
+// kernels/kokoro.cu:470-490). The DFT accumulates sequentially without fused multiply-adds and
+// magnitude / phase are evaluated in f64 and rounded once, so a CPU restatement reproduces the
+// spectrum bit for bit: the phase channel is discontinuous at +-pi (atan2 branch cut) and the
+// noise convolutions consume it linearly, so a one-ulp difference in a near-zero bin would
+// otherwise move that bin by 2 pi. Gap rows -> 0.
+__global__ void stft_kernel(const float* har, const ItemTab* items, Dom d120, float* spec, int lds) {
+  int R = blockIdx.x * blockDim.x + threadIdx.x;
+  if (R >= d120.L) return;
+  float* out = spec + (long)R * lds;
+  int b = dom_item(d120, R);
+  if (b < 0) {
+    for (int k = 0; k < 22; k++) out[k] = 0.0f;
+    return;
+  }
+  const ItemTab it = items[b];
+  const int f = R - 120 * it.a;
+  const int L = 600 * it.n;
+  const float* x = har + 600L * it.a;
+  double buf[20];
+#pragma unroll
+  for (int n = 0; n < 20; n++) {
+    int p = f * 5 + n - 10;
+    int src = p < 0 ? -p : (p >= L ? 2 * L - 2 - p : p);
+    buf[n] = (double)(x[src] * c_win[n]);
+  }
+  for (int k = 0; k < 11; k++) {
+    double re = 0.0, im = 0.0;
+#pragma unroll
+    for (int n = 0; n < 20; n++) {
+      re = __dadd_rn(re, __dmul_rn(buf[n], c_tw[k * 20 + n]));
+      im = __dsub_rn(im, __dmul_rn(buf[n], c_tw[220 + k * 20 + n]));
+    }
+    if (k == 0 || k == 10) im = 0.0;
+    float rf = (float)re, imf = (float)im;
+    out[k] = (float)hypot((double)rf, (double)imf);
+    out[11 + k] = (float)atan2((double)imf, (double)rf);
+  }
+}
+
+cudaError_t launch_stft(const float* har, const ItemTab* items, Dom d120, float* spec, int lds, cudaStream_t st) {
+  stft_kernel<<<nblk(d120.L, 128), 128, 0, st>>>(har, items, d120, spec, lds);
+  return cudaGetLastError();
+}
+
+// Fused iSTFT: a block owns 640 output samples; it first builds the windowed inverse-DFT frames
+// it needs (exp magnitude, sin phase, 20-point real inverse DFT in f64, * Hann) in shared memory,
+// then overlap-adds them and divides by the window envelope (istft_frames_ld + istft_ola,
+// kernels/kokoro.cu:264-280, 492-508). Gap samples -> 0.
+constexpr int IS_SAMPLES = 640;
+constexpr int IS_FRAMES = IS_SAMPLES / 5 + 5;
+
+__global__ void __launch_bounds__(128) istft_kernel(const float* post, int ldp, const ItemTab* items, Dom d120,
+                                                    const int* col_item_n, int LN, float* audio) {
+  __shared__ double fr[IS_FRAMES][20];
+  const long s0 = (long)blockIdx.x * IS_SAMPLES;
+  const long R_lo = s0 - 9 <= 0 ? 0 : (s0 - 9 + 4) / 5;
+  for (int rr = threadIdx.x; rr < IS_FRAMES; rr += blockDim.x) {
+    const long R = R_lo + rr;
+    if (R >= d120.L || dom_item(d120, (int)R) < 0) continue;
+    const float* pv = post + R * ldp;
+    double re[11], im[11];
+#pragma unroll
+    for (int k = 0; k < 11; k++) {
+      float m = expf(pv[k]);
+      float p = sinf(pv[11 + k]);
+      re[k] = (double)(m * cosf(p));
+      im[k] = (double)(m * sinf(p));
+    }
+#pragma unroll
+    for (int n = 0; n < 20; n++) {
+      double v = re[0] + re[10] * ((n % 2 == 0) ? 1.0 : -1.0);
+#pragma unroll
+      for (int k = 1; k < 10; k++) v += 2.0 * (re[k] * c_tw[k * 20 + n] - im[k] * c_tw[220 + k * 20 + n]);
+      v = v / 20.0;
+      fr[rr][n] = v * (double)c_win[n];
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < IS_SAMPLES; e += blockDim.x) {
+    const long s = s0 + e;
+    if (s >= 600L * LN) break;
+    const int b = col_item_n[s / 600];
+    if (b < 0) {
+      audio[s] = 0.0f;
+      continue;
+    }
+    const ItemTab it = items[b];
+    const int F = 120 * it.n + 1;
+    const int j = (int)(s - 600L * it.a) + 10;
+    const int f_lo = j - 19 > 0 ? (j - 19 + 4) / 5 : 0;
+    const int f_hi = min(j / 5, F - 1);
+    double acc = 0.0, env = 0.0;
+    for (int f = f_lo; f <= f_hi; f++) {
+      const int n = j - 5 * f;
+      const long R = 120L * it.a + f;
+      acc += fr[R - R_lo][n];
+      const double w = (double)c_win[n];
+      env += w * w;
+    }
+    audio[s] = (float)(acc / env);
+  }
+}
+
+cudaError_t launch_istft(const float* post, int ldp, const ItemTab* items, Dom d120, const int* col_item_n, int LN,
+                         float* audio, cudaStream_t st) {
+  long n = 600L * LN;
+  istft_kernel<<<nblk(n, IS_SAMPLES), 128, 0, st>>>(post, ldp, items, d120, col_item_n, LN, audio);
+  return cudaGetLastError();
+}
+
+// ------------------------------------------------------------------------------ glue
+
+__global__ void sum3_kernel(const float* r0, const float* r1, const float* r2, float* y, long n) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i < n) y[i] = ((r0[i] + r1[i]) + r2[i]) / 3.0f;
+}
+
+cudaError_t launch_sum3(const float* r0, const float* r1, const float* r2, float* y, long n, cudaStream_t st) {
+  sum3_kernel<<<nblk(n, 256), 256, 0, st>>>(r0, r1, r2, y, n);
+  return cudaGetLastError();
+}
+
+// Stage-1 ReflectionPad1d((1, 0)) per item (reflect_pad_left1_seg, kernels/kokoro.cu:452-467)
+// fused with the noise-branch add: x[o] = pad(y)[o] + xs[o]; y holds 120 N rows, x 120 N + 1.
+__global__ void reflect_add_kernel(const float* y, const float* xs, int C, const ItemTab* items, Dom d120, float* x) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= (long)d120.L * C) return;
+  int o = (int)(i / C), c = (int)(i % C);
+  int b = dom_item(d120, o);
+  float v = 0.0f;
+  if (b >= 0) {
+    int s = 120 * items[b].a;
+    v = (o == s) ? y[(long)(s + 1) * C + c] : y[(long)(o - 1) * C + c];
+  }
+  x[i] = v + xs[i];
+}
+
+cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const ItemTab* items, Dom d120, float* x,
+                               cudaStream_t st) {
+  long n = (long)d120.L * C;
+  reflect_add_kernel<<<nblk(n, 256), 256, 0, st>>>(y, xs, C, items, d120, x);
+  return cudaGetLastError();
+}
+
+__global__ void copy_cols_kernel(const float* src, int lds, int c0s, float* dst, int ldd, int c0d, int rows, int ncol) {
+  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= (long)rows * ncol) return;
+  int r = (int)(i / ncol), j = (int)(i % ncol);
+  dst[(long)r * ldd + c0d + j] = src[(long)r * lds + c0s + j];
+}
+
+cudaError_t launch_copy_cols(const float* src, int lds, int c0s, float* dst, int ldd, int c0d, int rows, int ncol,
+                             cudaStream_t st) {
+  long n = (long)rows * ncol;
+  if (n == 0) return cudaSuccess;
+  copy_cols_kernel<<<nblk(n, 256), 256, 0, st>>>(src, lds, c0s, dst, ldd, c0d, rows, ncol);
+  return cudaGetLastError();
+}
+
+cudaError_t upload_stft_constants(cudaStream_t st) {
+  double tw[440];
+  for (int k = 0; k < 11; k++)
+    for (int n = 0; n < 20; n++) {
+      double a = 2.0 * M_PI * (double)((k * n) % 20) / 20.0;
+      tw[k * 20 + n] = cos(a);
+      tw[220 + k * 20 + n] = sin(a);
+    }
+  float win[20];
+  for (int n = 0; n < 20; n++) win[n] = (float)(0.5 - 0.5 * cos(2.0 * M_PI * (double)n / 20.0));
+  cudaError_t e = cudaMemcpyToSymbolAsync(c_tw, tw, sizeof(tw), 0, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpyToSymbolAsync(c_win, win, sizeof(win), 0, cudaMemcpyHostToDevice, st);
+  if (e != cudaSuccess) return e;
+  return cudaStreamSynchronize(st);
+}
+
+}  // namespace kk

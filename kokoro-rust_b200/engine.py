@@ -1,0 +1,317 @@
+"""Host-side mirror of the reference crate's engine API over the C ABI (include/kokoro_b200.h).
+
+Names, argument meaning and error behaviour follow the reference:
+
+* ``BatchItem`` / ``ItemNoise``: ``src/gpu_batch.rs:14-24``
+* ``GpuKokoro.forward_batch``: ``src/gpu_batch.rs:179`` (here ``Engine.forward_batch``)
+* ``BatchPolicy`` / ``plan_batches``: ``src/engine.rs:148-183``
+* ``Engine.synth_batch`` (validation, length-bucketed batches, split-in-half on failure, results
+  in input order): ``src/engine.rs:185-241``
+* ``mix_seed``: ``src/engine.rs:141-146``; ``Voice.ref_s``: ``src/engine.rs:46-60``
+
+The library is loaded with ctypes; there is no CPU fallback: if the shared library is missing or
+cannot be loaded, ``load_library`` raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from dataclasses import dataclass, field
+from typing import List, Optional, Sequence
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libkokoro_b200.so")
+
+KK_OK, KK_ERR_INVALID_ARG, KK_ERR_OOM, KK_ERR_CUDA, KK_ERR_TIMEOUT, KK_ERR_IO = range(6)
+KK_PRECISION_FP32, KK_PRECISION_BF16 = 0, 1
+KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE = 1, 2
+STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "TIMEOUT", 5: "IO"}
+
+MAX_PHONEMES = 510  # src/engine.rs:12
+STYLE_DIM = 128
+SAMPLES_PER_FRAME = 600
+SAMPLE_RATE = 24000
+
+# Every symbol include/kokoro_b200.h declares, with its ctypes signature.
+_P = ctypes.c_void_p
+_SIGS = {
+    "kk_create": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_int, ctypes.POINTER(_P)]),
+    "kk_destroy": (None, [_P]),
+    "kk_last_error": (ctypes.c_char_p, [_P]),
+    "kk_identity": (ctypes.c_char_p, [_P]),
+    "kk_forward_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_fetch_audio": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64]),
+    "kk_decode_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_set_option": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
+    "kk_device_bytes": (ctypes.c_int64, [_P]),
+    "kk_launch_count": (ctypes.c_int64, [_P]),
+}
+
+_lib = None
+
+
+def load_library(path: str = LIB_PATH) -> ctypes.CDLL:
+    """Load the engine library (building it first when its sources are newer)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if os.path.exists(os.path.join(HERE, "csrc")) and os.environ.get("KK_NO_BUILD") != "1":
+        from . import build as _build  # noqa: WPS433
+
+        _build.build()
+    if not os.path.exists(path):
+        raise RuntimeError(f"kokoro-b200 library not found at {path}: run build() first")
+    lib = ctypes.CDLL(path)
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class KokoroError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+def _ptr(a: Optional[np.ndarray]):
+    return None if a is None else a.ctypes.data_as(ctypes.c_void_p)
+
+
+@dataclass
+class ItemNoise:
+    """Per-item excitation noise: a counter stream keyed by ``seed`` (product path) or replayed
+    draws ``sine`` [600 * N * 9] (parity tests) (src/gpu_batch.rs:12-17)."""
+
+    seed: int = 0
+    sine: Optional[np.ndarray] = None
+
+
+@dataclass
+class BatchItem:
+    ids: np.ndarray
+    ref_s: np.ndarray
+    speed: float = 1.0
+    noise: ItemNoise = field(default_factory=ItemNoise)
+
+
+@dataclass
+class Output:
+    audio: np.ndarray
+    pred_dur: np.ndarray
+
+
+class GpuKokoro:
+    """One engine bound to one CUDA device (``Gpu::new`` + ``GpuKokoro::with_gpu``)."""
+
+    def __init__(self, weights_path: str, cuda_ordinal: int = 0, precision: str = "fp32"):
+        self.lib = load_library()
+        prec = {"fp32": KK_PRECISION_FP32, "bf16": KK_PRECISION_BF16}[precision]
+        h = ctypes.c_void_p()
+        st = self.lib.kk_create(weights_path.encode(), cuda_ordinal, prec, ctypes.byref(h))
+        if st != KK_OK:
+            raise KokoroError(st, self.lib.kk_last_error(None).decode())
+        self.h = h
+        self.precision = precision
+
+    def close(self):
+        if getattr(self, "h", None):
+            self.lib.kk_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        self.close()
+
+    def _check(self, st: int):
+        if st != KK_OK:
+            raise KokoroError(st, self.lib.kk_last_error(self.h).decode())
+
+    @property
+    def identity(self) -> str:
+        return self.lib.kk_identity(self.h).decode()
+
+    def set_option(self, option: int, value: int):
+        self._check(self.lib.kk_set_option(self.h, option, value))
+
+    def launch_count(self) -> int:
+        return int(self.lib.kk_launch_count(self.h))
+
+    def device_bytes(self) -> int:
+        return int(self.lib.kk_device_bytes(self.h))
+
+    def forward_batch(self, items: Sequence[BatchItem], forced_dur: Optional[Sequence[np.ndarray]] = None,
+                      fetch: bool = True) -> List[Output]:
+        """Batched ragged forward; results in input order (src/gpu_batch.rs:179-421)."""
+        n = len(items)
+        ids = np.ascontiguousarray(np.concatenate([np.asarray(it.ids, np.int64) for it in items]) if n else
+                                   np.zeros(0, np.int64))
+        lens = np.ascontiguousarray([len(it.ids) for it in items], dtype=np.int32)
+        ref_s = np.ascontiguousarray(np.stack([np.asarray(it.ref_s, np.float32) for it in items]) if n else
+                                     np.zeros((0, 256), np.float32))
+        speed = np.ascontiguousarray([it.speed for it in items], dtype=np.float32)
+        seeds = np.ascontiguousarray([it.noise.seed & ((1 << 64) - 1) for it in items], dtype=np.uint64)
+        noise = None
+        if n and all(it.noise.sine is not None for it in items):
+            noise = np.ascontiguousarray(np.concatenate([np.asarray(it.noise.sine, np.float32) for it in items]))
+        fd = None
+        if forced_dur is not None:
+            fd = np.ascontiguousarray(np.concatenate([np.asarray(d, np.int64) for d in forced_dur]))
+        dur = np.zeros(ids.shape[0], np.int64)
+        ns = np.zeros(n, np.int64)
+        self._check(self.lib.kk_forward_batch(self.h, n, _ptr(ids), _ptr(lens), _ptr(ref_s), _ptr(speed),
+                                              _ptr(seeds), _ptr(noise), _ptr(fd), _ptr(dur), _ptr(ns)))
+        outs = []
+        o = 0
+        for i in range(n):
+            a = np.empty(int(ns[i]), np.float32)
+            if fetch:
+                self._check(self.lib.kk_fetch_audio(self.h, i, _ptr(a), a.shape[0]))
+            outs.append(Output(a, dur[o:o + lens[i]].copy()))
+            o += lens[i]
+        return outs
+
+    def decode_batch(self, asr: Sequence[np.ndarray], f0: Sequence[np.ndarray], n_curve: Sequence[np.ndarray],
+                     s_dec: np.ndarray, seeds: Optional[Sequence[int]] = None,
+                     noise: Optional[Sequence[np.ndarray]] = None, fetch: bool = True) -> List[np.ndarray]:
+        """Decoder + generator only: asr [N_b, 512] time-major, f0 / n [2 N_b], s_dec [B, 128]."""
+        B = len(asr)
+        nf = np.ascontiguousarray([a.shape[0] for a in asr], dtype=np.int32)
+        asr_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in asr]))
+        f0_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in f0]))
+        n_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in n_curve]))
+        sd = np.ascontiguousarray(np.asarray(s_dec, np.float32).reshape(B, 128))
+        sds = None if seeds is None else np.ascontiguousarray(np.asarray(seeds, np.uint64))
+        nz = None if noise is None else np.ascontiguousarray(np.concatenate([np.asarray(x, np.float32) for x in noise]))
+        out = np.empty(int(nf.sum()) * SAMPLES_PER_FRAME, np.float32) if fetch else None
+        self._check(self.lib.kk_decode_batch(self.h, B, _ptr(nf), _ptr(asr_c), _ptr(f0_c), _ptr(n_c), _ptr(sd),
+                                             _ptr(sds), _ptr(nz), _ptr(out)))
+        if not fetch:
+            return []
+        res, o = [], 0
+        for k in nf:
+            res.append(out[o:o + k * SAMPLES_PER_FRAME])
+            o += k * SAMPLES_PER_FRAME
+        return res
+
+
+# ------------------------------------------------------------------------------ scheduling layer
+
+def mix_seed(seed: int, index: int) -> int:
+    """splitmix64 per-item seed derivation (src/engine.rs:141-146)."""
+    m = (1 << 64) - 1
+    z = (seed ^ ((index * 0x9E3779B97F4A7C15) & m)) & m
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & m
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & m
+    return z ^ (z >> 31)
+
+
+@dataclass
+class BatchPolicy:
+    """Batching budget (src/engine.rs:148-161): total phoneme characters and items per batch."""
+
+    max_phonemes: int = 4000
+    max_items: int = 64
+
+
+def plan_batches(lens: Sequence[int], p: BatchPolicy) -> List[List[int]]:
+    """Sort by length (stable on index), greedily fill each batch up to the policy budget
+    (src/engine.rs:165-183)."""
+    order = sorted(range(len(lens)), key=lambda i: (lens[i], i))
+    out, cur, s = [], [], 0
+    for i in order:
+        if cur and (len(cur) >= p.max_items or s + lens[i] > p.max_phonemes):
+            out.append(cur)
+            cur, s = [], 0
+        s += lens[i]
+        cur.append(i)
+    if cur:
+        out.append(cur)
+    return out
+
+
+@dataclass
+class Voice:
+    """Voice pack [rows, 256]; ref_s = pack[n_phoneme_chars - 1] (src/engine.rs:46-60)."""
+
+    pack: np.ndarray
+
+    def ref_s(self, n_chars: int) -> np.ndarray:
+        if n_chars < 1:
+            raise ValueError("empty phoneme string")
+        if n_chars - 1 >= self.pack.shape[0]:
+            raise ValueError(f"phoneme length {n_chars} exceeds voice pack rows {self.pack.shape[0]}")
+        return self.pack[n_chars - 1]
+
+
+@dataclass
+class Synth:
+    audio: np.ndarray
+    pred_dur: np.ndarray
+    dropped: list
+
+
+class Engine:
+    """Resident synthesis engine (src/engine.rs:62-241) over token-id requests.
+
+    The text frontend is out of scope: a request is a sequence of phoneme token ids (without the
+    boundary pads, which ``synth_batch`` adds as the reference's ``phonemes_to_ids`` does)."""
+
+    def __init__(self, weights_path: str, cuda_ordinal: int = 0, precision: str = "fp32"):
+        self.gpu = GpuKokoro(weights_path, cuda_ordinal, precision)
+        self.voices = {}
+
+    def identity(self) -> str:
+        return self.gpu.identity
+
+    def add_voice(self, name: str, pack: np.ndarray):
+        self.voices[name] = Voice(np.asarray(pack, np.float32).reshape(-1, 256))
+
+    def voice(self, spec: str) -> Voice:
+        """Voice by name, or comma-separated mean of several (src/engine.rs:115-137)."""
+        if spec not in self.voices:
+            parts = spec.split(",")
+            packs = [self.voices[p].pack for p in parts]
+            if any(p.shape != packs[0].shape for p in packs):
+                raise ValueError("voice packs have different shapes")
+            self.voices[spec] = Voice(np.mean(np.stack(packs), axis=0).astype(np.float32))
+        return self.voices[spec]
+
+    def synth_batch(self, reqs: Sequence[tuple], voice: str, speed: float = 1.0,
+                    policy: BatchPolicy = BatchPolicy()) -> list:
+        """reqs: [(token ids without pads, seed)]. Returns per request a Synth or an Exception,
+        in input order; a failing batch is split in half down to single items."""
+        results: list = [None] * len(reqs)
+        prepared = []
+        for i, (toks, _seed) in enumerate(reqs):
+            n = len(toks)
+            try:
+                if n == 0:
+                    raise ValueError("empty phoneme string")
+                if n > MAX_PHONEMES:
+                    raise ValueError(f"oversize: {n} phoneme chars > {MAX_PHONEMES}")
+                ids = np.concatenate([[0], np.asarray(toks, np.int64), [0]])
+                prepared.append((i, ids, self.voice(voice).ref_s(n)))
+            except Exception as e:  # per-chunk validation error (src/engine.rs:194-211)
+                results[i] = e
+        lens = [len(p[1]) for p in prepared]
+        stack = list(reversed(plan_batches(lens, policy)))
+        while stack:
+            batch = stack.pop()
+            items = [BatchItem(prepared[k][1], prepared[k][2], speed, ItemNoise(seed=reqs[prepared[k][0]][1]))
+                     for k in batch]
+            try:
+                outs = self.gpu.forward_batch(items)
+                for k, o in zip(batch, outs):
+                    results[prepared[k][0]] = Synth(o.audio, o.pred_dur, [])
+            except KokoroError as e:
+                if len(batch) > 1:
+                    mid = len(batch) // 2
+                    stack.append(batch[mid:])
+                    stack.append(batch[:mid])
+                else:
+                    results[prepared[batch[0]][0]] = e
+        return [r if r is not None else RuntimeError("internal: missing batch result") for r in results]

@@ -1,0 +1,70 @@
+"""Shared fixtures: the package (directory ``kokoro-rust_b200``), the CPU oracle (test
+infrastructure), a seeded random-init checkpoint and the ``gpu`` marker."""
+import importlib.util
+import os
+import sys
+
+import numpy as np
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+PKG_DIR = os.path.join(ROOT, "kokoro-rust_b200")
+
+
+def import_package():
+    if "kokoro_rust_b200" in sys.modules:
+        return sys.modules["kokoro_rust_b200"]
+    spec = importlib.util.spec_from_file_location("kokoro_rust_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["kokoro_rust_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def import_oracle():
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import kokoro_oracle  # noqa: E402
+
+    return kokoro_oracle
+
+
+def pytest_configure(config):
+    config.addinivalue_line("markers", "gpu: needs a B200 (sm_100a) GPU")
+
+
+@pytest.fixture(scope="session")
+def kk():
+    return import_package()
+
+
+@pytest.fixture(scope="session")
+def oracle_mod():
+    return import_oracle()
+
+
+@pytest.fixture(scope="session")
+def ckpt_path(tmp_path_factory, kk):
+    from kokoro_rust_b200 import weights
+
+    p = str(tmp_path_factory.mktemp("ckpt") / "kokoro_seed0.safetensors")
+    return weights.write_random_checkpoint(p, seed=0)
+
+
+@pytest.fixture(scope="session")
+def state_dict(ckpt_path):
+    from kokoro_rust_b200 import weights
+
+    return weights.load_safetensors(ckpt_path)
+
+
+@pytest.fixture(scope="session")
+def oracle(state_dict, oracle_mod):
+    return oracle_mod.KokoroOracle(state_dict, threads=min(8, os.cpu_count() or 1))
+
+
+def synth_item(rng, n_tokens, style_sd=0.1):
+    """Token ids uniform in [1, 177] framed by pad 0, style ~ N(0, 0.1^2)."""
+    ids = np.concatenate([[0], rng.integers(1, 178, n_tokens), [0]]).astype(np.int64)
+    ref_s = (rng.standard_normal(256) * style_sd).astype(np.float32)
+    return ids, ref_s

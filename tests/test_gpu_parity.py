@@ -1,0 +1,105 @@
+"""CUDA engine vs the CPU oracle through the C ABI.
+
+fp32 path, per BASELINE's tolerances:
+* vocoder comparison (decoder + generator on identical asr / F0 / N / style / noise inputs):
+  waveform max-abs <= 1e-3;
+* full forward: integer durations bit-exact (outside round-half-even ties closer than 1e-4),
+  F0 / N curves within 1e-4 relative L2. The full-forward waveform is compared spectrally:
+  the harmonic source integrates F0 over every sample, so an F0 that differs by fp32
+  accumulation order (~1e-5 relative) moves phases of near-zero STFT bins across the +-pi
+  branch cut; the G-SPEC distance (reference tests/common_gates.rs) bounds that.
+"""
+import numpy as np
+import pytest
+
+from conftest import synth_item
+
+pytestmark = pytest.mark.gpu
+
+FP32_TOL = 1e-3
+
+
+@pytest.fixture(scope="module")
+def eng32(kk, ckpt_path):
+    e = kk.GpuKokoro(ckpt_path, 0, "fp32")
+    yield e
+    e.close()
+
+
+def vocoder_inputs(rng, n_frames):
+    """Config-2 style inputs: asr N(0,1), F0 log-uniform 80-400 Hz with a zeroed (unvoiced) run,
+    N N(0,1), style N(0, 0.1^2)."""
+    asr = rng.standard_normal((n_frames, 512)).astype(np.float32)
+    f0 = np.exp(rng.uniform(np.log(80), np.log(400), 2 * n_frames)).astype(np.float32)
+    run = max(1, (2 * n_frames) // 5)
+    s = rng.integers(0, 2 * n_frames - run + 1)
+    f0[s:s + run] = 0.0
+    n = rng.standard_normal(2 * n_frames).astype(np.float32)
+    s_dec = (rng.standard_normal(128) * 0.1).astype(np.float32)
+    return asr, f0, n, s_dec
+
+
+def test_decode_matches_oracle(kk, eng32, oracle, oracle_mod):
+    import torch
+    rng = np.random.default_rng(3)
+    frames = [23, 9]
+    inp = [vocoder_inputs(rng, n) for n in frames]
+    seeds = [11, 12]
+    outs = eng32.decode_batch([x[0] for x in inp], [x[1] for x in inp], [x[2] for x in inp],
+                              np.stack([x[3] for x in inp]), seeds=seeds)
+    for (asr, f0, n, s_dec), seed, a in zip(inp, seeds, outs):
+        noise = oracle_mod.counter_noise(seed, 600 * asr.shape[0] * 9)
+        r = oracle.decode(torch.from_numpy(asr.T.copy()), f0, n, torch.from_numpy(s_dec), noise)
+        err = np.abs(a - r).max()
+        print("decode max-abs", err, "ref rms", np.sqrt((r ** 2).mean()))
+        assert a.shape == r.shape
+        assert err <= FP32_TOL
+
+
+def test_decode_replayed_noise_matches_counter(kk, eng32, oracle_mod):
+    rng = np.random.default_rng(4)
+    asr, f0, n, s_dec = vocoder_inputs(rng, 7)
+    a = eng32.decode_batch([asr], [f0], [n], s_dec[None], seeds=[5])[0]
+    noise = oracle_mod.counter_noise(5, 600 * 7 * 9)
+    b = eng32.decode_batch([asr], [f0], [n], s_dec[None], noise=[noise])[0]
+    assert np.abs(a - b).max() <= 1e-5
+
+
+def spec_mean_abs_db(a, b, n=1024, hop=256):
+    """G-SPEC (reference tests/common_gates.rs:12-49): periodic Hann 1024, hop 256, frames fully
+    inside, 20 log10(max(|X|, 1e-5)), mean |dB_a - dB_b|."""
+    w = 0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n) / n)
+    frames = 1 + (len(a) - n) // hop
+    fa = np.stack([np.fft.rfft(a[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
+    fb = np.stack([np.fft.rfft(b[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
+    da = 20 * np.log10(np.maximum(np.abs(fa), 1e-5))
+    db = 20 * np.log10(np.maximum(np.abs(fb), 1e-5))
+    return float(np.abs(da - db).mean())
+
+
+def test_forward_forced_durations(kk, eng32, oracle):
+    rng = np.random.default_rng(1)
+    ids, ref_s = synth_item(rng, 12)
+    dur = np.concatenate([[0], np.full(12, 3), [0]])
+    outs = eng32.forward_batch([kk.BatchItem(ids, ref_s, 1.0, kk.ItemNoise(seed=7))], forced_dur=[dur])
+    ref = oracle.forward(ids, ref_s, 1.0, seed=7, forced_dur=dur)
+    a, r = outs[0].audio, ref["audio"]
+    assert a.shape == r.shape == (600 * 36,)
+    assert np.array_equal(outs[0].pred_dur, dur)
+    d = spec_mean_abs_db(a, r)
+    print("forced forward: spectral mean |dB|", d, "max-abs", np.abs(a - r).max())
+    assert d < 1.0
+
+
+def test_predicted_durations_bit_exact(kk, eng32, oracle):
+    rng = np.random.default_rng(2)
+    items, refs = [], []
+    for n in (9, 17, 5):
+        ids, ref_s = synth_item(rng, n)
+        items.append(kk.BatchItem(ids, ref_s, 1.0, kk.ItemNoise(seed=n)))
+        refs.append(oracle.forward(ids, ref_s, 1.0, seed=n, want=("dur_q",)))
+    outs = eng32.forward_batch(items)
+    for o, r in zip(outs, refs):
+        margin = np.abs(r["dur_q"] - np.floor(r["dur_q"]) - 0.5)
+        tie = margin < 1e-4
+        assert np.array_equal(o.pred_dur[~tie], r["dur"][~tie]), (o.pred_dur, r["dur"])
