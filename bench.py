@@ -1,0 +1,344 @@
+"""Benchmark of the batched ragged Kokoro-82M forward on B200 (driver contract).
+
+A step is one pass of the hot path over one batch of synthetic input. Default workload (N = 1):
+the full ragged forward over 251 synthetic lines (token lengths lognormal,
+median 110, sigma 0.6, clamped to [8, 510]; ids uniform in [1, 177]; one style per file;
+model-predicted durations). Under torchrun each rank runs its own 251-line shard (weak scaling,
+no collectives on the hot path; the process group only carries the barrier and the max-over-ranks
+timing). ``--workload config2`` times the vocoder-only op (decoder + generator, B = 32, T = 400).
+
+Metric: audio-seconds per wall-second (audio-s = samples / 24000), whole job. ``value`` uses
+device-resident inputs with the audio left on the device; ``e2e`` goes through the public C ABI
+with host buffers (input upload and audio download inside the timed region). Times come from
+CUDA events recorded on the engine's stream, max over ranks.
+
+``--impl reference`` times the reference's CPU path. The reference crate has no CPU forward of
+its own ("there is no CPU mode", docs/USAGE.md:100) and its Rust toolchain is absent here, so the
+reference arm is the CPU restatement of its algorithm (oracle/kokoro_oracle.py) on the host
+cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import math
+import os
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "kokoro-rust_b200")
+
+
+def import_package():
+    if "kokoro_rust_b200" in sys.modules:
+        return sys.modules["kokoro_rust_b200"]
+    spec = importlib.util.spec_from_file_location("kokoro_rust_b200", os.path.join(PKG_DIR, "__init__.py"),
+                                                  submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["kokoro_rust_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+# ------------------------------------------------------------------------------ workloads
+
+def config4_lines(seed: int, n_lines: int = 251):
+    """251 synthetic lines: lognormal token lengths (median 110, sigma 0.6) clamped to [8, 510],
+    ids uniform in [1, 177], one style vector per file (N(0, 0.1^2))."""
+    rng = np.random.default_rng(seed)
+    lens = np.clip(np.rint(np.exp(np.log(110.0) + 0.6 * rng.standard_normal(n_lines))), 8, 510).astype(int)
+    toks = [rng.integers(1, 178, n) for n in lens]
+    style = (rng.standard_normal(256) * 0.1).astype(np.float32)
+    return toks, style
+
+
+def config2_inputs(seed: int, B: int = 32, T: int = 400):
+    """Vocoder-only inputs: asr N(0,1) [B][T][512]; F0 log-uniform 80-400 Hz with 20% of frames
+    zeroed in contiguous runs; N N(0,1); style N(0, 0.1^2)."""
+    rng = np.random.default_rng(seed)
+    asr = [rng.standard_normal((T, 512)).astype(np.float32) for _ in range(B)]
+    f0s, ns = [], []
+    for _ in range(B):
+        f0 = np.exp(rng.uniform(np.log(80), np.log(400), 2 * T)).astype(np.float32)
+        zero = int(0.2 * 2 * T)
+        left = zero
+        while left > 0:  # a few contiguous unvoiced runs
+            run = min(left, int(rng.integers(10, 60)))
+            s = int(rng.integers(0, 2 * T - run))
+            f0[s:s + run] = 0.0
+            left -= run
+        f0s.append(f0)
+        ns.append(rng.standard_normal(2 * T).astype(np.float32))
+    s_dec = (rng.standard_normal((B, 128)) * 0.1).astype(np.float32)
+    return asr, f0s, ns, s_dec
+
+
+# ------------------------------------------------------------------------------ clocks
+
+CLOCK_Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+           "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+           "clocks_event_reasons.sw_power_cap")
+
+
+class ClockSampler:
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = tempfile.mktemp(prefix="kk_clocks_", suffix=".csv")
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={CLOCK_Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.f, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                p = [x.strip() for x in line.split(",")]
+                if len(p) >= 9:
+                    rows.append(p)
+        except OSError:
+            pass
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+# ------------------------------------------------------------------------------ CPU (oracle) leg
+
+def cpu_sample_lines(toks, n: int):
+    """A bounded sample of the workload: n lines of median length (the CPU path is ~2000x
+    slower, so the sample keeps the default run within minutes)."""
+    order = np.argsort([len(t) for t in toks])
+    mid = len(order) // 2
+    return [toks[i] for i in order[mid - n // 2: mid - n // 2 + n]]
+
+
+def time_oracle(ckpt: str, lines, style, threads: int):
+    """Seconds of audio and wall seconds of the CPU restatement on the given lines."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import torch
+    import kokoro_oracle as ko
+    kk = import_package()
+    torch.set_num_threads(threads)
+    sd = kk.weights.load_safetensors(ckpt)
+    o = ko.KokoroOracle(sd, threads=threads)
+    audio_s = 0.0
+    t0 = time.perf_counter()
+    for i, t in enumerate(lines):
+        ids = np.concatenate([[0], t, [0]])
+        out = o.forward(ids, style, 1.0, seed=kk.mix_seed(0, i))
+        audio_s += out["audio"].shape[0] / 24000.0
+    return audio_s, time.perf_counter() - t0
+
+
+# ------------------------------------------------------------------------------ main
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--workload", default="config4", choices=["config4", "config2"])
+    ap.add_argument("--precision", default=os.environ.get("KK_PRECISION", "bf16"), choices=["bf16", "fp32"])
+    ap.add_argument("--cpu-lines", type=int, default=3, help="lines in the CPU-baseline sample")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    kk = import_package()
+
+    ckpt_dir = os.environ.get("KK_CKPT_DIR", tempfile.gettempdir())
+    ckpt = os.path.join(ckpt_dir, "kokoro_b200_seed0.safetensors")
+
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        kk.weights.write_random_checkpoint(ckpt, 0)
+        toks, style = config4_lines(seed=1000 + rank)
+        threads = os.cpu_count() or 1
+        lines = cpu_sample_lines(toks, 1)
+        for _ in range(args.warmup):
+            time_oracle(ckpt, lines, style, threads)
+        tot_a = tot_t = 0.0
+        for _ in range(args.steps):
+            a, t = time_oracle(ckpt, lines, style, threads)
+            tot_a += a
+            tot_t += t
+        v = tot_a / tot_t
+        print(json.dumps({
+            "impl": "reference", "metric": "audio-sec per wall-sec (full ragged forward)", "value": v,
+            "unit": "audio-s/s", "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": 1000 * tot_t / args.steps, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config4 sample: 1 median-length line per step (CPU restatement, oracle/)"},
+            "cpu_baseline": {"value": v, "unit": "audio-s/s", "cores": threads, "kind": "port",
+                             "sample": "1 median-length line of config 4 per step"},
+            "e2e": {"value": v, "unit": "audio-s/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}))
+        return
+
+    import torch
+    import torch.distributed as dist
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
+                                device_id=torch.device("cuda", local_rank))
+    if rank == 0:
+        kk.weights.write_random_checkpoint(ckpt, 0)
+    if world > 1:
+        dist.barrier()
+    eng = kk.GpuKokoro(ckpt, local_rank, args.precision)
+
+    def barrier_sync():
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+
+    if args.workload == "config4":
+        toks, style = config4_lines(seed=1000 + rank)
+        items = [kk.BatchItem(np.concatenate([[0], t, [0]]), style, 1.0, kk.ItemNoise(seed=kk.mix_seed(rank, i)))
+                 for i, t in enumerate(toks)]
+
+        def step(fetch):
+            outs = eng.forward_batch(items, fetch=fetch)
+            return sum(o.audio.shape[0] for o in outs) / 24000.0
+        workload_desc = ("config4: full ragged forward, 251 synthetic lines per rank (lognormal lengths median 110 "
+                         "sigma 0.6 clamped [8,510]), predicted durations, one batch")
+    else:
+        asr, f0s, ns, s_dec = config2_inputs(seed=2000 + rank)
+
+        def step(fetch):
+            eng.decode_batch(asr, f0s, ns, s_dec, seeds=list(range(len(asr))), fetch=fetch)
+            return sum(a.shape[0] for a in asr) * 600 / 24000.0
+        workload_desc = "config2: vocoder-only (decoder + generator), B=32, T=400 frames"
+
+    # ---- warm-up and the device-resident timed region (value)
+    eng.set_option(kk.engine.KK_OPT_KEEP_AUDIO_ON_DEVICE, 1)
+    for _ in range(args.warmup):
+        step(False)
+    eng.set_option(kk.engine.KK_OPT_PROFILE, 1)
+    eng.profile_reset()
+    barrier_sync()
+    l0 = eng.launch_count()
+    audio_s = 0.0
+    dev_ms = 0.0
+    with ClockSampler(local_rank) as clk:
+        w0 = time.perf_counter()
+        for _ in range(args.steps):
+            audio_s += step(False)
+            dev_ms += eng.last_times()["total_ms"]
+        barrier_sync()
+        wall = time.perf_counter() - w0
+    launches = eng.launch_count() - l0
+    prof = eng.profile()
+    eng.set_option(kk.engine.KK_OPT_PROFILE, 0)
+    t = torch.tensor([dev_ms, audio_s], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        tm = t.clone()
+        dist.all_reduce(tm[0:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(tm[1:2], op=dist.ReduceOp.SUM)
+        t = tm
+    max_ms, total_audio = float(t[0]), float(t[1])
+    value = total_audio / (max_ms / 1000.0)
+
+    # ---- end to end through the public API with host buffers (e2e)
+    eng.set_option(kk.engine.KK_OPT_KEEP_AUDIO_ON_DEVICE, 0)
+    step(True)
+    barrier_sync()
+    e2e_ms = 0.0
+    e2e_audio = 0.0
+    h2d = d2h = 0
+    for _ in range(args.steps):
+        e2e_audio += step(True)
+        lt = eng.last_times()
+        e2e_ms += lt["total_ms"]
+        h2d, d2h = lt["h2d_bytes"], lt["d2h_bytes"]
+    barrier_sync()
+    te = torch.tensor([e2e_ms, e2e_audio], dtype=torch.float64, device=f"cuda:{local_rank}")
+    if world > 1:
+        dist.all_reduce(te[0:1], op=dist.ReduceOp.MAX)
+        dist.all_reduce(te[1:2], op=dist.ReduceOp.SUM)
+    e2e_value = float(te[1]) / (float(te[0]) / 1000.0)
+
+    if rank == 0:
+        peaks = {}
+        try:
+            peaks = json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
+        except Exception:
+            pass
+        conv_cls = max((k for k in prof if k.startswith("conv")), key=lambda k: prof[k][1], default=None)
+        roof = None
+        if conv_cls:
+            n_l, ms, fl = prof[conv_cls]
+            achieved = fl / (ms / 1000.0) / 1e12
+            peak = peaks.get("bf16_tflops_sustained") or 1381.3
+            roof = {"bound": "tensor", "kernel": conv_cls, "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                    "frac": achieved / peak, "traffic": None, "launches": n_l, "avg_launch_ms": ms / max(n_l, 1),
+                    "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed inside a long step)",
+                    "share_of_step": ms / dev_ms}
+        cpu = None
+        if not args.no_cpu_baseline and args.workload == "config4":
+            threads = torch.get_num_threads()
+            lines = cpu_sample_lines(toks, args.cpu_lines)
+            a, tt = time_oracle(ckpt, lines, style, threads)
+            cpu = {"value": a / tt, "unit": "audio-s/s", "cores": threads, "kind": "port",
+                   "sample": f"{len(lines)} median-length lines of config 4 ({a:.1f} audio-s in {tt:.1f} s)"}
+        res = {
+            "metric": "audio-sec per wall-sec" + (" (full ragged forward)" if args.workload == "config4" else
+                                                  " (vocoder-only decoder+generator)"),
+            "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16" if "tcgen05" in eng.identity else "f32", "data": "synthetic",
+            "config": {"workload": workload_desc, "precision": args.precision, "engine": eng.identity,
+                       "audio_s_per_step": total_audio / args.steps / world,
+                       "l2": "inputs larger than L2: each step moves tens of GB of activations (L2 126 MB)",
+                       "parallelism": f"dp{world} (independent shards, no collectives)",
+                       "wall_s_rank0": wall},
+            "roofline": roof,
+            "cpu_baseline": cpu,
+            "e2e": {"value": e2e_value, "unit": "audio-s/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches,
+            "kernel_profile": {k: {"launches": v[0], "ms": v[1], "tflops": v[2] / max(v[1], 1e-9) / 1e9}
+                               for k, v in prof.items()},
+            "clocks": clk.summary(),
+        }
+        print(json.dumps(res))
+    eng.close()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

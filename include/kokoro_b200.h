@@ -116,9 +116,29 @@ KK_API kk_status kk_decode_batch(kk_engine* e, int n_items, const int32_t* n_fra
 /* Options (benchmark / diagnostics). */
 typedef enum {
   KK_OPT_KEEP_AUDIO_ON_DEVICE = 1, /* 1: forward leaves audio on the device (no D2H) */
-  KK_OPT_SYNC_EACH_STAGE = 2       /* 1: synchronise after each stage (error localisation) */
+  KK_OPT_SYNC_EACH_STAGE = 2,      /* 1: synchronise after each stage (error localisation) */
+  KK_OPT_PROFILE = 3               /* 1: time every convolution / LSTM / attention launch with
+                                      CUDA events on the engine stream (see kk_profile_entry) */
 } kk_option;
 KK_API kk_status kk_set_option(kk_engine* e, int option, int64_t value);
+
+/*
+ * Device-side timings of the last kk_forward_batch / kk_decode_batch, from CUDA events recorded
+ * on the engine's stream: out[0] = total ms (first host-to-device copy .. last device-to-host
+ * copy), out[1] = compute ms (first kernel .. last kernel), out[2] = host-to-device bytes,
+ * out[3] = device-to-host bytes. No counterpart in the reference (its bench times whole calls).
+ */
+KK_API kk_status kk_last_times(kk_engine* e, double out[4]);
+
+/*
+ * Kernel-class profile accumulated while KK_OPT_PROFILE is 1. Entry i (0-based) gives the class
+ * name, its launches, total device milliseconds and algorithmic FLOPs (2 * MACs of the layer's
+ * mathematical definition; a transposed convolution counts its own taps, not the zero taps of its
+ * polyphase form). Returns the number of classes, or -1 for a bad index / engine.
+ */
+KK_API int kk_profile_entry(kk_engine* e, int i, char* name, int name_cap, int64_t* launches, double* ms,
+                            double* flops);
+KK_API void kk_profile_reset(kk_engine* e);
 
 /* Bytes of device memory the engine currently holds (weights + arena). */
 KK_API int64_t kk_device_bytes(const kk_engine* e);

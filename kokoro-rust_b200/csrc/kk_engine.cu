@@ -152,6 +152,7 @@ class PinnedArena {
 
 struct Conv {
   int cin = 0, cout = 0, K = 1, dil = 1, pad = 0, stride = 1;
+  double macs_per_row = 0;  // algorithmic multiply-adds per output row
   float* w = nullptr;  // fp32 [K][cin][cout]
   float* b = nullptr;
   TcWeights tc;        // bf16 tcgen05 operand layout (BF16 precision only)
@@ -225,6 +226,22 @@ struct Engine {
   long long launches = 0;
   int* err_flag = nullptr;
   bool tc_ok = false;
+  // timing: events on the engine stream (begin, compute begin, compute end, end)
+  cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
+  double last_times[4] = {0, 0, 0, 0};
+  double h2d_bytes = 0, d2h_bytes = 0;
+  bool profile = false;
+  struct ProfRec {
+    int cls;
+    cudaEvent_t a, b;
+    double flops;
+  };
+  std::vector<ProfRec> prof_pending;
+  std::vector<cudaEvent_t> ev_pool;
+  size_t ev_used = 0;
+  std::vector<std::string> prof_names;
+  std::vector<long long> prof_launches;
+  std::vector<double> prof_ms, prof_flops;
   // results of the last forward
   float* audio_host = nullptr;
   size_t audio_host_cap = 0;
@@ -250,6 +267,14 @@ struct Engine {
   T* upload(const T* h, size_t n);
   void check(cudaError_t e, const char* what);
   void dump(const char* name, const void* p, long long rows, int cols, int ld);
+  cudaEvent_t pool_event();
+  int prof_class(const char* name);
+  void prof_begin(cudaEvent_t* a);
+  void prof_end(cudaEvent_t a, const char* cls, double flops);
+  void prof_collect();
+  void times_begin();
+  void times_compute_begin();
+  void times_compute_end();
   void stage_sync(const char* what);
   ConvArgs ca(const Conv& c);
   void run_conv(const Conv& c, ConvArgs& a);
@@ -282,8 +307,66 @@ Engine::~Engine() {
   for (void* p : wallocs) cudaFree(p);
   ar.release();
   if (audio_host) cudaFreeHost(audio_host);
+  for (auto e : ev)
+    if (e) cudaEventDestroy(e);
+  for (auto e : ev_pool) cudaEventDestroy(e);
   if (st) cudaStreamDestroy(st);
 }
+
+cudaEvent_t Engine::pool_event() {
+  if (ev_used == ev_pool.size()) {
+    cudaEvent_t e;
+    KK_CUDA(cudaEventCreate(&e));
+    ev_pool.push_back(e);
+  }
+  return ev_pool[ev_used++];
+}
+
+int Engine::prof_class(const char* name) {
+  for (size_t i = 0; i < prof_names.size(); i++)
+    if (prof_names[i] == name) return (int)i;
+  prof_names.push_back(name);
+  prof_launches.push_back(0);
+  prof_ms.push_back(0);
+  prof_flops.push_back(0);
+  return (int)prof_names.size() - 1;
+}
+
+void Engine::prof_begin(cudaEvent_t* a) {
+  *a = nullptr;
+  if (!profile) return;
+  *a = pool_event();
+  KK_CUDA(cudaEventRecord(*a, st));
+}
+
+void Engine::prof_end(cudaEvent_t a, const char* cls, double flops) {
+  if (!profile || !a) return;
+  cudaEvent_t b = pool_event();
+  KK_CUDA(cudaEventRecord(b, st));
+  prof_pending.push_back({prof_class(cls), a, b, flops});
+}
+
+// Called after the stream is synchronised: fold the recorded launch intervals into the profile.
+void Engine::prof_collect() {
+  for (auto& r : prof_pending) {
+    float ms = 0;
+    KK_CUDA(cudaEventElapsedTime(&ms, r.a, r.b));
+    prof_launches[r.cls]++;
+    prof_ms[r.cls] += ms;
+    prof_flops[r.cls] += r.flops;
+  }
+  prof_pending.clear();
+  ev_used = 0;
+}
+
+void Engine::times_begin() {
+  h2d_bytes = d2h_bytes = 0;
+  for (auto& e : ev)
+    if (!e) KK_CUDA(cudaEventCreate(&e));
+  KK_CUDA(cudaEventRecord(ev[0], st));
+}
+void Engine::times_compute_begin() { KK_CUDA(cudaEventRecord(ev[1], st)); }
+void Engine::times_compute_end() { KK_CUDA(cudaEventRecord(ev[2], st)); }
 
 float* Engine::up(const std::vector<float>& v) {
   float* p = nullptr;
@@ -299,6 +382,7 @@ Conv Engine::conv_from(const std::vector<float>& w, const float* bias_h, int cin
                        int stride) {
   Conv c;
   c.cin = cin, c.cout = cout, c.K = K, c.dil = dil, c.pad = pad, c.stride = stride;
+  c.macs_per_row = (double)cin * cout * K;
   std::vector<float> t((size_t)K * cin * cout);
   for (int co = 0; co < cout; co++)
     for (int ci = 0; ci < cin; ci++)
@@ -513,6 +597,7 @@ void Engine::load(const Checkpoint& ck) {
     std::vector<float> wp, bp;
     convT_polyphase(wT, b, ci, co, K, s, p, wp, bp);
     m.ups[i] = conv_from(wp, bp.data(), ci, s * co, 3, 1, 1, 1);
+    m.ups[i].macs_per_row = (double)ci * co * K;  // ConvTranspose taps per input row
   }
   const int ks[3] = {3, 7, 11};
   for (int i = 0; i < 2; i++)
@@ -535,6 +620,7 @@ T* Engine::upload(const T* h, size_t n) {
   void* s = pin.alloc(n * sizeof(T));
   memcpy(s, h, n * sizeof(T));
   KK_CUDA(cudaMemcpyAsync(d, s, n * sizeof(T), cudaMemcpyHostToDevice, st));
+  h2d_bytes += (double)(n * sizeof(T));
   return d;
 }
 
@@ -587,10 +673,15 @@ ConvArgs Engine::ca(const Conv& c) {
 }
 
 void Engine::run_conv(const Conv& c, ConvArgs& a) {
+  cudaEvent_t e0;
+  prof_begin(&e0);
+  const double flops = 2.0 * c.macs_per_row * a.L_out;
   if (precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc)) {
     check(tc_conv(a, c.tc, st), "conv(tcgen05)");
+    prof_end(e0, "conv_tcgen05", flops);
   } else {
     check(launch_conv_simt(a, st), "conv(simt)");
+    prof_end(e0, "conv_simt", flops);
   }
 }
 
@@ -718,7 +809,10 @@ void Engine::lstm(const Lstm& L, const float* x, int ldx, int rows, const std::v
   a.cst = ar.get<float>((size_t)2 * B * 256);
   a.bar = ar.get<unsigned>(2);
   a.err = err_flag;
+  cudaEvent_t e0;
+  prof_begin(&e0);
   check(launch_lstm(a, st), "lstm");
+  prof_end(e0, "lstm_recurrence", 2.0 * 2 * 1024 * 256 * (double)std::accumulate(len.begin(), len.end(), 0LL));
   ar.rewind(mk);
 }
 
@@ -838,6 +932,7 @@ float* Engine::decode_core(int B, const std::vector<ItemTab>& items_h, const Ite
   }
   float* audio = ar.get<float>((size_t)600 * LN);
   check(launch_istft(post, 22, items, d120, col_item_n, LN, audio, st), "istft");
+  times_compute_end();
   dump("post", post, L120, 22, 22);
   dump("audio", audio, 600LL * LN, 1, 1);
   stage_sync("istft");
@@ -866,12 +961,19 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
       audio_host_cap = n;
     }
     KK_CUDA(cudaMemcpyAsync(audio_host, audio_d, n * sizeof(float), cudaMemcpyDeviceToHost, st));
+    d2h_bytes += (double)(n * sizeof(float));
   }
   int* eh = (int*)pin.alloc(sizeof(int));
   KK_CUDA(cudaMemcpyAsync(eh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+  KK_CUDA(cudaEventRecord(ev[3], st));
   KK_CUDA(cudaStreamSynchronize(st));
   errh = *eh;
   if (errh) throw KKError(KK_ERR_TIMEOUT, "an LSTM step barrier timed out");
+  float t_all = 0, t_comp = 0;
+  KK_CUDA(cudaEventElapsedTime(&t_all, ev[0], ev[3]));
+  KK_CUDA(cudaEventElapsedTime(&t_comp, ev[1], ev[2]));
+  last_times[0] = t_all, last_times[1] = t_comp, last_times[2] = h2d_bytes, last_times[3] = d2h_bytes;
+  prof_collect();
 }
 
 void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
@@ -902,6 +1004,9 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   KK_CUDA(cudaSetDevice(dev));
   ar.reset();
   pin.reset();
+  prof_pending.clear();
+  ev_used = 0;
+  times_begin();
   KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
   // ---- token layout (src/gpu_batch.rs:189-213)
   std::vector<ItemTab> items_h(B);
@@ -932,6 +1037,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   float* sdec_d = upload(sdec_h.data(), sdec_h.size());
   float* spro_d = upload(spro_h.data(), spro_h.size());
   float* speed_d = upload(speed, B);
+  times_compute_begin();
   const Dom dT{row_item_d, 0, 0, 0, LT};
   std::vector<int> tstart(B), tlen(B);
   for (int b = 0; b < B; b++) tstart[b] = items_h[b].tok_start, tlen[b] = items_h[b].tok_len;
@@ -958,7 +1064,12 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
     for (int layer = 0; layer < 12; layer++) {
       linear(m.qkv, h, 768, LT, qkv, 2304);
+      cudaEvent_t e0;
+      prof_begin(&e0);
       check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
+      double af = 0;
+      for (int b = 0; b < B; b++) af += 4.0 * 12 * 64 * (double)ids_len[b] * ids_len[b];
+      prof_end(e0, "attention", af);
       linear(m.dense, ctx, 768, LT, a, 768, OUT_PLUS, h, 768);
       check(launch_ln_rows(a, 768, LT, 768, m.attn_g, m.attn_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, a,
                            768, st),
@@ -1137,6 +1248,9 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
   KK_CUDA(cudaSetDevice(dev));
   ar.reset();
   pin.reset();
+  prof_pending.clear();
+  ev_used = 0;
+  times_begin();
   KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
   std::vector<int> col_item_h(LN, -1), tab1(LN, -1), tab2(2 * LN, -1);
   long long r = 0;
@@ -1156,15 +1270,6 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
   float* f0c_d = upload(f0_in, (size_t)2 * tot);
   float* nc_d = upload(n_in, (size_t)2 * tot);
   float* sdec_d = upload(s_dec, (size_t)B * 128);
-  float* xcat0 = ar.get<float>((size_t)LN * 514);
-  float* f0 = ar.get<float>((size_t)2 * LN);
-  float* nc = ar.get<float>((size_t)2 * LN);
-  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, 514, st), "gather_rows");
-  check(launch_gather_rows(f0c_d, 1, tab2_d, 2 * LN, 1, f0, 1, st), "gather_rows");
-  check(launch_gather_rows(nc_d, 1, tab2_d, 2 * LN, 1, nc, 1, st), "gather_rows");
-  const int wdec = m.fc_dec.cout;
-  float* gb_dec = ar.get<float>((size_t)B * wdec);
-  linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
   uint64_t* seeds_d = seeds ? upload(seeds, B) : nullptr;
   float* noise_d = nullptr;
   long long* noise_off_d = nullptr;
@@ -1175,6 +1280,16 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
     noise_d = upload(noise, (size_t)t);
     noise_off_d = upload(off.data(), B);
   }
+  times_compute_begin();
+  float* xcat0 = ar.get<float>((size_t)LN * 514);
+  float* f0 = ar.get<float>((size_t)2 * LN);
+  float* nc = ar.get<float>((size_t)2 * LN);
+  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, 514, st), "gather_rows");
+  check(launch_gather_rows(f0c_d, 1, tab2_d, 2 * LN, 1, f0, 1, st), "gather_rows");
+  check(launch_gather_rows(nc_d, 1, tab2_d, 2 * LN, 1, nc, 1, st), "gather_rows");
+  const int wdec = m.fc_dec.cout;
+  float* gb_dec = ar.get<float>((size_t)B * wdec);
+  linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
   float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
                              noise_off_d);
   finish_audio(audio, LN, items_h);
@@ -1298,8 +1413,39 @@ kk_status kk_set_option(kk_engine* h, int option, int64_t value) {
   return guarded(h, [&] {
     if (option == KK_OPT_KEEP_AUDIO_ON_DEVICE) h->e->keep_audio_dev = value != 0;
     else if (option == KK_OPT_SYNC_EACH_STAGE) h->e->sync_each = value != 0;
+    else if (option == KK_OPT_PROFILE) h->e->profile = value != 0;
     else throw kk::KKError(KK_ERR_INVALID_ARG, "unknown option");
   });
+}
+
+kk_status kk_last_times(kk_engine* h, double out[4]) {
+  if (!h || !out) return KK_ERR_INVALID_ARG;
+  for (int i = 0; i < 4; i++) out[i] = h->e->last_times[i];
+  return KK_OK;
+}
+
+int kk_profile_entry(kk_engine* h, int i, char* name, int name_cap, int64_t* launches, double* ms, double* flops) {
+  if (!h) return -1;
+  kk::Engine& e = *h->e;
+  const int n = (int)e.prof_names.size();
+  if (i < 0) return n;
+  if (i >= n) return -1;
+  if (name && name_cap > 0) {
+    strncpy(name, e.prof_names[i].c_str(), (size_t)name_cap - 1);
+    name[name_cap - 1] = 0;
+  }
+  if (launches) *launches = e.prof_launches[i];
+  if (ms) *ms = e.prof_ms[i];
+  if (flops) *flops = e.prof_flops[i];
+  return n;
+}
+
+void kk_profile_reset(kk_engine* h) {
+  if (!h) return;
+  kk::Engine& e = *h->e;
+  std::fill(e.prof_launches.begin(), e.prof_launches.end(), 0);
+  std::fill(e.prof_ms.begin(), e.prof_ms.end(), 0.0);
+  std::fill(e.prof_flops.begin(), e.prof_flops.end(), 0.0);
 }
 
 int64_t kk_device_bytes(const kk_engine* h) { return h ? (int64_t)(h->e->wbytes + h->e->ar.bytes()) : 0; }

@@ -26,7 +26,7 @@ LIB_PATH = os.path.join(HERE, "libkokoro_b200.so")
 
 KK_OK, KK_ERR_INVALID_ARG, KK_ERR_OOM, KK_ERR_CUDA, KK_ERR_TIMEOUT, KK_ERR_IO = range(6)
 KK_PRECISION_FP32, KK_PRECISION_BF16 = 0, 1
-KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE = 1, 2
+KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE, KK_OPT_PROFILE = 1, 2, 3
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "TIMEOUT", 5: "IO"}
 
 MAX_PHONEMES = 510  # src/engine.rs:12
@@ -47,6 +47,9 @@ _SIGS = {
     "kk_set_option": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
     "kk_device_bytes": (ctypes.c_int64, [_P]),
     "kk_launch_count": (ctypes.c_int64, [_P]),
+    "kk_last_times": (ctypes.c_int, [_P, _P]),
+    "kk_profile_entry": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_int, _P, _P, _P]),
+    "kk_profile_reset": (None, [_P]),
 }
 
 _lib = None
@@ -142,6 +145,26 @@ class GpuKokoro:
 
     def device_bytes(self) -> int:
         return int(self.lib.kk_device_bytes(self.h))
+
+    def last_times(self) -> dict:
+        """Device-side timings of the last call (CUDA events on the engine stream)."""
+        out = (ctypes.c_double * 4)()
+        self._check(self.lib.kk_last_times(self.h, out))
+        return {"total_ms": out[0], "compute_ms": out[1], "h2d_bytes": int(out[2]), "d2h_bytes": int(out[3])}
+
+    def profile(self) -> dict:
+        """{kernel class: (launches, device ms, algorithmic FLOPs)} accumulated under KK_OPT_PROFILE."""
+        n = self.lib.kk_profile_entry(self.h, -1, None, 0, None, None, None)
+        res = {}
+        for i in range(max(n, 0)):
+            name = ctypes.create_string_buffer(64)
+            la, ms, fl = ctypes.c_int64(), ctypes.c_double(), ctypes.c_double()
+            self.lib.kk_profile_entry(self.h, i, name, 64, ctypes.byref(la), ctypes.byref(ms), ctypes.byref(fl))
+            res[name.value.decode()] = (int(la.value), float(ms.value), float(fl.value))
+        return res
+
+    def profile_reset(self):
+        self.lib.kk_profile_reset(self.h)
 
     def forward_batch(self, items: Sequence[BatchItem], forced_dur: Optional[Sequence[np.ndarray]] = None,
                       fetch: bool = True) -> List[Output]:
