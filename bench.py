@@ -170,6 +170,8 @@ def main():
     ap.add_argument("--precision", default=os.environ.get("KK_PRECISION", "bf16"), choices=["bf16", "fp32"])
     ap.add_argument("--cpu-lines", type=int, default=3, help="lines in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--items", type=int, default=32, help="config2: utterances per batch")
+    ap.add_argument("--frames", type=int, default=400, help="config2: frames per utterance")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -236,12 +238,12 @@ def main():
         workload_desc = ("config4: full ragged forward, 251 synthetic lines per rank (lognormal lengths median 110 "
                          "sigma 0.6 clamped [8,510]), predicted durations, one batch")
     else:
-        asr, f0s, ns, s_dec = config2_inputs(seed=2000 + rank)
+        asr, f0s, ns, s_dec = config2_inputs(seed=2000 + rank, B=args.items, T=args.frames)
 
         def step(fetch):
             eng.decode_batch(asr, f0s, ns, s_dec, seeds=list(range(len(asr))), fetch=fetch)
             return sum(a.shape[0] for a in asr) * 600 / 24000.0
-        workload_desc = "config2: vocoder-only (decoder + generator), B=32, T=400 frames"
+        workload_desc = f"config2: vocoder-only (decoder + generator), B={args.items}, T={args.frames} frames"
 
     # ---- warm-up and the device-resident timed region (value)
     eng.set_option(kk.engine.KK_OPT_KEEP_AUDIO_ON_DEVICE, 1)

@@ -74,6 +74,7 @@ struct ConvArgs {
   const float* gb;    // gamma|beta rows: item b at gb + b*ldgb, gamma [0,cin), beta [cin,2cin)
   int ldgb;
   const float* alpha; // [cin]
+  const float2* coef; // optional [B][cin] AdaIN folded to x * A + B (tensor-core path only)
   Dom din;            // domain of the input rows (after in_up2)
   // weights: f32 [K][cout][cin] (SIMT path)
   const float* w;

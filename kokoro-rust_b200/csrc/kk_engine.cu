@@ -210,6 +210,11 @@ struct Model {
 };
 
 static const int DILS[3] = {1, 3, 5};
+// Row strides of the decoder's channel-concatenation buffers, rounded up to 16 bytes so that
+// tensor-memory-access copies and vector loads apply: [asr | f0 | n] (514 channels) and
+// [x | asr_res | f0 | n] (1090 channels).
+static const int X0_LD = 516;
+static const int CAT_LD = 1092;
 
 struct Engine {
   int dev = 0;
@@ -226,6 +231,8 @@ struct Engine {
   long long launches = 0;
   int* err_flag = nullptr;
   bool tc_ok = false;
+  const char* tc_trace_dir = getenv("KK_TC_TRACE_DIR");  // diagnostics: per-launch pipeline cycle accounting
+  int cur_B = 0;  // items of the batch being run
   // timing: events on the engine stream (begin, compute begin, compute end, end)
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
   double last_times[4] = {0, 0, 0, 0};
@@ -677,7 +684,25 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   prof_begin(&e0);
   const double flops = 2.0 * c.macs_per_row * a.L_out;
   if (precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc)) {
-    check(tc_conv(a, c.tc, st), "conv(tcgen05)");
+    unsigned long long* tr = nullptr;
+    if (tc_trace_dir) {
+      tr = ar.get<unsigned long long>(16);
+      KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
+    }
+    check(tc_conv(a, c.tc, err_flag, st, tr), "conv(tcgen05)");
+    if (tr) {
+      unsigned long long h[16];
+      KK_CUDA(cudaStreamSynchronize(st));
+      KK_CUDA(cudaMemcpy(h, tr, sizeof(h), cudaMemcpyDeviceToHost));
+      FILE* f = fopen((std::string(tc_trace_dir) + "/tc_trace.txt").c_str(), "a");
+      if (f) {
+        fprintf(f, "K=%d dil=%d cin=%d cout=%d L=%d in=%d out=%d |", a.K, a.dil, a.cin, a.cout, a.L_out, a.in_mode,
+                a.out_mode);
+        for (int i = 0; i < 12; i++) fprintf(f, " %llu", h[i]);
+        fprintf(f, "\n");
+        fclose(f);
+      }
+    }
     prof_end(e0, "conv_tcgen05", flops);
   } else {
     check(launch_conv_simt(a, st), "conv(simt)");
@@ -707,6 +732,12 @@ void Engine::adain_args(ConvArgs& a, const AdaIN& n, const float* mean, const fl
   a.in_mode = mode;
   a.mean = mean, a.rstd = rstd, a.nw = n.nw, a.nb = n.nb, a.gb = gb + n.off, a.ldgb = ldgb, a.slope = slope,
   a.alpha = alpha;
+  a.coef = nullptr;
+  if (precision == KK_PRECISION_BF16 && tc_ok) {
+    float2* coef = ar.get<float2>((size_t)cur_B * n.c);
+    check(launch_adain_coef(mean, rstd, n.nw, n.nb, gb + n.off, ldgb, cur_B, n.c, coef, st), "adain_coef");
+    a.coef = coef;
+  }
 }
 
 // AdainResBlk1d (src/gpu_batch.rs:103-135): y = (conv2(act(AdaIN2(conv1(pool?(act(AdaIN1(x))))))) + sc) / sqrt(2)
@@ -829,26 +860,26 @@ float* Engine::decode_core(int B, const std::vector<ItemTab>& items_h, const Ite
   const Dom d120{col_item_n, LN, 120, 1, 120 * LN + 1};
   const int L2 = 2 * LN, L20 = 20 * LN, L120 = 120 * LN + 1;
   // ---- decoder (pre-generator)
-  float* catA = ar.get<float>((size_t)LN * 1090);
-  float* catB = ar.get<float>((size_t)LN * 1090);
+  float* catA = ar.get<float>((size_t)LN * CAT_LD);
+  float* catB = ar.get<float>((size_t)LN * CAT_LD);
   CurveConv wf{m.f0conv_w, m.f0conv_b}, wn{m.nconv_w, m.nconv_b};
-  check(launch_curve_conv(f0, nc, d2, LN, wf, wn, xcat0, 514, 512, catA, 1090, 1088, catB, 1090, 1088, st),
+  check(launch_curve_conv(f0, nc, d2, LN, wf, wn, xcat0, X0_LD, 512, catA, CAT_LD, 1088, catB, CAT_LD, 1088, st),
         "curve_conv");
   {
     ConvArgs a = ca(m.asr_res);
-    a.x = xcat0, a.ldx = 514, a.in_mode = IN_MASK, a.din = dN, a.L_in = LN;
-    a.y = catA + 1024, a.ldy = 1090, a.L_out = LN;
+    a.x = xcat0, a.ldx = X0_LD, a.in_mode = IN_MASK, a.din = dN, a.L_in = LN;
+    a.y = catA + 1024, a.ldy = CAT_LD, a.L_out = LN;
     run_conv(m.asr_res, a);
-    check(launch_copy_cols(catA, 1090, 1024, catB, 1090, 1024, LN, 64, st), "copy_cols");
+    check(launch_copy_cols(catA, CAT_LD, 1024, catB, CAT_LD, 1024, LN, 64, st), "copy_cols");
   }
-  dump("xcat0", xcat0, LN, 514, 514);
-  resblk(m.enc, xcat0, 514, dN, dN, catA, 1090, gb_dec, ldgb, items, B, max_n);
-  dump("enc", catA, LN, 1090, 1090);
-  resblk(m.dec[0], catA, 1090, dN, dN, catB, 1090, gb_dec, ldgb, items, B, max_n);
-  resblk(m.dec[1], catB, 1090, dN, dN, catA, 1090, gb_dec, ldgb, items, B, max_n);
-  resblk(m.dec[2], catA, 1090, dN, dN, catB, 1090, gb_dec, ldgb, items, B, max_n);
+  dump("xcat0", xcat0, LN, 514, X0_LD);
+  resblk(m.enc, xcat0, X0_LD, dN, dN, catA, CAT_LD, gb_dec, ldgb, items, B, max_n);
+  dump("enc", catA, LN, 1090, CAT_LD);
+  resblk(m.dec[0], catA, CAT_LD, dN, dN, catB, CAT_LD, gb_dec, ldgb, items, B, max_n);
+  resblk(m.dec[1], catB, CAT_LD, dN, dN, catA, CAT_LD, gb_dec, ldgb, items, B, max_n);
+  resblk(m.dec[2], catA, CAT_LD, dN, dN, catB, CAT_LD, gb_dec, ldgb, items, B, max_n);
   float* xd = ar.get<float>((size_t)L2 * 512);
-  resblk(m.dec[3], catB, 1090, dN, d2, xd, 512, gb_dec, ldgb, items, B, max_n);
+  resblk(m.dec[3], catB, CAT_LD, dN, d2, xd, 512, gb_dec, ldgb, items, B, max_n);
   dump("xd", xd, L2, 512, 512);
   stage_sync("decoder");
   // ---- harmonic source + STFT (one launch each for the whole batch)
@@ -968,7 +999,8 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
   KK_CUDA(cudaEventRecord(ev[3], st));
   KK_CUDA(cudaStreamSynchronize(st));
   errh = *eh;
-  if (errh) throw KKError(KK_ERR_TIMEOUT, "an LSTM step barrier timed out");
+  if (errh) throw KKError(KK_ERR_TIMEOUT, errh == 1 ? "an LSTM step barrier timed out"
+                                                    : "a tcgen05 convolution pipeline wait timed out");
   float t_all = 0, t_comp = 0;
   KK_CUDA(cudaEventElapsedTime(&t_all, ev[0], ev[3]));
   KK_CUDA(cudaEventElapsedTime(&t_comp, ev[1], ev[2]));
@@ -1039,6 +1071,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   float* speed_d = upload(speed, B);
   times_compute_begin();
   const Dom dT{row_item_d, 0, 0, 0, LT};
+  cur_B = B;
   std::vector<int> tstart(B), tlen(B);
   for (int b = 0; b < B; b++) tstart[b] = items_h[b].tok_start, tlen[b] = items_h[b].tok_len;
   // ---- fused style projections (every AdaIN / AdaLN gamma|beta of the batch)
@@ -1122,7 +1155,8 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     KK_CUDA(cudaMemcpyAsync(dh, dur_d, sizeof(int) * LT, cudaMemcpyDeviceToHost, st));
     KK_CUDA(cudaMemcpyAsync(eh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
     KK_CUDA(cudaStreamSynchronize(st));
-    if (*eh) throw KKError(KK_ERR_TIMEOUT, "an LSTM step barrier timed out");
+    if (*eh) throw KKError(KK_ERR_TIMEOUT, *eh == 1 ? "an LSTM step barrier timed out"
+                                                    : "a tcgen05 convolution pipeline wait timed out");
     memcpy(dur_h.data(), dh, sizeof(int) * LT);
   }
   if (dur_out) {
@@ -1192,7 +1226,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   dump("nc", nc, 2LL * LN, 1, 1);
   stage_sync("f0n");
   // ---- text encoder (src/gpu_batch.rs:457-481) and alignment of its output (asr)
-  float* xcat0 = ar.get<float>((size_t)LN * 514);
+  float* xcat0 = ar.get<float>((size_t)LN * X0_LD);
   {
     auto mk = ar.mark();
     float* e = ar.get<float>((size_t)LT * 512);
@@ -1211,7 +1245,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     }
     float* t_en = nxt;
     lstm(m.te_lstm, cur, 512, LT, tstart, tlen, t_en, 512);
-    check(launch_gather_rows(t_en, 512, src_row_d, LN, 512, xcat0, 514, st), "gather_rows");
+    check(launch_gather_rows(t_en, 512, src_row_d, LN, 512, xcat0, X0_LD, st), "gather_rows");
     ar.rewind(mk);
   }
   stage_sync("text encoder");
@@ -1281,10 +1315,11 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
     noise_off_d = upload(off.data(), B);
   }
   times_compute_begin();
-  float* xcat0 = ar.get<float>((size_t)LN * 514);
+  cur_B = B;
+  float* xcat0 = ar.get<float>((size_t)LN * X0_LD);
   float* f0 = ar.get<float>((size_t)2 * LN);
   float* nc = ar.get<float>((size_t)2 * LN);
-  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, 514, st), "gather_rows");
+  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, X0_LD, st), "gather_rows");
   check(launch_gather_rows(f0c_d, 1, tab2_d, 2 * LN, 1, f0, 1, st), "gather_rows");
   check(launch_gather_rows(nc_d, 1, tab2_d, 2 * LN, 1, nc, 1, st), "gather_rows");
   const int wdec = m.fc_dec.cout;

@@ -447,6 +447,23 @@ cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, i
   return cudaGetLastError();
 }
 
+__global__ void adain_coef_kernel(const float* mean, const float* rstd, const float* nw, const float* nb,
+                                  const float* gb, int ldgb, int B, int C, float2* coef) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * C) return;
+  int b = i / C, c = i % C;
+  const float* g = gb + (long)b * ldgb;
+  float g1 = 1.0f + g[c];
+  float s = rstd[i] * nw[c];
+  coef[i] = make_float2(g1 * s, g1 * (nb[c] - mean[i] * s) + g[C + c]);
+}
+
+cudaError_t launch_adain_coef(const float* mean, const float* rstd, const float* nw, const float* nb, const float* gb,
+                              int ldgb, int B, int C, float2* coef, cudaStream_t st) {
+  adain_coef_kernel<<<nblk((long)B * C, 256), 256, 0, st>>>(mean, rstd, nw, nb, gb, ldgb, B, C, coef);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------ AdaIN + pool
 
 __device__ __forceinline__ float pool_in(const ConvArgs& p, const float* x, int L, int i, int c) {

@@ -69,6 +69,12 @@ cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, i
                          int plus1, int max_len, double* part, float* mean, float* rstd,
                          cudaStream_t st);
 
+// AdaIN folded into one affine map per (item, channel) for the bf16 tensor-core path:
+// coef[b][c] = (A, B) with AdaIN(x) = x * A + B, A = (1 + gamma) * rstd * nw,
+// B = (1 + gamma) * (nb - mean * rstd * nw) + beta.
+cudaError_t launch_adain_coef(const float* mean, const float* rstd, const float* nw, const float* nb,
+                              const float* gb, int ldgb, int B, int C, float2* coef, cudaStream_t st);
+
 // AdaIN + leaky ReLU (0.2) followed by the depthwise ConvTranspose1d(k3, s2, p1, op1) "pool"
 // (adain_apply_seg + dw_convT_k3s2, kernels/kokoro.cu:152-167, 317-334): x [L][C] -> y [2L][C]
 cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw,

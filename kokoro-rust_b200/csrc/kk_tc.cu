@@ -1,10 +1,739 @@
-// tcgen05 convolution: placeholder until the kernel lands; the BF16 mode falls back to nothing
-// here because tc_available() reports false (the engine then runs the fp32 kernels).
+// tcgen05 implicit-GEMM 1-D convolution (BF16 precision mode).
+//
+// GEMM view of one output tile: D[co, t] (TMEM, fp32, 128 lanes x 256 columns) =
+//   sum over input-channel blocks cb (64 channels) and taps k of
+//   A_k,cb[co, ci] (weights, bf16, K-major)  x  B_k,cb[t, ci] (activations, bf16, K-major)
+// issued as tcgen05.mma.cta_group::1.kind::f16 with M = 128, N = 256, K = 16.
+//
+// Operand staging (no tensor maps, no swizzle; canonical no-swizzle K-major layout of 8-row x
+// 16-byte core matrices):
+//  * weights: a load-time image of 16 KB blocks [co tile][cb][tap], each block laid out exactly as
+//    its shared-memory operand (LBO 2048 B between 8-channel chunks, SBO 128 B between 8-row
+//    groups), streamed with one cp.async.bulk per block into a 4-stage ring;
+//  * activations: 8 producer warps read the f32 input rows of the tile's window
+//    [t0 - pad, t0 + 256 + (K-1)*dil - pad), apply the layer's prologue (gap masking,
+//    AdaIN + leaky ReLU, AdaIN + Snake, leaky ReLU, nearest x2 upsample) and store bf16 in a
+//    time-contiguous layout: chunk j (8 channels) holds all window rows at 16 B per row. Because
+//    the rows of a chunk are contiguous, the B operand of tap k is the same window with its start
+//    address moved by k * dil rows: the window is staged once per channel block and reused by every
+//    tap (this is the implicit GEMM; no im2col, no per-tap reload).
+//  * accumulators: two 256-column TMEM buffers, so the epilogue (4 warps, tcgen05.ld 32x32b) of one
+//    tile overlaps the MMAs of the next; the epilogue applies bias / residual / shortcut / gelu and
+//    writes time-major f32 rows (32 lanes = 32 consecutive channels: coalesced 128-byte stores).
+//
+// Warp roles (14 warps): 0 weight loader + TMEM owner, 1 MMA issuer (one elected lane), 2-5
+// epilogue, 6-13 activation producers. Persistent CTAs walk the tiles in time-fastest order so
+// the CTAs running together share one co tile's weights in L2.
+//
+// Every mbarrier wait is bounded (1 s of %globaltimer): on expiry the CTA records the failure in
+// the engine's error flag, drains its own bulk copies (bounded), releases its TMEM and returns.
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include <string.h>
+#include <vector>
+
 #include "kk_tc.h"
 
 namespace kk {
-bool tc_available() { return false; }
-cudaError_t tc_make_weights(const float*, int, int, int, TcWeights*) { return cudaErrorNotSupported; }
-bool tc_supported(const ConvArgs&, const TcWeights&) { return false; }
-cudaError_t tc_conv(const ConvArgs&, const TcWeights&, cudaStream_t) { return cudaErrorNotSupported; }
+
+constexpr int TC_M = 128;
+constexpr int TC_N = 256;
+constexpr int TC_KB = 64;
+constexpr int TC_WST = 4;
+constexpr int TC_XST_MAX = 4;  // activation-window ring stages (3 when shared memory allows)
+constexpr int TC_MAX_WIN = 512;
+constexpr int TC_EC = 16;                       // epilogue chunk: 16 time rows x 128 channels
+constexpr int TC_EBUF = TC_EC * TC_M * 4;       // 8 KB staging buffer
+constexpr int TC_THREADS = 448;
+constexpr int TC_WBLOCK = TC_M * TC_KB * 2;  // 16 KB weight block
+constexpr unsigned long long TC_TIMEOUT_NS = 1000000000ull;
+
+// ------------------------------------------------------------------------------ PTX wrappers
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ unsigned long long tc_now() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ void mbar_init(uint64_t* b, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(b)), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* b) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(b)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* b, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(b)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and raises the CTA abort flag + engine error flag) on expiry.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
+  if (mbar_try(b, parity)) return true;
+  const unsigned long long t0 = tc_now();
+  while (true) {
+    if (mbar_try(b, parity)) return true;
+    if (*abort_flag) return false;
+    if (tc_now() - t0 > TC_TIMEOUT_NS) {
+      *abort_flag = 1;
+      atomicExch(err, 2);
+      return false;
+    }
+  }
+}
+// mbar_wait that adds the cycles it waited to *acc (when acc is not null).
+__device__ __forceinline__ bool mbar_wait_t(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                            unsigned long long* acc) {
+  if (!acc) return mbar_wait(b, parity, abort_flag, err);
+  const long long c0 = clock64();
+  const bool ok = mbar_wait(b, parity, abort_flag, err);
+  *acc += (unsigned long long)(clock64() - c0);
+  return ok;
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+      : "memory");
+}
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.tile.bulk_group [%0, {%1, %2}], [%3];" ::"l"(map), "r"(x),
+               "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_read1() { asm volatile("cp.async.bulk.wait_group.read 1;" ::: "memory"); }
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, no swizzle, K-major: start, LBO (between the two 8-element K
+// chunks of one MMA), SBO (between 8-row groups), version 1 (Blackwell).
+__device__ __forceinline__ uint64_t sdesc(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+  return (uint64_t)((addr >> 4) & 0x3FFF) | ((uint64_t)((lbo >> 4) & 0x3FFF) << 16) |
+         ((uint64_t)((sbo >> 4) & 0x3FFF) << 32) | (1ull << 46);
+}
+// Instruction descriptor, kind::f16: D f32, A bf16, B bf16, both K-major, M = 128, N = 256.
+constexpr uint32_t TC_IDESC = (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(TC_N >> 3) << 17) |
+                              ((uint32_t)(TC_M >> 4) << 24);
+
+__device__ __forceinline__ void mma_bf16(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(a), "l"(b), "r"(TC_IDESC), "r"(accumulate)
+      : "memory");
+}
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// ------------------------------------------------------------------------------ kernel
+
+struct TcArgs {
+  CUtensorMap ymap;   // output rows [L_out][cout] f32 (row stride ldy), box 128 channels x 16 rows
+  CUtensorMap rmap;   // residual rows (y for OUT_ADD, sc for OUT_PLUS), same box
+  int tma_out;        // 1: epilogue writes through shared memory + TMA (16-byte aligned row stride)
+  ConvArgs a;
+  const __nv_bfloat16* wimg;
+  int ncb;        // input-channel blocks of 64
+  int n_cot;      // output-channel tiles of 128
+  int n_tt;       // time tiles of 256
+  int win_rows;   // 256 + (K - 1) * dil
+  int win_pad;    // window rows rounded to 8, + 1 (bank-conflict-free producer stores)
+  int xst;        // activation-window ring stages
+  int* err;
+  unsigned long long* trace;  // optional cycle accounting of CTA 0 (diagnostics), 16 counters
+};
+
+// Cycle accounting (CTA 0, when p.trace is set): slot indices.
+enum TcTrace : int {
+  TR_MMA_WAIT_ACC = 0, TR_MMA_WAIT_X = 1, TR_MMA_WAIT_W = 2, TR_MMA_TOTAL = 3,
+  TR_LD_WAIT_W = 4, TR_LD_TOTAL = 5,
+  TR_PR_WAIT_X = 6, TR_PR_WORK = 7, TR_PR_ITEM = 8,
+  TR_EP_WAIT = 9, TR_EP_WORK = 10, TR_TILES = 11
+};
+
+__global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_constant__ TcArgs p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  const ConvArgs& a = p.a;
+  uint8_t* wbuf = smem;                                       // TC_WST x 16 KB
+  const uint32_t xbytes = 8u * p.win_pad * 16u;
+  const int XST = p.xst;
+  uint8_t* xbuf = smem + TC_WST * TC_WBLOCK;                  // XST x xbytes
+  float* stage = (float*)(xbuf + XST * xbytes);               // 2 x 8 KB epilogue staging
+  float* resb = stage + 2 * TC_EC * TC_M;                     // 2 x 8 KB residual chunks
+  uint64_t* bars = (uint64_t*)(resb + 2 * TC_EC * TC_M);
+  uint64_t* w_full = bars;
+  uint64_t* w_empty = bars + TC_WST;
+  uint64_t* x_full = bars + 2 * TC_WST;
+  uint64_t* x_empty = x_full + TC_XST_MAX;
+  uint64_t* acc_full = x_empty + TC_XST_MAX;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* res_full = acc_empty + 2;
+  uint32_t* tmem_slot = (uint32_t*)(res_full + 2);
+  volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
+  int* ritem = (int*)(tmem_slot + 4);                         // item of each window row (producers)
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ntiles = p.n_cot * p.n_tt;
+  const int K = a.K;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < TC_WST; i++) {
+      mbar_init(&w_full[i], 1);
+      mbar_init(&w_empty[i], 1);
+    }
+    for (int i = 0; i < XST; i++) {
+      mbar_init(&x_full[i], 8);
+      mbar_init(&x_empty[i], 1);
+    }
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&acc_full[i], 1);
+      mbar_init(&acc_empty[i], 4);
+      mbar_init(&res_full[i], 1);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 512;" ::"r"(smem_u32(tmem_slot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- weight loader
+    if (lane == 0) {
+      unsigned long long tw = 0;
+      unsigned long long* tr = (p.trace && blockIdx.x == 0) ? &tw : nullptr;
+      const long long t_start = clock64();
+      uint32_t it = 0;
+      for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
+        const int cot = tile / p.n_tt;
+        const uint8_t* src = (const uint8_t*)p.wimg + (size_t)cot * p.ncb * K * TC_WBLOCK;
+        for (int s = 0; s < p.ncb * K; s++, it++) {
+          const int st = it % TC_WST;
+          if (!mbar_wait_t(&w_empty[st], ((it / TC_WST) & 1) ^ 1, abort_flag, p.err, tr)) break;
+          mbar_arrive_expect_tx(&w_full[st], TC_WBLOCK);
+          bulk_g2s(wbuf + st * TC_WBLOCK, src + (size_t)s * TC_WBLOCK, TC_WBLOCK, &w_full[st]);
+        }
+      }
+      if (tr) {
+        p.trace[TR_LD_WAIT_W] = tw;
+        p.trace[TR_LD_TOTAL] = (unsigned long long)(clock64() - t_start);
+      }
+      if (*abort_flag) {
+        // drain this CTA's bulk copies still in flight before the shared memory is released
+        const uint32_t first = it > TC_WST ? it - TC_WST : 0;
+        for (uint32_t j = first; j < it; j++) {
+          const unsigned long long t0 = tc_now();
+          while (!mbar_try(&w_full[j % TC_WST], (j / TC_WST) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      unsigned long long twa = 0, twx = 0, tww = 0;
+      const bool trc = p.trace && blockIdx.x == 0;
+      const long long t_start = clock64();
+      uint32_t wit = 0, xit = 0, lt = 0;
+      for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
+        const int ab = lt & 1;
+        if (!mbar_wait_t(&acc_empty[ab], ((lt >> 1) & 1) ^ 1, abort_flag, p.err, trc ? &twa : nullptr)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + ab * TC_N;
+        bool ok = true;
+        for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
+          const int xs = xit % XST;
+          if (!mbar_wait_t(&x_full[xs], (xit / XST) & 1, abort_flag, p.err, trc ? &twx : nullptr)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t xb = smem_u32(xbuf + xs * xbytes);
+          for (int k = 0; k < K; k++, wit++) {
+            const int ws = wit % TC_WST;
+            if (!mbar_wait_t(&w_full[ws], (wit / TC_WST) & 1, abort_flag, p.err, trc ? &tww : nullptr)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t wb = smem_u32(wbuf + ws * TC_WBLOCK);
+#pragma unroll
+            for (int kk = 0; kk < 4; kk++) {
+              const uint64_t ad = sdesc(wb + kk * 2 * 2048, 2048, 128);
+              const uint64_t bd = sdesc(xb + (uint32_t)(k * a.dil) * 16u + kk * 2 * 16u * p.win_pad,
+                                        16u * p.win_pad, 128);
+              mma_bf16(d, ad, bd, (cb | k | kk) != 0);
+            }
+            mma_commit(&w_empty[ws]);
+          }
+          if (ok) mma_commit(&x_empty[xs]);
+        }
+        if (!ok) break;
+        mma_commit(&acc_full[ab]);
+      }
+      if (trc) {
+        p.trace[TR_MMA_WAIT_ACC] = twa;
+        p.trace[TR_MMA_WAIT_X] = twx;
+        p.trace[TR_MMA_WAIT_W] = tww;
+        p.trace[TR_MMA_TOTAL] = (unsigned long long)(clock64() - t_start);
+        p.trace[TR_TILES] = lt;
+      }
+    }
+  } else if (warp < 6) {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const bool trc = p.trace && blockIdx.x == 0 && warp == 2 && lane == 0;
+    unsigned long long tew = 0;
+    uint32_t rcount = 0;   // residual chunks consumed (buffer / parity of res_full)
+    uint32_t rissued = 0;  // residual chunk loads issued (lead thread)
+    const long long t_start = clock64();
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
+      const int ab = lt & 1;
+      if (!mbar_wait_t(&acc_full[ab], (lt >> 1) & 1, abort_flag, p.err, trc ? &tew : nullptr)) break;
+      tc_fence_after();
+      const int cot = tile / p.n_tt, tt = tile % p.n_tt;
+      const int co = cot * TC_M + q * 32 + lane;
+      const int t0 = tt * TC_N;
+      const bool co_ok = co < a.cout;
+      const float bias = (co_ok && a.bias) ? a.bias[co] : 0.0f;
+      const int out_mode = a.out_mode, L_out = a.L_out;
+      const long ldy = a.ldy;
+      float* __restrict__ y = a.y;
+      const float oscale = a.oscale;
+      const bool need_res = out_mode == OUT_ADD || out_mode == OUT_PLUS;
+      if (p.tma_out) {
+        // 16 chunks of 16 rows: TMEM -> registers -> (+bias, residual from a TMA-loaded chunk,
+        // gelu) -> shared staging -> one TMA tensor store per chunk (rows / channels past the
+        // output are clipped by the tensor bounds).
+        const bool lead = (warp == 2 && lane == 0);
+        const int ep = q * 32 + lane;  // channel within the tile = this thread's TMEM lane
+        if (need_res && lead) {
+          const int rb = rcount & 1;
+          mbar_arrive_expect_tx(&res_full[rb], TC_EBUF);
+          tma_load_2d(resb + rb * TC_EC * TC_M, &p.rmap, cot * TC_M, t0, &res_full[rb]);
+          rissued = rcount + 1;
+        }
+        for (int c = 0; c < TC_N / TC_EC; c++) {
+          if (need_res && lead && c + 1 < TC_N / TC_EC) {
+            const int rb = (rcount + 1) & 1;
+            mbar_arrive_expect_tx(&res_full[rb], TC_EBUF);
+            tma_load_2d(resb + rb * TC_EC * TC_M, &p.rmap, cot * TC_M, t0 + (c + 1) * TC_EC, &res_full[rb]);
+            rissued = rcount + 2;
+          }
+          float v[TC_EC];
+          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + c * TC_EC, v);
+          if (c == TC_N / TC_EC - 1) {
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&acc_empty[ab]);  // accumulator fully read
+          }
+          const float* rr = resb;
+          if (need_res) {
+            const int rb = rcount & 1;
+            mbar_wait(&res_full[rb], (rcount >> 1) & 1, abort_flag, p.err);  // failure -> abort flag
+            rr = resb + rb * TC_EC * TC_M;
+            rcount++;
+          }
+          float* sb = stage + (c & 1) * TC_EC * TC_M;
+          if (lead) bulk_wait_read1();  // the store issued two chunks ago has read this buffer
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          if (*abort_flag) break;  // uniform: every epilogue thread sees the flag after the barrier
+#pragma unroll
+          for (int jj = 0; jj < TC_EC; jj++) {
+            float r = v[jj] + bias;
+            if (out_mode == OUT_ADD) r = rr[jj * TC_M + ep] + r;
+            else if (out_mode == OUT_PLUS) r = (r + rr[jj * TC_M + ep]) * oscale;
+            else if (out_mode == OUT_GELU) r = gelu_new(r);
+            sb[jj * TC_M + ep] = r;
+          }
+          fence_proxy_async();
+          asm volatile("bar.sync 2, 128;" ::: "memory");
+          if (lead) {
+            tma_store_2d(&p.ymap, cot * TC_M, t0 + c * TC_EC, sb);
+            bulk_commit();
+          }
+        }
+        continue;
+      }
+      const bool need_res_d = co_ok && need_res;
+      const float* __restrict__ rsrc = out_mode == OUT_ADD ? a.y : a.sc;
+      const long rld = out_mode == OUT_ADD ? a.ldy : a.ldsc;
+      // residual operands are software-pipelined one 32-column chunk ahead
+      float res[32];
+#pragma unroll
+      for (int jj = 0; jj < 32; jj++) {
+        const int t = t0 + jj;
+        res[jj] = (need_res_d && t < L_out) ? rsrc[(long)t * rld + co] : 0.0f;
+      }
+      for (int c0 = 0; c0 < TC_N; c0 += 32) {
+        float v[32];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + c0, v);
+#pragma unroll
+        for (int jj = 0; jj < 32; jj++) {
+          float r = v[jj] + bias;
+          if (out_mode == OUT_ADD) r = res[jj] + r;
+          else if (out_mode == OUT_PLUS) r = (r + res[jj]) * oscale;
+          else if (out_mode == OUT_GELU) r = gelu_new(r);
+          v[jj] = r;
+        }
+        if (c0 + 32 < TC_N) {
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++) {
+            const int t = t0 + c0 + 32 + jj;
+            res[jj] = (need_res_d && t < L_out) ? rsrc[(long)t * rld + co] : 0.0f;
+          }
+        }
+        if (co_ok) {
+          float* __restrict__ yp = y + (long)(t0 + c0) * ldy + co;
+#pragma unroll
+          for (int jj = 0; jj < 32; jj++)
+            if (t0 + c0 + jj < L_out) yp[(long)jj * ldy] = v[jj];
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[ab]);
+    }
+    if (p.tma_out && warp == 2 && lane == 0) {
+      for (uint32_t k = rcount; k < rissued; k++) {  // residual loads still in flight (abort path)
+        const unsigned long long t0 = tc_now();
+        while (!mbar_try(&res_full[k & 1], (k >> 1) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+        }
+      }
+      bulk_wait_all();  // stores complete before exit
+    }
+    if (trc) {
+      p.trace[TR_EP_WAIT] = tew;
+      p.trace[TR_EP_WORK] = (unsigned long long)(clock64() - t_start) - tew;
+    }
+  } else {
+    // ---------------------------------------------------------------- activation producers
+    // At each tile the producers first resolve the item of every window row into shared memory
+    // (one lookup per row, shared by all channel blocks). Thread (row lane rl = ptid / 8, chunk
+    // j = ptid % 8) then converts 8 channels of rows rl, rl + 32, ...: four rows are loaded
+    // before any is used, and the item's AdaIN coefficients stay in registers until it changes.
+    const int ptid = threadIdx.x - 6 * 32;  // 0..255
+    const int j = ptid & 7, rl = ptid >> 3;
+    const float* __restrict__ xg = a.x;
+    const long ldx = a.ldx;
+    const int cin = a.cin, L_in = a.L_in, up2 = a.in_up2, win_rows = p.win_rows;
+    const float2* __restrict__ coef = a.coef;
+    const float slope = a.slope;
+    const bool vec_ok = (ldx % 4 == 0) && ((((uintptr_t)xg) & 15) == 0);
+    const bool affine = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE;
+    const bool snake = a.in_mode == IN_ADAIN_SNAKE;
+    const bool leaky_on = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_LEAKY_MASK;
+    uint32_t xit = 0;
+    const bool trc = p.trace && blockIdx.x == 0 && ptid == 0;
+    unsigned long long tpw = 0, tpi = 0;
+    const long long t_start = clock64();
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
+      const int tt = tile % p.n_tt;
+      const int base = tt * TC_N - a.pad;
+      const long long ti0 = clock64();
+      asm volatile("bar.sync 1, 256;" ::: "memory");  // previous tile's windows are all written
+      for (int r = ptid; r < win_rows; r += 256) {
+        const int g = base + r;
+        ritem[r] = (g < 0 || g >= L_in) ? -1 : (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, g));
+      }
+      asm volatile("bar.sync 1, 256;" ::: "memory");
+      if (trc) tpi += (unsigned long long)(clock64() - ti0);
+      bool ok = true;
+      for (int cb = 0; cb < p.ncb; cb++, xit++) {
+        const int xs = xit % XST;
+        if (!mbar_wait_t(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
+          ok = false;
+          break;
+        }
+        uint8_t* xb = xbuf + xs * xbytes + (size_t)j * 16 * p.win_pad;
+        const int c0 = cb * TC_KB + j * 8;
+        const bool ch_ok = c0 < cin;
+        const int nch = ch_ok ? min(8, cin - c0) : 0;
+        float al[8], ial[8], ca[8], cbb[8];
+        int cached = -1;
+        if (snake) {
+#pragma unroll
+          for (int e = 0; e < 8; e++) {
+            al[e] = e < nch ? a.alpha[c0 + e] : 1.0f;
+            ial[e] = 1.0f / al[e];
+          }
+        }
+        for (int r = rl; r < win_rows; r += 128) {
+          float v[4][8];
+          int b[4];
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int rr = r + 32 * u;
+            b[u] = (rr < win_rows && ch_ok) ? ritem[rr] : -1;
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[u][e] = 0.0f;
+            if (b[u] >= 0) {
+              const int g = base + rr;
+              const float* src = xg + (long)(up2 ? (g >> 1) : g) * ldx + c0;
+              if (vec_ok && nch == 8) {
+                const float4 u0 = __ldg(reinterpret_cast<const float4*>(src));
+                const float4 u1 = __ldg(reinterpret_cast<const float4*>(src + 4));
+                v[u][0] = u0.x, v[u][1] = u0.y, v[u][2] = u0.z, v[u][3] = u0.w;
+                v[u][4] = u1.x, v[u][5] = u1.y, v[u][6] = u1.z, v[u][7] = u1.w;
+              } else {
+#pragma unroll
+                for (int e = 0; e < 8; e++)
+                  if (e < nch) v[u][e] = __ldg(src + e);
+              }
+            }
+          }
+#pragma unroll
+          for (int u = 0; u < 4; u++) {
+            const int rr = r + 32 * u;
+            if (rr >= win_rows) break;
+            if (b[u] >= 0) {
+              if (affine) {
+                if (b[u] != cached) {
+                  cached = b[u];
+#pragma unroll
+                  for (int e = 0; e < 8; e++) {
+                    const float2 q2 = e < nch ? coef[(long)cached * cin + c0 + e] : make_float2(0.0f, 0.0f);
+                    ca[e] = q2.x, cbb[e] = q2.y;
+                  }
+                }
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                  float t = fmaf(v[u][e], ca[e], cbb[e]);
+                  if (snake) {
+                    const float sn = __sinf(al[e] * t);
+                    t = fmaf(ial[e], sn * sn, t);
+                  } else {
+                    t = leaky(t, slope);
+                  }
+                  v[u][e] = t;
+                }
+              } else if (leaky_on) {
+#pragma unroll
+                for (int e = 0; e < 8; e++) v[u][e] = leaky(v[u][e], slope);
+              }
+            }
+            uint4 pk;
+            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[u][0], v[u][1]);
+            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[u][2], v[u][3]);
+            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[u][4], v[u][5]);
+            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[u][6], v[u][7]);
+            memcpy(&pk.x, &h0, 4);
+            memcpy(&pk.y, &h1, 4);
+            memcpy(&pk.z, &h2, 4);
+            memcpy(&pk.w, &h3, 4);
+            *reinterpret_cast<uint4*>(xb + (size_t)rr * 16) = pk;
+          }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&x_full[xs]);
+      }
+      if (!ok) break;
+    }
+    if (trc) {
+      p.trace[TR_PR_WAIT_X] = tpw;
+      p.trace[TR_PR_ITEM] = tpi;
+      p.trace[TR_PR_WORK] = (unsigned long long)(clock64() - t_start) - tpw - tpi;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 512;" ::"r"(tmem) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------------------ host side
+
+bool tc_available() {
+  int dev = 0, major = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return false;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return false;
+  return major == 10;
+}
+
+static inline uint16_t f2bf(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights* out) {
+  const int n_cot = (cout + TC_M - 1) / TC_M, ncb = (cin + TC_KB - 1) / TC_KB;
+  const size_t n = (size_t)n_cot * ncb * K * (TC_M * TC_KB);
+  std::vector<uint16_t> img(n, 0);
+  for (int cot = 0; cot < n_cot; cot++)
+    for (int cb = 0; cb < ncb; cb++)
+      for (int k = 0; k < K; k++) {
+        uint16_t* blk = img.data() + (((size_t)cot * ncb + cb) * K + k) * (TC_M * TC_KB);
+        for (int r = 0; r < TC_M; r++) {
+          const int co = cot * TC_M + r;
+          if (co >= cout) continue;
+          for (int c = 0; c < TC_KB; c++) {
+            const int ci = cb * TC_KB + c;
+            if (ci >= cin) continue;
+            // chunk j = c / 8 at 2048 B, row group r / 8 at 128 B, row r % 8 at 16 B, element c % 8
+            const size_t off = (size_t)(c >> 3) * 1024 + (size_t)(r >> 3) * 64 + (size_t)(r & 7) * 8 + (c & 7);
+            blk[off] = f2bf(w[((size_t)co * cin + ci) * K + k]);
+          }
+        }
+      }
+  void* d = nullptr;
+  cudaError_t e = cudaMalloc(&d, n * 2);
+  if (e != cudaSuccess) return e;
+  e = cudaMemcpy(d, img.data(), n * 2, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    cudaFree(d);
+    return e;
+  }
+  out->w = d;
+  out->bytes = n * 2;
+  out->cin = cin, out->cout = cout, out->K = K;
+  out->cin_pad = ncb * TC_KB, out->cout_pad = n_cot * TC_M;
+  return cudaSuccess;
+}
+
+bool tc_supported(const ConvArgs& a, const TcWeights& t) {
+  if (a.stride != 1 || a.K != t.K || a.cin != t.cin || a.cout != t.cout) return false;
+  if (a.L_out < 64) return false;  // tiny row counts (per-item style projections) stay on SIMT
+  if ((a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && !a.coef) return false;
+  if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
+  return true;
+}
+
+static size_t tc_smem(int win_pad, int xst) {
+  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + 4 * TC_EBUF +
+         (2 * TC_WST + 2 * TC_XST_MAX + 6) * 8 + 16 + TC_MAX_WIN * 4;
+}
+
+static int g_num_sms[64] = {0};
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)f;
+    else
+      cudaGetLastError();
+  }
+  return fn;
+}
+
+// f32 rows [rows][cols] with row stride ld floats; box = 128 columns x 16 rows, no swizzle.
+static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long cols, long ld) {
+  EncodeTiledFn fn = encode_fn();
+  if (!fn || (ld % 4) != 0 || (((uintptr_t)base) & 15) != 0 || rows <= 0 || cols <= 0) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint32_t box[2] = {(cuuint32_t)TC_M, (cuuint32_t)TC_EC};
+  cuuint32_t estr[2] = {1, 1};
+  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_t st, unsigned long long* trace) {
+  TcArgs p;
+  memset(&p, 0, sizeof(p));
+  p.trace = trace;
+  p.tma_out = make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy) ? 1 : 0;
+  if (p.tma_out && a.out_mode == OUT_ADD) p.tma_out = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy) ? 1 : 0;
+  if (p.tma_out && a.out_mode == OUT_PLUS) p.tma_out = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc) ? 1 : 0;
+  p.a = a;
+  p.wimg = (const __nv_bfloat16*)t.w;
+  p.ncb = t.cin_pad / TC_KB;
+  p.n_cot = t.cout_pad / TC_M;
+  p.n_tt = (a.L_out + TC_N - 1) / TC_N;
+  p.win_rows = TC_N + (a.K - 1) * a.dil;
+  p.win_pad = ((p.win_rows + 7) / 8) * 8 + 1;
+  p.err = err;
+  p.xst = 3;
+  while (p.xst > 2 && tc_smem(p.win_pad, p.xst) > 227 * 1024) p.xst--;
+  const size_t smem = tc_smem(p.win_pad, p.xst);
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 64 && g_num_sms[dev] == 0) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_num_sms[dev] = n;
+    cudaError_t e = cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
+    if (e != cudaSuccess) return e;
+  }
+  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  const int ntiles = p.n_cot * p.n_tt;
+  const int grid = ntiles < g_num_sms[dev < 64 ? dev : 0] ? ntiles : g_num_sms[dev < 64 ? dev : 0];
+  tc_conv_kernel<<<grid, TC_THREADS, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
 }  // namespace kk

@@ -20,7 +20,10 @@ bool tc_available();
 cudaError_t tc_make_weights(const float* w_torch, int cin, int cout, int K, TcWeights* out);
 // Whether this convolution shape / mode runs on the tcgen05 kernel.
 bool tc_supported(const ConvArgs& a, const TcWeights& t);
-// Launch the tcgen05 convolution (same semantics as launch_conv_simt).
-cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, cudaStream_t st);
+// Launch the tcgen05 convolution (same semantics as launch_conv_simt). `err` receives 2 if a
+// bounded pipeline wait expires.
+// `trace` (optional) receives cycle accounting of CTA 0 per pipeline role (16 counters).
+cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_t st,
+                    unsigned long long* trace = nullptr);
 
 }  // namespace kk
