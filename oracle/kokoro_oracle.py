@@ -149,27 +149,27 @@ TW_COS, TW_SIN = _twiddles()
 HANN = (0.5 - 0.5 * np.cos(2.0 * np.pi * np.arange(20) / 20.0)).astype(F32)  # src/gpu.rs:101
 
 
-def sinegen_har(f0c: np.ndarray, noise: np.ndarray, lw: np.ndarray, lb: float) -> np.ndarray:
-    """Harmonic source of one item (kernels/kokoro.cu:188-254, src/gpu_batch.rs:319-350).
+def _rad(f0c: np.ndarray, t: np.ndarray) -> np.ndarray:
+    """rad_h(t) = remainder(f0[nearest source of t] * (h + 1) / 24000, 1) (kernels/kokoro.cu:188-204)."""
+    L = f0c.shape[0]
+    near = F32(1.0 / UPSAMPLE)
+    hs = np.arange(HARMONICS, dtype=F32)[:, None] + F32(1.0)
+    src = np.minimum(np.floor(t.astype(F32) * near).astype(np.int64), L - 1)
+    a = ((f0c[src][None, :] * hs) / F32(24000.0)).astype(F32)
+    m = np.fmod(a, F32(1.0))
+    return np.where((m != 0) & (m < 0), m + F32(1.0), m).astype(F32)
 
-    f0c: F0 curve [L] (2N domain); noise: [S * 9] f32 draws (index t*9 + h); returns har [S]."""
+
+def sine_phase_pre(f0c: np.ndarray) -> np.ndarray:
+    """phase_pre [9, D]: linear downsample (x 1/300) of rad, f64 cumulative sum, * 2 pi * 300
+    (sine_phase_pre, kernels/kokoro.cu:206-226; FMA placement of the reference). rand_ini is
+    added by the reference only at sample 0, which this downsample never reads (real >= 149.5),
+    so it cannot change the result."""
     f0c = np.asarray(f0c, F32)
     L = f0c.shape[0]
     S = L * UPSAMPLE
     D = int(math.floor(S * (1.0 / UPSAMPLE)))
-    near = F32(1.0 / UPSAMPLE)
     down = F32(1.0 / (1.0 / UPSAMPLE))
-    up = F32(1.0 / UPSAMPLE)
-    hs = np.arange(HARMONICS, dtype=F32)[:, None] + F32(1.0)
-
-    def rad(t):
-        src = np.minimum(np.floor(t.astype(F32) * near).astype(np.int64), L - 1)
-        a = ((f0c[src][None, :] * hs) / F32(24000.0)).astype(F32)
-        m = np.fmod(a, F32(1.0))
-        return np.where((m != 0) & (m < 0), m + F32(1.0), m).astype(F32)
-
-    # phase_pre (sine_phase_pre): rand_ini is added only at sample 0, which this linear
-    # downsample never reads (real >= 149.5), so it cannot change the output.
     d = np.arange(D)
     real = fma32(down, d.astype(F32) + F32(0.5), F32(-0.5))
     real = np.maximum(real, F32(0.0))
@@ -177,11 +177,20 @@ def sinegen_har(f0c: np.ndarray, noise: np.ndarray, lw: np.ndarray, lb: float) -
     l1 = np.clip(real - i0.astype(F32), F32(0.0), F32(1.0)).astype(F32)
     i1 = np.where(i0 < S - 1, i0 + 1, i0)
     l0 = (F32(1.0) - l1).astype(F32)
-    v = fma32(rad(i0), l0[None, :], (rad(i1) * l1[None, :]).astype(F32))
+    v = fma32(_rad(f0c, i0), l0[None, :], (_rad(f0c, i1) * l1[None, :]).astype(F32))
     acc = np.cumsum(v.astype(np.float64), axis=1)
-    pp = ((acc.astype(F32) * F32(2.0)) * PI_F * F32(300.0)).astype(F32)  # [9, D]
+    return ((acc.astype(F32) * F32(2.0)) * PI_F * F32(300.0)).astype(F32)
 
-    # har_source
+
+def har_from_phase(f0c: np.ndarray, pp: np.ndarray, noise: np.ndarray, lw: np.ndarray, lb: float) -> np.ndarray:
+    """har[t] = tanh(sum_h lw_h (0.1 sin(phase(t, h)) uv + amp noise[t, h]) + lb), phase linearly
+    upsampled (x 300) from phase_pre (sine_har_source, kernels/kokoro.cu:228-254)."""
+    f0c = np.asarray(f0c, F32)
+    L = f0c.shape[0]
+    S = L * UPSAMPLE
+    D = pp.shape[1]
+    near = F32(1.0 / UPSAMPLE)
+    up = F32(1.0 / UPSAMPLE)
     t = np.arange(S)
     src = np.minimum(np.floor(t.astype(F32) * near).astype(np.int64), L - 1)
     f0 = f0c[src]
@@ -201,6 +210,14 @@ def sinegen_har(f0c: np.ndarray, noise: np.ndarray, lw: np.ndarray, lb: float) -
         vv = ((sine * uv).astype(F32) + (amp * nz[:, h]).astype(F32)).astype(F32)
         acc = (acc + (F32(lw[h]) * vv).astype(F32)).astype(F32)
     return np.tanh((acc + F32(lb)).astype(np.float64)).astype(F32)
+
+
+def sinegen_har(f0c: np.ndarray, noise: np.ndarray, lw: np.ndarray, lb: float) -> np.ndarray:
+    """Harmonic source of one item (kernels/kokoro.cu:188-254, src/gpu_batch.rs:319-350).
+
+    f0c: F0 curve [L] (2N domain); noise: [S * 9] f32 draws (index t*9 + h); returns har [S]."""
+    f0c = np.asarray(f0c, F32)
+    return har_from_phase(f0c, sine_phase_pre(f0c), noise, lw, lb)
 
 
 def stft20(x: np.ndarray) -> np.ndarray:
@@ -250,6 +267,45 @@ def istft20(post: np.ndarray) -> np.ndarray:
         env[HOP * f : HOP * f + 20] += w2
     j = np.arange(n_out) + 10
     return (acc[j] / env[j]).astype(F32)
+
+
+# ----------------------------------------------------------------------------- layer arithmetic
+
+def chan_stats(x: np.ndarray, eps: float = 1e-5):
+    """Per-channel mean / rstd over time of x [C, T]: biased variance, eps 1e-5, accumulated in
+    f64 (chan_stats_seg, kernels/kokoro.cu:776-810)."""
+    xn = np.asarray(x, F32).astype(np.float64)
+    mean = xn.mean(axis=1)
+    var = ((xn - mean[:, None]) ** 2).mean(axis=1)
+    return mean.astype(F32), (F32(1.0) / np.sqrt(var.astype(F32) + F32(eps))).astype(F32)
+
+
+def adain_apply(x, mean, rstd, nw, nb, gamma, beta, slope=None):
+    """(1 + gamma) * ((x - mean) * rstd * nw + nb) + beta, then optional leaky ReLU
+    (adain_apply_seg, kernels/kokoro.cu:317-334). x [C, T]; per-channel vectors."""
+    x = np.asarray(x, F32)
+    v = ((x - mean[:, None]) * rstd[:, None]).astype(F32)
+    v = ((F32(1.0) + gamma[:, None]) * (v * nw[:, None] + nb[:, None]) + beta[:, None]).astype(F32)
+    if slope is not None:
+        v = np.where(v < 0, v * F32(slope), v).astype(F32)
+    return v
+
+
+def lstm_dir(gx: torch.Tensor, whh: torch.Tensor, bhh: torch.Tensor, reverse: bool) -> torch.Tensor:
+    """One LSTM direction: gates = gx[t] + (W_hh h + b_hh), order i, f, g, o
+    (lstm_seq_batched, kernels/kokoro.cu:400-450). gx [T, 4H] already includes W_ih x + b_ih."""
+    T = gx.shape[0]
+    H = whh.shape[1]
+    h = torch.zeros(H)
+    c = torch.zeros(H)
+    out = torch.zeros(T, H)
+    for t in (range(T - 1, -1, -1) if reverse else range(T)):
+        g = gx[t] + (whh @ h + bhh)
+        i, f_, gg, o = g[:H], g[H:2 * H], g[2 * H:3 * H], g[3 * H:]
+        c = torch.sigmoid(f_) * c + torch.sigmoid(i) * torch.tanh(gg)
+        h = torch.sigmoid(o) * torch.tanh(c)
+        out[t] = h
+    return out
 
 
 # ----------------------------------------------------------------------------- model
@@ -322,24 +378,10 @@ class KokoroOracle:
 
     # -- LSTM (kernels/kokoro.cu:400-450; torch gate order i, f, g, o)
     def bilstm(self, x, prefix):
-        T = x.shape[0]
         outs = []
         for sfx, rev in (("", False), ("_reverse", True)):
             gx = x @ self.t(f"{prefix}.weight_ih_l0{sfx}").T + self.t(f"{prefix}.bias_ih_l0{sfx}")
-            whh = self.t(f"{prefix}.weight_hh_l0{sfx}")
-            bhh = self.t(f"{prefix}.bias_hh_l0{sfx}")
-            H = whh.shape[1]
-            h = torch.zeros(H)
-            c = torch.zeros(H)
-            out = torch.zeros(T, H)
-            order = range(T - 1, -1, -1) if rev else range(T)
-            for t in order:
-                g = gx[t] + (whh @ h + bhh)
-                i, f_, gg, o = g[:H], g[H:2 * H], g[2 * H:3 * H], g[3 * H:]
-                c = torch.sigmoid(f_) * c + torch.sigmoid(i) * torch.tanh(gg)
-                h = torch.sigmoid(o) * torch.tanh(c)
-                out[t] = h
-            outs.append(out)
+            outs.append(lstm_dir(gx, self.t(f"{prefix}.weight_hh_l0{sfx}"), self.t(f"{prefix}.bias_hh_l0{sfx}"), rev))
         return torch.cat(outs, dim=1)
 
     # -- AdaIN family (kernels/kokoro.cu:776-810, 317-334)

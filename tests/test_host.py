@@ -1,0 +1,96 @@
+"""Host-side scheduling mirror of the reference engine (src/engine.rs:46-241)."""
+import numpy as np
+import pytest
+
+
+def ref_plan(lens, max_ph, max_items):
+    """Restatement of plan_batches (src/engine.rs:165-183) used as the expected answer."""
+    order = sorted(range(len(lens)), key=lambda i: (lens[i], i))
+    out, cur, s = [], [], 0
+    for i in order:
+        if cur and (len(cur) >= max_items or s + lens[i] > max_ph):
+            out.append(cur)
+            cur, s = [], 0
+        s += lens[i]
+        cur.append(i)
+    return out + ([cur] if cur else [])
+
+
+def test_plan_batches_budget_and_order(kk):
+    rng = np.random.default_rng(0)
+    lens = list(rng.integers(2, 512, 300))
+    p = kk.BatchPolicy(max_phonemes=4000, max_items=64)
+    plan = kk.plan_batches(lens, p)
+    assert plan == ref_plan(lens, 4000, 64)
+    assert sorted(i for b in plan for i in b) == list(range(300))
+    for b in plan:
+        assert len(b) <= 64 and (len(b) == 1 or sum(lens[i] for i in b) <= 4000)
+    flat = [lens[i] for b in plan for i in b]
+    assert flat == sorted(flat)
+    assert kk.plan_batches([], p) == []
+    assert kk.plan_batches([9999], p) == [[0]]  # oversize single item still gets a batch
+
+
+class FakeGpu:
+    """Fails any batch larger than `limit` with OOM (the split-in-half trigger)."""
+
+    def __init__(self, kk, limit):
+        self.kk, self.limit, self.calls = kk, limit, []
+
+    def forward_batch(self, items):
+        self.calls.append(len(items))
+        if len(items) > self.limit:
+            raise self.kk.KokoroError(2, "device arena: cannot allocate")
+        return [self.kk.Output(np.full(600 * len(it.ids), float(len(it.ids)), np.float32),
+                               np.full(len(it.ids), 1, np.int64)) for it in items]
+
+
+def make_engine(kk, limit):
+    e = kk.Engine.__new__(kk.Engine)
+    e.gpu = FakeGpu(kk, limit)
+    e.voices = {}
+    e.add_voice("v", np.arange(510 * 256, dtype=np.float32).reshape(510, 256))
+    return e
+
+
+def test_synth_batch_splits_in_half_and_keeps_order(kk):
+    e = make_engine(kk, limit=3)
+    rng = np.random.default_rng(1)
+    reqs = [(list(rng.integers(1, 178, n)), i) for i, n in enumerate(rng.integers(1, 60, 17))]
+    reqs[4] = ([], 4)                  # empty -> per-item error
+    reqs[9] = (list(range(1, 600)), 9)  # oversize -> per-item error
+    res = e.synth_batch(reqs, "v", 1.0, kk.BatchPolicy(max_phonemes=10_000, max_items=64))
+    assert len(res) == 17
+    for i, r in enumerate(res):
+        if i in (4, 9):
+            assert isinstance(r, Exception)
+        else:
+            n_ids = len(reqs[i][0]) + 2
+            assert r.audio.shape == (600 * n_ids,) and r.audio[0] == n_ids  # its own output
+    # split-in-half order of src/engine.rs:229-234: a failing batch is replaced by its halves,
+    # first half first
+    expect, stack = [], [15]
+    while stack:
+        n = stack.pop()
+        expect.append(n)
+        if n > 3:
+            stack += [n - n // 2, n // 2]
+    assert e.gpu.calls == expect
+
+
+def test_single_item_failure_is_reported(kk):
+    e = make_engine(kk, limit=0)
+    res = e.synth_batch([([1, 2, 3], 0), ([4, 5], 1)], "v")
+    assert all(isinstance(r, kk.KokoroError) for r in res)
+
+
+def test_voice_rules(kk):
+    e = make_engine(kk, limit=10)
+    v = e.voice("v")
+    assert np.array_equal(v.ref_s(1), v.pack[0]) and np.array_equal(v.ref_s(510), v.pack[509])
+    with pytest.raises(ValueError):
+        v.ref_s(0)
+    with pytest.raises(ValueError):
+        v.ref_s(511)
+    e.add_voice("w", np.zeros((510, 256), np.float32))
+    assert np.allclose(e.voice("v,w").pack, v.pack / 2)
