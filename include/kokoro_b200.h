@@ -113,6 +113,32 @@ KK_API kk_status kk_decode_batch(kk_engine* e, int n_items, const int32_t* n_fra
                           const float* f0, const float* n, const float* s_dec,
                           const uint64_t* seeds, const float* noise, float* audio_out);
 
+/*
+ * kk_decode_batch_noalloc -- kk_decode_batch for callers that cannot allocate device memory.
+ * No counterpart in the reference crate.
+ *
+ * Who needs it: a caller that vocodes short chunks from a latency-bound thread (a streaming
+ * audio callback cannot wait on cudaMalloc, which may synchronise the whole device and take
+ * milliseconds) and a caller that shares a GPU under a fixed memory budget (the engine's arena
+ * would otherwise grow to fit a new batch shape). This entry point allocates nothing: no device
+ * memory, no pinned host memory, no events. Its scratch is one static device array of 64 MiB that
+ * every GPU loading this library holds until the process exits; inputs are copied from, and the
+ * audio written straight to, the caller's host buffers (synchronously).
+ *
+ * Limits: at most 8 items and 120 N-frames per call, counting 2 gap frames per item (one item
+ * of up to 118 frames, about 2.95 s of audio); larger calls return KK_ERR_INVALID_ARG before any
+ * work. audio_out must hold sum(600 * N_b) floats. Arguments and results otherwise as
+ * kk_decode_batch.
+ *
+ * The first call on a device looks up the array's device address (once per device, with that
+ * device current); make that first call before any stream capture. All calls on a device share
+ * the array and it keeps the last call's contents: calls whose GPU work overlaps (two threads or
+ * two engines on one device) race on it and must be serialised by the caller.
+ */
+KK_API kk_status kk_decode_batch_noalloc(kk_engine* e, int n_items, const int32_t* n_frames, const float* asr,
+                                         const float* f0, const float* n, const float* s_dec,
+                                         const uint64_t* seeds, const float* noise, float* audio_out);
+
 /* Options (benchmark / diagnostics). */
 typedef enum {
   KK_OPT_KEEP_AUDIO_ON_DEVICE = 1, /* 1: forward leaves audio on the device (no D2H) */

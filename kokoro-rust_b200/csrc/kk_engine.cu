@@ -48,9 +48,24 @@ class Arena {
     blocks_.clear();
     cur_ = 0;
   }
+  // External-block mode: allocations are carved from one caller-provided device block and never
+  // reach cudaMalloc; exhausting the block throws. Only kk_decode_batch_noalloc uses it.
+  void set_external(void* base, size_t cap) {
+    ext_base_ = static_cast<char*>(base);
+    ext_cap_ = cap;
+    ext_used_ = 0;
+  }
+  void clear_external() { ext_base_ = nullptr; }
   void* alloc(size_t bytes) {
     bytes = (bytes + 255) & ~size_t(255);
     if (bytes == 0) bytes = 256;
+    if (ext_base_) {
+      if (ext_used_ + bytes > ext_cap_)
+        throw KKError(KK_ERR_INVALID_ARG, "static scratch exhausted (batch above the no-allocation limit)");
+      void* p = ext_base_ + ext_used_;
+      ext_used_ += bytes;
+      return p;
+    }
     while (cur_ < blocks_.size()) {
       Block& b = blocks_[cur_];
       if (b.used + bytes <= b.cap) {
@@ -84,8 +99,15 @@ class Arena {
   struct Mark {
     size_t blk, used;
   };
-  Mark mark() const { return {cur_, cur_ < blocks_.size() ? blocks_[cur_].used : 0}; }
+  Mark mark() const {
+    if (ext_base_) return {~size_t(0), ext_used_};
+    return {cur_, cur_ < blocks_.size() ? blocks_[cur_].used : 0};
+  }
   void rewind(Mark m) {
+    if (ext_base_) {
+      ext_used_ = m.used;
+      return;
+    }
     for (size_t i = m.blk + 1; i < blocks_.size(); i++) blocks_[i].used = 0;
     if (m.blk < blocks_.size()) blocks_[m.blk].used = m.used;
     cur_ = m.blk;
@@ -107,6 +129,8 @@ class Arena {
   };
   std::vector<Block> blocks_;
   size_t cur_ = 0;
+  char* ext_base_ = nullptr;
+  size_t ext_cap_ = 0, ext_used_ = 0;
 };
 
 // Pinned host staging for the uploads and downloads of one call (reset per call).
@@ -231,6 +255,7 @@ struct Engine {
   long long launches = 0;
   int* err_flag = nullptr;
   bool tc_ok = false;
+  bool noalloc_active = false;  // inside kk_decode_batch_noalloc: no events, no pinned staging
   const char* tc_trace_dir = getenv("KK_TC_TRACE_DIR");  // diagnostics: per-launch pipeline cycle accounting
   int cur_B = 0;  // items of the batch being run
   // timing: events on the engine stream (begin, compute begin, compute end, end)
@@ -300,12 +325,17 @@ struct Engine {
   float* decode_core(int B, const std::vector<ItemTab>& items_h, const ItemTab* items, const int* col_item_n, int LN,
                      float* xcat0, float* f0, float* nc, const float* gb_dec, int ldgb, const uint64_t* seeds_d,
                      const float* noise_d, const long long* noise_off_d);
+  float* decode_core(int B, int max_n, const ItemTab* items, const int* col_item_n, int LN, float* xcat0, float* f0,
+                     float* nc, const float* gb_dec, int ldgb, const uint64_t* seeds_d, const float* noise_d,
+                     const long long* noise_off_d);
   void finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h);
   void forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
                const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
                int64_t* nsamp_out);
   void decode(int B, const int32_t* n_frames, const float* asr, const float* f0, const float* n, const float* s_dec,
               const uint64_t* seeds, const float* noise, float* audio_out);
+  void decode_noalloc(int B, const int32_t* n_frames, const float* asr, const float* f0, const float* n,
+                      const float* s_dec, const uint64_t* seeds, const float* noise, float* audio_out);
 };
 
 Engine::~Engine() {
@@ -341,7 +371,7 @@ int Engine::prof_class(const char* name) {
 
 void Engine::prof_begin(cudaEvent_t* a) {
   *a = nullptr;
-  if (!profile) return;
+  if (!profile || noalloc_active) return;
   *a = pool_event();
   KK_CUDA(cudaEventRecord(*a, st));
 }
@@ -372,8 +402,14 @@ void Engine::times_begin() {
     if (!e) KK_CUDA(cudaEventCreate(&e));
   KK_CUDA(cudaEventRecord(ev[0], st));
 }
-void Engine::times_compute_begin() { KK_CUDA(cudaEventRecord(ev[1], st)); }
-void Engine::times_compute_end() { KK_CUDA(cudaEventRecord(ev[2], st)); }
+void Engine::times_compute_begin() {
+  if (noalloc_active) return;
+  KK_CUDA(cudaEventRecord(ev[1], st));
+}
+void Engine::times_compute_end() {
+  if (noalloc_active) return;
+  KK_CUDA(cudaEventRecord(ev[2], st));
+}
 
 float* Engine::up(const std::vector<float>& v) {
   float* p = nullptr;
@@ -854,6 +890,12 @@ float* Engine::decode_core(int B, const std::vector<ItemTab>& items_h, const Ite
                            const uint64_t* seeds_d, const float* noise_d, const long long* noise_off_d) {
   int max_n = 0;
   for (auto& it : items_h) max_n = std::max(max_n, it.n);
+  return decode_core(B, max_n, items, col_item_n, LN, xcat0, f0, nc, gb_dec, ldgb, seeds_d, noise_d, noise_off_d);
+}
+
+float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* col_item_n, int LN, float* xcat0,
+                           float* f0, float* nc, const float* gb_dec, int ldgb, const uint64_t* seeds_d,
+                           const float* noise_d, const long long* noise_off_d) {
   const Dom dN{col_item_n, LN, 1, 0, LN};
   const Dom d2{col_item_n, LN, 2, 0, 2 * LN};
   const Dom d20{col_item_n, LN, 20, 0, 20 * LN};
@@ -1337,6 +1379,113 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
   }
 }
 
+// ------------------------------------------------------------------------------ no-allocation decode
+
+// Scratch of kk_decode_batch_noalloc: one static device array per GPU that loads this library
+// (held until the process exits). Every call on a device shares it.
+constexpr size_t NOALLOC_SCRATCH_BYTES = size_t(64) << 20;
+constexpr int NOALLOC_MAX_ITEMS = 8;
+constexpr int NOALLOC_MAX_FRAMES = 120;  // N-domain frames of a call, 2 gap frames per item included
+static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
+// Device address of g_noalloc_scratch on the current device, looked up once per device (the
+// host-side symbol is only a stand-in and must never be handed to a kernel).
+static void* noalloc_scratch(int dev) {
+  static void* addr[64] = {};
+  if (dev < 0 || dev >= 64) throw KKError(KK_ERR_INVALID_ARG, "device ordinal above 63");
+  if (!addr[dev]) {
+    void* p = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    addr[dev] = p;
+  }
+  return addr[dev];
+}
+
+void Engine::decode_noalloc(int B, const int32_t* n_frames, const float* asr, const float* f0_in, const float* n_in,
+                            const float* s_dec, const uint64_t* seeds, const float* noise, float* audio_out) {
+  KK_REQUIRE(B > 0, "empty batch");
+  KK_REQUIRE(B <= NOALLOC_MAX_ITEMS, "kk_decode_batch_noalloc: more than 8 items in one call");
+  KK_REQUIRE(n_frames && asr && f0_in && n_in && s_dec && audio_out, "null input or output pointer");
+  ItemTab items_a[NOALLOC_MAX_ITEMS];
+  int LN = 0, max_n = 0;
+  long long tot = 0;
+  for (int b = 0; b < B; b++) {
+    KK_REQUIRE(n_frames[b] >= 1, "frame count out of range");
+    KK_REQUIRE(n_frames[b] <= NOALLOC_MAX_FRAMES - GAP_N && LN + n_frames[b] + GAP_N <= NOALLOC_MAX_FRAMES,
+               "kk_decode_batch_noalloc: more than 120 frames in one call (2 gap frames per item included)");
+    items_a[b] = {0, 0, LN, n_frames[b]};
+    LN += n_frames[b] + GAP_N;
+    tot += n_frames[b];
+    max_n = std::max(max_n, n_frames[b]);
+  }
+  KK_CUDA(cudaSetDevice(dev));
+  struct Guard {  // leave the engine's normal (allocating) mode however the call ends
+    Engine* e;
+    ~Guard() {
+      e->ar.clear_external();
+      e->noalloc_active = false;
+    }
+  } guard{this};
+  ar.set_external(noalloc_scratch(dev), NOALLOC_SCRATCH_BYTES);
+  noalloc_active = true;
+  KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
+  int col_item[NOALLOC_MAX_FRAMES], tab1[NOALLOC_MAX_FRAMES], tab2[2 * NOALLOC_MAX_FRAMES];
+  for (int i = 0; i < LN; i++) col_item[i] = tab1[i] = -1;
+  for (int i = 0; i < 2 * LN; i++) tab2[i] = -1;
+  long long r = 0;
+  for (int b = 0; b < B; b++) {
+    for (int i = 0; i < items_a[b].n; i++) {
+      col_item[items_a[b].a + i] = b;
+      tab1[items_a[b].a + i] = (int)(r + i);
+    }
+    for (int i = 0; i < 2 * items_a[b].n; i++) tab2[2 * items_a[b].a + i] = (int)(2 * r + i);
+    r += items_a[b].n;
+  }
+  // synchronous copies straight from the caller's (pageable) buffers: no pinned staging
+  auto put = [&](const void* h, size_t bytes) -> void* {
+    void* d = ar.alloc(bytes);
+    if (bytes) KK_CUDA(cudaMemcpyAsync(d, h, bytes, cudaMemcpyHostToDevice, st));
+    return d;
+  };
+  long long noise_off[NOALLOC_MAX_ITEMS];
+  long long nz = 0;
+  for (int b = 0; b < B; b++) noise_off[b] = nz, nz += 600LL * 9 * items_a[b].n;
+  ItemTab* items_d = (ItemTab*)put(items_a, sizeof(ItemTab) * B);
+  int* col_item_d = (int*)put(col_item, sizeof(int) * LN);
+  int* tab1_d = (int*)put(tab1, sizeof(int) * LN);
+  int* tab2_d = (int*)put(tab2, sizeof(int) * 2 * LN);
+  float* asr_d = (float*)put(asr, sizeof(float) * tot * 512);
+  float* f0c_d = (float*)put(f0_in, sizeof(float) * 2 * tot);
+  float* nc_d = (float*)put(n_in, sizeof(float) * 2 * tot);
+  float* sdec_d = (float*)put(s_dec, sizeof(float) * B * 128);
+  uint64_t* seeds_d = seeds ? (uint64_t*)put(seeds, sizeof(uint64_t) * B) : nullptr;
+  float* noise_d = noise ? (float*)put(noise, sizeof(float) * nz) : nullptr;
+  long long* noise_off_d = noise ? (long long*)put(noise_off, sizeof(long long) * B) : nullptr;
+  cur_B = B;
+  float* xcat0 = ar.get<float>((size_t)LN * X0_LD);
+  float* f0 = ar.get<float>((size_t)2 * LN);
+  float* nc = ar.get<float>((size_t)2 * LN);
+  check(launch_gather_rows(asr_d, 512, tab1_d, LN, 512, xcat0, X0_LD, st), "gather_rows");
+  check(launch_gather_rows(f0c_d, 1, tab2_d, 2 * LN, 1, f0, 1, st), "gather_rows");
+  check(launch_gather_rows(nc_d, 1, tab2_d, 2 * LN, 1, nc, 1, st), "gather_rows");
+  const int wdec = m.fc_dec.cout;
+  float* gb_dec = ar.get<float>((size_t)B * wdec);
+  linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
+  float* audio = decode_core(B, max_n, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
+                             noise_off_d);
+  long long o = 0;
+  for (int b = 0; b < B; b++) {
+    KK_CUDA(cudaMemcpyAsync(audio_out + o, audio + 600LL * items_a[b].a, sizeof(float) * 600LL * items_a[b].n,
+                            cudaMemcpyDeviceToHost, st));
+    o += 600LL * items_a[b].n;
+  }
+  int errh = 0;
+  KK_CUDA(cudaMemcpyAsync(&errh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+  KK_CUDA(cudaStreamSynchronize(st));
+  if (errh) throw KKError(KK_ERR_TIMEOUT, "a tcgen05 convolution pipeline wait timed out");
+}
+
 }  // namespace kk
 
 // ------------------------------------------------------------------------------ C ABI
@@ -1441,6 +1590,13 @@ kk_status kk_decode_batch(kk_engine* h, int n_items, const int32_t* n_frames, co
                           float* audio_out) {
   if (!h) return KK_ERR_INVALID_ARG;
   return guarded(h, [&] { h->e->decode(n_items, n_frames, asr, f0, n, s_dec, seeds, noise, audio_out); });
+}
+
+kk_status kk_decode_batch_noalloc(kk_engine* h, int n_items, const int32_t* n_frames, const float* asr, const float* f0,
+                                  const float* n, const float* s_dec, const uint64_t* seeds, const float* noise,
+                                  float* audio_out) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] { h->e->decode_noalloc(n_items, n_frames, asr, f0, n, s_dec, seeds, noise, audio_out); });
 }
 
 kk_status kk_set_option(kk_engine* h, int option, int64_t value) {

@@ -44,6 +44,7 @@ _SIGS = {
     "kk_forward_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_fetch_audio": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64]),
     "kk_decode_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_decode_batch_noalloc": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_set_option": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
     "kk_device_bytes": (ctypes.c_int64, [_P]),
     "kk_launch_count": (ctypes.c_int64, [_P]),
@@ -214,6 +215,33 @@ class GpuKokoro:
                                              _ptr(sds), _ptr(nz), _ptr(out)))
         if not fetch:
             return []
+        res, o = [], 0
+        for k in nf:
+            res.append(out[o:o + k * SAMPLES_PER_FRAME])
+            o += k * SAMPLES_PER_FRAME
+        return res
+
+
+    def decode_batch_noalloc(self, asr: Sequence[np.ndarray], f0: Sequence[np.ndarray],
+                             n_curve: Sequence[np.ndarray], s_dec: np.ndarray,
+                             seeds: Optional[Sequence[int]] = None,
+                             noise: Optional[Sequence[np.ndarray]] = None) -> List[np.ndarray]:
+        """decode_batch without any device / pinned-host allocation, for callers that cannot
+        allocate (a streaming audio thread must not wait on cudaMalloc; a GPU shared under a fixed
+        memory budget must not let the engine's arena grow). Scratch is a 64 MiB static device
+        array shared by every call on the device; at most 8 items and 120 N-frames per call
+        (2 gap frames per item included). Calls that overlap on one device race on the array."""
+        B = len(asr)
+        nf = np.ascontiguousarray([a.shape[0] for a in asr], dtype=np.int32)
+        asr_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in asr]))
+        f0_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in f0]))
+        n_c = np.ascontiguousarray(np.concatenate([np.asarray(a, np.float32) for a in n_curve]))
+        sd = np.ascontiguousarray(np.asarray(s_dec, np.float32).reshape(B, 128))
+        sds = None if seeds is None else np.ascontiguousarray(np.asarray(seeds, np.uint64))
+        nz = None if noise is None else np.ascontiguousarray(np.concatenate([np.asarray(x, np.float32) for x in noise]))
+        out = np.empty(int(nf.sum()) * SAMPLES_PER_FRAME, np.float32)
+        self._check(self.lib.kk_decode_batch_noalloc(self.h, B, _ptr(nf), _ptr(asr_c), _ptr(f0_c), _ptr(n_c),
+                                                     _ptr(sd), _ptr(sds), _ptr(nz), _ptr(out)))
         res, o = [], 0
         for k in nf:
             res.append(out[o:o + k * SAMPLES_PER_FRAME])
