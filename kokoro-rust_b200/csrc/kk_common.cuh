@@ -87,6 +87,10 @@ struct ConvArgs {
   const float* sc;  // OUT_PLUS shortcut [L_out][ldsc]
   int ldsc;
   float oscale;
+  // optional fused AdaIN statistics of the output (tensor-core path): per (item, channel)
+  // sum and sum of squares, accumulated into stat[(b * cout + co) * 2 + {0, 1}] (f64, pre-zeroed)
+  double* stat;
+  Dom dout;           // domain of the output rows (item lookup for stat)
 };
 
 __device__ __forceinline__ float leaky(float v, float s) { return v < 0.0f ? v * s : v; }

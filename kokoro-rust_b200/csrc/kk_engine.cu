@@ -229,6 +229,7 @@ struct Model {
   float* lw;
   float lb;
   Conv noise0, noise1, ups[2], post;
+  Conv noise0_rows;  // BF16 mode: noise_convs.0 as a 2-tap conv over 6-frame rows (see load)
   SnakeBlk noise_res[2], rb[6];
   Conv fc_dec, fc_pro;  // all AdaIN / AdaLN style projections fused: cin 128, cout = sum of 2C
 };
@@ -310,6 +311,9 @@ struct Engine {
   void stage_sync(const char* what);
   ConvArgs ca(const Conv& c);
   void run_conv(const Conv& c, ConvArgs& a);
+  bool tc_route(const Conv& c, const ConvArgs& a) const;
+  void run_conv_stats(const Conv& c, ConvArgs& a, const Dom& dout, const ItemTab* items, int B, int max_len,
+                      float** mean, float** rstd);
   void stats(const float* x, int ldx, int C, const Dom& d, const ItemTab* items, int B, int max_len, float** mean,
              float** rstd);
   void adain_args(ConvArgs& a, const AdaIN& n, const float* mean, const float* rstd, const float* gb, int ldgb, int mode,
@@ -628,6 +632,22 @@ void Engine::load(const Checkpoint& ck) {
   m.lw = up(ck.get(g + ".m_source.l_linear.weight", {1, 9}));
   m.lb = ck.get(g + ".m_source.l_linear.bias", {1})[0];
   m.noise0 = load_conv(ck, g + ".noise_convs.0", 22, 256, 12, 1, 3, 6, true);
+  if (precision == KK_PRECISION_BF16 && tc_ok) {
+    // Conv1d(22 -> 256, k12, stride 6, pad 3) over the spectrum rows equals a 2-tap stride-1 conv
+    // over "6-frame rows" X'[q] = spec rows 6q-3 .. 6q+2 (132 channels: frame j, channel c at
+    // j*22 + c): y[o] = W'_0 X'[o] + W'_1 X'[o+1] with W'_m[co][j*22 + c] = W[co][c][6m + j].
+    // With 3 zero rows ahead of the spectrum, X' is a plain strided view (row stride 132 floats).
+    auto w = ck.conv_weight(g + ".noise_convs.0", {256, 22, 12});
+    auto b = ck.get(g + ".noise_convs.0.bias", {256});
+    std::vector<float> w2((size_t)256 * 132 * 2);
+    for (int co = 0; co < 256; co++)
+      for (int mm = 0; mm < 2; mm++)
+        for (int j = 0; j < 6; j++)
+          for (int c = 0; c < 22; c++)
+            w2[((size_t)co * 132 + j * 22 + c) * 2 + mm] = w[((size_t)co * 22 + c) * 12 + 6 * mm + j];
+    m.noise0_rows = conv_from(w2, b.data(), 132, 256, 2, 1, 0, 1);
+    m.noise0_rows.macs_per_row = (double)22 * 256 * 12;
+  }
   m.noise1 = load_conv(ck, g + ".noise_convs.1", 22, 128, 1, 1, 0, 1, true);
   m.noise_res[0] = load_snake(ck, g + ".noise_res.0", 256, 7, fdw, fdb);
   m.noise_res[1] = load_snake(ck, g + ".noise_res.1", 128, 11, fdw, fdb);
@@ -734,7 +754,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       if (f) {
         fprintf(f, "K=%d dil=%d cin=%d cout=%d L=%d in=%d out=%d |", a.K, a.dil, a.cin, a.cout, a.L_out, a.in_mode,
                 a.out_mode);
-        for (int i = 0; i < 12; i++) fprintf(f, " %llu", h[i]);
+        for (int i = 0; i < 16; i++) fprintf(f, " %llu", h[i]);
         fprintf(f, "\n");
         fclose(f);
       }
@@ -743,6 +763,31 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   } else {
     check(launch_conv_simt(a, st), "conv(simt)");
     prof_end(e0, "conv_simt", flops);
+  }
+}
+
+bool Engine::tc_route(const Conv& c, const ConvArgs& a) const {
+  return precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc);
+}
+
+// Run a convolution and produce the AdaIN statistics of its output [L_out][cout] (ldy == cout):
+// fused into the tensor-core epilogue when the layer runs there, else a separate stats pass.
+void Engine::run_conv_stats(const Conv& c, ConvArgs& a, const Dom& dout, const ItemTab* items, int B, int max_len,
+                            float** mean, float** rstd) {
+  if (tc_route(c, a)) {
+    double* part = ar.get<double>((size_t)2 * B * c.cout);
+    KK_CUDA(cudaMemsetAsync(part, 0, sizeof(double) * 2 * B * c.cout, st));
+    a.stat = part;
+    a.dout = dout;
+    run_conv(c, a);
+    *mean = ar.get<float>((size_t)B * c.cout);
+    *rstd = ar.get<float>((size_t)B * c.cout);
+    check(launch_stats_from_sums(part, c.cout, items, B, dout.scale == 0 ? 1 : dout.scale, dout.plus1, *mean, *rstd,
+                                 st),
+          "stats_from_sums");
+  } else {
+    run_conv(c, a);
+    stats(a.y, a.ldy, c.cout, dout, items, B, max_len, mean, rstd);
   }
 }
 
@@ -797,8 +842,7 @@ void Engine::resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, co
     adain_args(a, R.n1, m1, r1, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
   }
   a.y = h, a.ldy = R.dout, a.L_out = dout.L;
-  run_conv(R.c1, a);
-  stats(h, R.dout, R.dout, dout, items, B, max_n * scale_out, &m2, &r2);
+  run_conv_stats(R.c1, a, dout, items, B, max_n * scale_out, &m2, &r2);
   const float* sc = x;
   int ldsc = ldx;
   if (R.has_sc) {
@@ -826,14 +870,14 @@ void Engine::snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d
   float* h = ar.get<float>((size_t)d.L * C);
   const float* cur = xin;
   const int max_len = max_n * d.scale + d.plus1;
+  float *m1 = nullptr, *r1 = nullptr;
+  stats(xin, C, C, d, items, B, max_len, &m1, &r1);
   for (int i = 0; i < 3; i++) {
-    float *m1, *r1, *m2, *r2;
-    stats(cur, C, C, d, items, B, max_len, &m1, &r1);
+    float *m2, *r2;
     ConvArgs a = ca(S.c1[i]);
     a.x = cur, a.ldx = C, a.din = d, a.L_in = d.L, a.y = h, a.ldy = C, a.L_out = d.L;
     adain_args(a, S.a1[i], m1, r1, gb, ldgb, IN_ADAIN_SNAKE, 0.0f, S.al1[i]);
-    run_conv(S.c1[i], a);
-    stats(h, C, C, d, items, B, max_len, &m2, &r2);
+    run_conv_stats(S.c1[i], a, d, items, B, max_len, &m2, &r2);
     ConvArgs b = ca(S.c2[i]);
     b.x = h, b.ldx = C, b.din = d, b.L_in = d.L, b.y = out, b.ldy = C, b.L_out = d.L;
     adain_args(b, S.a2[i], m2, r2, gb, ldgb, IN_ADAIN_SNAKE, 0.0f, S.al2[i]);
@@ -842,7 +886,11 @@ void Engine::snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d
     } else {
       b.out_mode = OUT_ADD;
     }
-    run_conv(S.c2[i], b);
+    if (i < 2) {
+      run_conv_stats(S.c2[i], b, d, items, B, max_len, &m1, &r1);  // statistics of the next sub-block's input
+    } else {
+      run_conv(S.c2[i], b);
+    }
     cur = out;
   }
   ar.rewind(mk);
@@ -930,7 +978,11 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   float* har = ar.get<float>((size_t)600 * LN);
   check(launch_har_source(f0, pp, L2, items, col_item_n, LN, seeds_d, noise_d, noise_off_d, m.lw, m.lb, har, st),
         "har_source");
-  float* spec = ar.get<float>((size_t)L120 * 22);
+  // spectrum rows with 3 zero rows in front and 8 behind (the 6-frame-row view of noise_convs.0)
+  float* spec_pad = ar.get<float>((size_t)(L120 + 11) * 22);
+  float* spec = spec_pad + 3 * 22;
+  KK_CUDA(cudaMemsetAsync(spec_pad, 0, sizeof(float) * 3 * 22, st));
+  KK_CUDA(cudaMemsetAsync(spec + (size_t)L120 * 22, 0, sizeof(float) * 8 * 22, st));
   check(launch_stft(har, items, d120, spec, 22, st), "stft");
   dump("har", har, 600LL * LN, 1, 1);
   dump("spec", spec, L120, 22, 22);
@@ -942,9 +994,16 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L20 * 256);
     float* xsr = ar.get<float>((size_t)L20 * 256);
-    ConvArgs a = ca(m.noise0);
-    a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256, a.L_out = L20;
-    run_conv(m.noise0, a);
+    if (m.noise0_rows.w) {
+      // gap rows of the spectrum are zero (stft), so the 6-frame-row view needs no masking
+      ConvArgs a = ca(m.noise0_rows);
+      a.x = spec_pad, a.ldx = 132, a.in_mode = IN_NOMASK, a.L_in = L20 + 1, a.y = xs, a.ldy = 256, a.L_out = L20;
+      run_conv(m.noise0_rows, a);
+    } else {
+      ConvArgs a = ca(m.noise0);
+      a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256, a.L_out = L20;
+      run_conv(m.noise0, a);
+    }
     snake(m.noise_res[0], xs, xsr, d20, gb_dec, ldgb, items, B, max_n);
     ConvArgs u = ca(m.ups[0]);
     u.x = xd, u.ldx = 512, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d2, u.L_in = L2;

@@ -447,6 +447,25 @@ cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, i
   return cudaGetLastError();
 }
 
+__global__ void stats_from_sums_kernel(const double* part, int C, const ItemTab* items, int B, int scale, int plus1,
+                                      float* mean, float* rstd) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= B * C) return;
+  const ItemTab it = items[i / C];
+  const double n = (double)(it.n * scale + plus1);
+  const double m = part[2L * i] / n;
+  double var = part[2L * i + 1] / n - m * m;
+  if (var < 0.0) var = 0.0;
+  mean[i] = (float)m;
+  rstd[i] = 1.0f / sqrtf((float)var + 1e-5f);
+}
+
+cudaError_t launch_stats_from_sums(const double* part, int C, const ItemTab* items, int B, int scale, int plus1,
+                                   float* mean, float* rstd, cudaStream_t st) {
+  stats_from_sums_kernel<<<nblk((long)B * C, 256), 256, 0, st>>>(part, C, items, B, scale, plus1, mean, rstd);
+  return cudaGetLastError();
+}
+
 __global__ void adain_coef_kernel(const float* mean, const float* rstd, const float* nw, const float* nb,
                                   const float* gb, int ldgb, int B, int C, float2* coef) {
   int i = blockIdx.x * blockDim.x + threadIdx.x;

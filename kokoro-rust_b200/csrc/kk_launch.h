@@ -69,6 +69,11 @@ cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, i
                          int plus1, int max_len, double* part, float* mean, float* rstd,
                          cudaStream_t st);
 
+// mean / rstd from fused output sums (tensor-core conv epilogue): part[b][c] = (sum, sum of squares)
+// over the item's span of the domain (scale, plus1); biased variance, eps 1e-5.
+cudaError_t launch_stats_from_sums(const double* part, int C, const ItemTab* items, int B, int scale, int plus1,
+                                   float* mean, float* rstd, cudaStream_t st);
+
 // AdaIN folded into one affine map per (item, channel) for the bf16 tensor-core path:
 // coef[b][c] = (A, B) with AdaIN(x) = x * A + B, A = (1 + gamma) * rstd * nw,
 // B = (1 + gamma) * (nb - mean * rstd * nw) + beta.

@@ -40,11 +40,14 @@ namespace kk {
 constexpr int TC_M = 128;
 constexpr int TC_N = 256;
 constexpr int TC_KB = 64;
-constexpr int TC_WST = 4;
+constexpr int TC_WST = 3;
 constexpr int TC_XST_MAX = 4;  // activation-window ring stages (3 when shared memory allows)
 constexpr int TC_MAX_WIN = 512;
-constexpr int TC_EC = 16;                       // epilogue chunk: 16 time rows x 128 channels
-constexpr int TC_EBUF = TC_EC * TC_M * 4;       // 8 KB staging buffer
+constexpr int TC_EC = 16;                       // epilogue chunk: 16 time rows x 32 channels per warp
+constexpr int TC_RES_DEPTH = 4;                 // residual chunks in flight per epilogue warp
+constexpr int TC_EBOX = TC_EC * 32 * 4;         // 2 KB: one warp's chunk (TMA box 32 channels x 16 rows)
+// per epilogue warp: 2 staging chunks, TC_RES_DEPTH residual chunks, the item of each output row
+constexpr int TC_EPI_WARP_BYTES = 2 * TC_EBOX + TC_RES_DEPTH * TC_EBOX + 256 * 4;
 constexpr int TC_THREADS = 448;
 constexpr int TC_WBLOCK = TC_M * TC_KB * 2;  // 16 KB weight block
 constexpr unsigned long long TC_TIMEOUT_NS = 1000000000ull;
@@ -164,6 +167,26 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float* v) {
+  uint32_t r[64];
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x64.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,"
+      "%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32,%33,%34,%35,%36,%37,%38,%39,%40,%41,%42,%43,%44,%45,"
+      "%46,%47,%48,%49,%50,%51,%52,%53,%54,%55,%56,%57,%58,%59,%60,%61,%62,%63}, [%64];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
+        "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
+        "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31]),
+        "=r"(r[32]), "=r"(r[33]), "=r"(r[34]), "=r"(r[35]), "=r"(r[36]), "=r"(r[37]), "=r"(r[38]), "=r"(r[39]),
+        "=r"(r[40]), "=r"(r[41]), "=r"(r[42]), "=r"(r[43]), "=r"(r[44]), "=r"(r[45]), "=r"(r[46]), "=r"(r[47]),
+        "=r"(r[48]), "=r"(r[49]), "=r"(r[50]), "=r"(r[51]), "=r"(r[52]), "=r"(r[53]), "=r"(r[54]), "=r"(r[55]),
+        "=r"(r[56]), "=r"(r[57]), "=r"(r[58]), "=r"(r[59]), "=r"(r[60]), "=r"(r[61]), "=r"(r[62]), "=r"(r[63])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 64; i++) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   uint32_t r[16];
   asm volatile(
@@ -199,7 +222,8 @@ enum TcTrace : int {
   TR_MMA_WAIT_ACC = 0, TR_MMA_WAIT_X = 1, TR_MMA_WAIT_W = 2, TR_MMA_TOTAL = 3,
   TR_LD_WAIT_W = 4, TR_LD_TOTAL = 5,
   TR_PR_WAIT_X = 6, TR_PR_WORK = 7, TR_PR_ITEM = 8,
-  TR_EP_WAIT = 9, TR_EP_WORK = 10, TR_TILES = 11
+  TR_EP_WAIT = 9, TR_EP_WORK = 10, TR_TILES = 11,
+  TR_EP_TMEM = 12, TR_EP_RES = 13, TR_EP_STBUF = 14, TR_EP_STATS = 15
 };
 
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_constant__ TcArgs p) {
@@ -209,17 +233,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   const uint32_t xbytes = 8u * p.win_pad * 16u;
   const int XST = p.xst;
   uint8_t* xbuf = smem + TC_WST * TC_WBLOCK;                  // XST x xbytes
-  float* stage = (float*)(xbuf + XST * xbytes);               // 2 x 8 KB epilogue staging
-  float* resb = stage + 2 * TC_EC * TC_M;                     // 2 x 8 KB residual chunks
-  uint64_t* bars = (uint64_t*)(resb + 2 * TC_EC * TC_M);
+  uint8_t* epi = xbuf + XST * xbytes;                         // 4 x TC_EPI_WARP_BYTES (epilogue warps)
+  uint64_t* bars = (uint64_t*)(epi + 4 * TC_EPI_WARP_BYTES);
   uint64_t* w_full = bars;
   uint64_t* w_empty = bars + TC_WST;
   uint64_t* x_full = bars + 2 * TC_WST;
   uint64_t* x_empty = x_full + TC_XST_MAX;
   uint64_t* acc_full = x_empty + TC_XST_MAX;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* res_full = acc_empty + 2;
-  uint32_t* tmem_slot = (uint32_t*)(res_full + 2);
+  uint64_t* res_full = acc_empty + 2;                         // [4 warps][TC_RES_DEPTH]
+  uint32_t* tmem_slot = (uint32_t*)(res_full + 4 * TC_RES_DEPTH);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   int* ritem = (int*)(tmem_slot + 4);                         // item of each window row (producers)
 
@@ -239,8 +262,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
       mbar_init(&acc_empty[i], 4);
-      mbar_init(&res_full[i], 1);
     }
+    for (int i = 0; i < 4 * TC_RES_DEPTH; i++) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -338,85 +361,153 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     }
   } else if (warp < 6) {
     // ---------------------------------------------------------------- epilogue
+    // Each of the 4 epilogue warps owns the 32 channels of its TMEM lane quarter end to end: its
+    // own staging chunks, TMA store boxes (32 channels x 16 rows), residual ring and row-item
+    // table, so the warps never wait for one another.
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int ew = warp - 2;
+    float* stg = (float*)(epi + ew * TC_EPI_WARP_BYTES);         // [2][16][32]
+    float* rsb = stg + 2 * TC_EC * 32;                            // [TC_RES_DEPTH][16][32]
+    int* eit = (int*)(rsb + TC_RES_DEPTH * TC_EC * 32);           // [256]
+    uint64_t* rbar = res_full + ew * TC_RES_DEPTH;
     const bool trc = p.trace && blockIdx.x == 0 && warp == 2 && lane == 0;
     unsigned long long tew = 0;
-    uint32_t rcount = 0;   // residual chunks consumed (buffer / parity of res_full)
-    uint32_t rissued = 0;  // residual chunk loads issued (lead thread)
+    long long t_tmem = 0, t_res = 0, t_stbuf = 0, t_stats = 0;
     const long long t_start = clock64();
+    uint32_t rcons = 0, riss = 0;  // residual chunks consumed / issued by this warp
+    const int out_mode = a.out_mode, L_out = a.L_out;
+    const long ldy = a.ldy;
+    float* __restrict__ y = a.y;
+    const float oscale = a.oscale;
+    const bool need_res = out_mode == OUT_ADD || out_mode == OUT_PLUS;
+    double* const stat = a.stat;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
       const int ab = lt & 1;
-      if (!mbar_wait_t(&acc_full[ab], (lt >> 1) & 1, abort_flag, p.err, trc ? &tew : nullptr)) break;
-      tc_fence_after();
       const int cot = tile / p.n_tt, tt = tile % p.n_tt;
-      const int co = cot * TC_M + q * 32 + lane;
+      const int co0 = cot * TC_M + q * 32;
+      const int co = co0 + lane;
       const int t0 = tt * TC_N;
       const bool co_ok = co < a.cout;
       const float bias = (co_ok && a.bias) ? a.bias[co] : 0.0f;
-      const int out_mode = a.out_mode, L_out = a.L_out;
-      const long ldy = a.ldy;
-      float* __restrict__ y = a.y;
-      const float oscale = a.oscale;
-      const bool need_res = out_mode == OUT_ADD || out_mode == OUT_PLUS;
-      if (p.tma_out) {
-        // 16 chunks of 16 rows: TMEM -> registers -> (+bias, residual from a TMA-loaded chunk,
-        // gelu) -> shared staging -> one TMA tensor store per chunk (rows / channels past the
-        // output are clipped by the tensor bounds).
-        const bool lead = (warp == 2 && lane == 0);
-        const int ep = q * 32 + lane;  // channel within the tile = this thread's TMEM lane
-        if (need_res && lead) {
-          const int rb = rcount & 1;
-          mbar_arrive_expect_tx(&res_full[rb], TC_EBUF);
-          tma_load_2d(resb + rb * TC_EC * TC_M, &p.rmap, cot * TC_M, t0, &res_full[rb]);
-          rissued = rcount + 1;
+      // residual chunks of this tile start loading before the accumulator is ready
+      if (p.tma_out && need_res && lane == 0) {
+        for (int c = 0; c < TC_RES_DEPTH; c++, riss++) {
+          const int sl = riss % TC_RES_DEPTH;
+          mbar_arrive_expect_tx(&rbar[sl], TC_EBOX);
+          tma_load_2d(rsb + sl * TC_EC * 32, &p.rmap, co0, t0 + c * TC_EC, &rbar[sl]);
         }
-        for (int c = 0; c < TC_N / TC_EC; c++) {
-          if (need_res && lead && c + 1 < TC_N / TC_EC) {
-            const int rb = (rcount + 1) & 1;
-            mbar_arrive_expect_tx(&res_full[rb], TC_EBUF);
-            tma_load_2d(resb + rb * TC_EC * TC_M, &p.rmap, cot * TC_M, t0 + (c + 1) * TC_EC, &res_full[rb]);
-            rissued = rcount + 2;
+      }
+      if (stat) {
+        for (int rr = lane; rr < TC_N; rr += 32) {
+          const int t = t0 + rr;
+          eit[rr] = t < L_out ? dom_item(a.dout, t) : -1;
+        }
+        __syncwarp();
+      }
+      int s_item = -1;
+      float s_sum = 0.0f, s_sq = 0.0f;
+      auto s_flush = [&]() {
+        if (s_item >= 0 && co_ok) {
+          atomicAdd(stat + ((long)s_item * a.cout + co) * 2, (double)s_sum);
+          atomicAdd(stat + ((long)s_item * a.cout + co) * 2 + 1, (double)s_sq);
+        }
+        s_item = -1;
+        s_sum = 0.0f;
+        s_sq = 0.0f;
+      };
+      auto s_chunk = [&](int r0, const float* vals, int n) {  // statistics of rows r0 .. r0 + n - 1
+        const int b0 = eit[r0], b1 = eit[r0 + n - 1];
+        if (b0 == b1 && b0 >= 0) {  // one item spans the chunk (item spans are contiguous)
+          if (b0 != s_item) {
+            s_flush();
+            s_item = b0;
           }
-          float v[TC_EC];
-          tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + c * TC_EC, v);
-          if (c == TC_N / TC_EC - 1) {
+          for (int jj = 0; jj < n; jj++) {
+            s_sum += vals[jj];
+            s_sq = fmaf(vals[jj], vals[jj], s_sq);
+          }
+        } else {
+          for (int jj = 0; jj < n; jj++) {
+            const int b = eit[r0 + jj];
+            if (b != s_item) {
+              s_flush();
+              s_item = b;
+            }
+            if (b >= 0) {
+              s_sum += vals[jj];
+              s_sq = fmaf(vals[jj], vals[jj], s_sq);
+            }
+          }
+        }
+      };
+      if (!mbar_wait_t(&acc_full[ab], (lt >> 1) & 1, abort_flag, p.err, trc ? &tew : nullptr)) break;
+      tc_fence_after();
+      if (p.tma_out) {
+        bool bad = false;
+        for (int sc = 0; sc < TC_N / 64 && !bad; sc++) {
+          float v[64];
+          long long tq = trc ? clock64() : 0;
+          tmem_ld64(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + sc * 64, v);
+          if (trc) t_tmem += clock64() - tq;
+          if (sc == TC_N / 64 - 1) {
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&acc_empty[ab]);  // accumulator fully read
           }
-          const float* rr = resb;
-          if (need_res) {
-            const int rb = rcount & 1;
-            mbar_wait(&res_full[rb], (rcount >> 1) & 1, abort_flag, p.err);  // failure -> abort flag
-            rr = resb + rb * TC_EC * TC_M;
-            rcount++;
-          }
-          float* sb = stage + (c & 1) * TC_EC * TC_M;
-          if (lead) bulk_wait_read1();  // the store issued two chunks ago has read this buffer
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          if (*abort_flag) break;  // uniform: every epilogue thread sees the flag after the barrier
 #pragma unroll
-          for (int jj = 0; jj < TC_EC; jj++) {
-            float r = v[jj] + bias;
-            if (out_mode == OUT_ADD) r = rr[jj * TC_M + ep] + r;
-            else if (out_mode == OUT_PLUS) r = (r + rr[jj * TC_M + ep]) * oscale;
-            else if (out_mode == OUT_GELU) r = gelu_new(r);
-            sb[jj * TC_M + ep] = r;
-          }
-          fence_proxy_async();
-          asm volatile("bar.sync 2, 128;" ::: "memory");
-          if (lead) {
-            tma_store_2d(&p.ymap, cot * TC_M, t0 + c * TC_EC, sb);
-            bulk_commit();
+          for (int sub = 0; sub < 64 / TC_EC; sub++) {
+            const int c = sc * (64 / TC_EC) + sub;
+            const float* rr = rsb;
+            long long tq = trc ? clock64() : 0;
+            if (need_res) {
+              const int sl = rcons % TC_RES_DEPTH;
+              if (!mbar_wait(&rbar[sl], (rcons / TC_RES_DEPTH) & 1, abort_flag, p.err)) bad = true;
+              rr = rsb + sl * TC_EC * 32;
+            }
+            if (trc) t_res += clock64() - tq, tq = clock64();
+            float* sb = stg + (c & 1) * TC_EC * 32;
+            if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
+            __syncwarp();
+            if (trc) t_stbuf += clock64() - tq;
+            float vals[TC_EC];
+#pragma unroll
+            for (int jj = 0; jj < TC_EC; jj++) {
+              float r = v[sub * TC_EC + jj] + bias;
+              if (out_mode == OUT_ADD) r = rr[jj * 32 + lane] + r;
+              else if (out_mode == OUT_PLUS) r = (r + rr[jj * 32 + lane]) * oscale;
+              else if (out_mode == OUT_GELU) r = gelu_new(r);
+              vals[jj] = r;
+              sb[jj * 32 + lane] = r;
+            }
+            if (trc) tq = clock64();
+            if (stat) s_chunk(c * TC_EC, vals, TC_EC);
+            if (trc) t_stats += clock64() - tq;
+            fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) {
+              tma_store_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
+              bulk_commit();
+            }
+            if (need_res) {  // every lane has read this residual slot: refill it
+              if (lane == 0 && c + TC_RES_DEPTH < TC_N / TC_EC) {
+                const int sl = riss % TC_RES_DEPTH;
+                mbar_arrive_expect_tx(&rbar[sl], TC_EBOX);
+                tma_load_2d(rsb + sl * TC_EC * 32, &p.rmap, co0, t0 + (c + TC_RES_DEPTH) * TC_EC, &rbar[sl]);
+              }
+              if (c + TC_RES_DEPTH < TC_N / TC_EC) riss++;
+              rcons++;
+            }
           }
         }
+        if (stat) s_flush();
+        if (bad) break;
         continue;
       }
+      // direct stores (row stride not 16-byte aligned): residual loads one 32-row chunk ahead
       const bool need_res_d = co_ok && need_res;
       const float* __restrict__ rsrc = out_mode == OUT_ADD ? a.y : a.sc;
       const long rld = out_mode == OUT_ADD ? a.ldy : a.ldsc;
-      // residual operands are software-pipelined one 32-column chunk ahead
       float res[32];
 #pragma unroll
       for (int jj = 0; jj < 32; jj++) {
@@ -447,22 +538,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           for (int jj = 0; jj < 32; jj++)
             if (t0 + c0 + jj < L_out) yp[(long)jj * ldy] = v[jj];
         }
+        if (stat) s_chunk(c0, v, 32);
       }
+      if (stat) s_flush();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
-    if (p.tma_out && warp == 2 && lane == 0) {
-      for (uint32_t k = rcount; k < rissued; k++) {  // residual loads still in flight (abort path)
+    if (p.tma_out && lane == 0) {
+      for (uint32_t k = rcons; k < riss; k++) {  // residual loads still in flight (abort path)
         const unsigned long long t0 = tc_now();
-        while (!mbar_try(&res_full[k & 1], (k >> 1) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+        while (!mbar_try(&rbar[k % TC_RES_DEPTH], (k / TC_RES_DEPTH) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
         }
       }
-      bulk_wait_all();  // stores complete before exit
+      bulk_wait_all();  // this warp's stores complete before exit
     }
     if (trc) {
       p.trace[TR_EP_WAIT] = tew;
       p.trace[TR_EP_WORK] = (unsigned long long)(clock64() - t_start) - tew;
+      p.trace[TR_EP_TMEM] = t_tmem;
+      p.trace[TR_EP_RES] = t_res;
+      p.trace[TR_EP_STBUF] = t_stbuf;
+      p.trace[TR_EP_STATS] = t_stats;
     }
   } else {
     // ---------------------------------------------------------------- activation producers
@@ -663,8 +760,8 @@ bool tc_supported(const ConvArgs& a, const TcWeights& t) {
 }
 
 static size_t tc_smem(int win_pad, int xst) {
-  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + 4 * TC_EBUF +
-         (2 * TC_WST + 2 * TC_XST_MAX + 6) * 8 + 16 + TC_MAX_WIN * 4;
+  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + 4 * TC_EPI_WARP_BYTES +
+         (2 * TC_WST + 2 * TC_XST_MAX + 4 + 4 * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
 }
 
 static int g_num_sms[64] = {0};
@@ -689,13 +786,13 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// f32 rows [rows][cols] with row stride ld floats; box = 128 columns x 16 rows, no swizzle.
+// f32 rows [rows][cols] with row stride ld floats; box = 32 columns x 16 rows, no swizzle.
 static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long cols, long ld) {
   EncodeTiledFn fn = encode_fn();
   if (!fn || (ld % 4) != 0 || (((uintptr_t)base) & 15) != 0 || rows <= 0 || cols <= 0) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {(cuuint32_t)TC_M, (cuuint32_t)TC_EC};
+  cuuint32_t box[2] = {32u, (cuuint32_t)TC_EC};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
