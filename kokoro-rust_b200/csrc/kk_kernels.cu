@@ -258,10 +258,9 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
 // ------------------------------------------------------------------------------ LSTM
 
 constexpr int LH = 256;            // hidden units per direction
-constexpr int L_UNITS = 4;         // hidden units owned by one CTA (all four gates)
-constexpr int L_CTAS_PER_DIR = LH / L_UNITS;
-constexpr int L_KC = 32;           // k-chunk of the staged hidden state
-constexpr int L_IPC = 64;          // items per chunk (one per thread group of 4 units)
+constexpr int L_UNITS = 16;        // hidden units owned by one CTA (all four gates: 64 rows of W_hh)
+constexpr int L_UBLK = LH / L_UNITS;
+constexpr int L_HLD = LH + 4;      // row stride of the staged hidden states (floats)
 constexpr unsigned long long L_TIMEOUT_NS = 2000000000ull;
 
 __device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
@@ -276,82 +275,121 @@ __device__ __forceinline__ unsigned long long globaltimer_ns() {
 }
 
 // Bidirectional LSTM recurrence for all items of a batch (kernels/kokoro.cu:400-450 semantics:
-// gates = gx + (W_hh h + b_hh), order i, f, g, o). CTA (dir, unit block) keeps its 16 rows of
-// W_hh in shared memory for the whole sequence; thread (unit, item lane) owns one (item, unit)
-// and computes its four gates, so the cell update needs no exchange. One bounded step barrier
-// per direction: a wait longer than 2 s sets *err and every CTA returns.
-__global__ void __launch_bounds__(256) lstm_kernel(LstmArgs a) {
-  __shared__ float Ws[16][LH + 4];
-  __shared__ float Hs[L_IPC][L_KC + 1];
+// gates = gx + (W_hh h + b_hh), order i, f, g, o; fp32 throughout). CTA (dir, group, unit block):
+// W_hh rows of its 16 units (4 gates) stay in shared memory for the whole sequence; each step the
+// group's active hidden states are staged once (float4, L2), thread (unit, item lane) computes the
+// four gate dot products of its unit for items lane, lane + 16, ... with float4 register blocking,
+// keeps the cell states of those (unit, item) pairs in registers, and writes the new hidden state.
+// One bounded barrier per step over the 16 CTAs of (dir, group): a wait longer than 2 s sets *err
+// and every CTA returns.
+template <int IPT>
+__global__ void __launch_bounds__(256, 1) lstm_kernel(const LstmArgs a) {
+  extern __shared__ __align__(16) float lsm[];
+  float* Ws = lsm;                       // [16 units][4 gates][256]
+  float* Hs = lsm + L_UNITS * 4 * LH;    // [IPG][L_HLD]
   __shared__ int s_abort;
-  const int dir = blockIdx.x / L_CTAS_PER_DIR;
-  const int j0 = (blockIdx.x % L_CTAS_PER_DIR) * L_UNITS;
-  const int tid = threadIdx.x, jl = tid & 3, il = tid >> 2;
-  const int j = j0 + jl;
-  for (int i = tid; i < 16 * LH; i += 256) {
-    int r = i / LH, k = i % LH;
-    int g = r >> 2, u = r & 3;
-    Ws[r][k] = a.whh[((long)dir * 4 * LH + g * LH + j0 + u) * LH + k];
+  const int per_dir = a.G * L_UBLK;
+  const int dir = blockIdx.x / per_dir;
+  const int g = (blockIdx.x / L_UBLK) % a.G;
+  const int u0 = (blockIdx.x % L_UBLK) * L_UNITS;
+  const int tid = threadIdx.x, uu = tid >> 4, il = tid & 15;
+  const int unit = u0 + uu;
+  for (int i = tid; i < L_UNITS * 4 * LH / 4; i += 256) {
+    const int row = i / (LH / 4), k4 = i % (LH / 4);
+    const int u = row >> 2, gate = row & 3;
+    reinterpret_cast<float4*>(Ws)[i] =
+        reinterpret_cast<const float4*>(a.whh + ((long)dir * 4 * LH + gate * LH + u0 + u) * LH)[k4];
   }
   float bh[4];
 #pragma unroll
-  for (int g = 0; g < 4; g++) bh[g] = a.bhh[dir * 4 * LH + g * LH + j];
+  for (int q = 0; q < 4; q++) bh[q] = a.bhh[dir * 4 * LH + q * LH + unit];
+  const int* items = a.gitems + g * a.IPG;
+  const int* act = a.gact + (long)g * a.Tmax;
+  unsigned* bar = a.bar + dir * a.G + g;
+  float c[IPT];
+#pragma unroll
+  for (int m = 0; m < IPT; m++) c[m] = 0.0f;
   __syncthreads();
   for (int s = 0; s < a.Tmax; s++) {
-    const int na = a.act[s];
-    const float* hp = a.hbuf + ((long)(s & 1) * 2 + dir) * (long)a.B * LH;
-    float* hn = a.hbuf + ((long)((s + 1) & 1) * 2 + dir) * (long)a.B * LH;
-    for (int ic = 0; ic < na; ic += L_IPC) {
-      const int rank = ic + il;
-      const bool valid = rank < na;
-      const int b = valid ? a.order[rank] : 0;
-      float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-      for (int kc = 0; kc < LH; kc += L_KC) {
-        __syncthreads();
-        for (int i = tid; i < L_IPC * L_KC; i += 256) {
-          int ii = i / L_KC, kk = i % L_KC;
-          int rr = ic + ii;
-          Hs[ii][kk] = rr < na ? __ldcg(hp + (long)a.order[rr] * LH + kc + kk) : 0.0f;
-        }
-        __syncthreads();
-#pragma unroll 8
-        for (int kk = 0; kk < L_KC; kk++) {
-          const float hv = Hs[il][kk];
-          acc[0] = fmaf(Ws[jl][kc + kk], hv, acc[0]);
-          acc[1] = fmaf(Ws[4 + jl][kc + kk], hv, acc[1]);
-          acc[2] = fmaf(Ws[8 + jl][kc + kk], hv, acc[2]);
-          acc[3] = fmaf(Ws[12 + jl][kc + kk], hv, acc[3]);
+    const int na = act[s];
+    if (na == 0) return;  // the group's items are done (same for all 16 CTAs of the group)
+    {
+      const float* hp = a.hbuf + ((long)(s & 1) * 2 + dir) * (long)a.B * LH;
+      float* hn = a.hbuf + ((long)((s + 1) & 1) * 2 + dir) * (long)a.B * LH;
+      for (int i = tid; i < na * (LH / 4); i += 256) {
+        const int slot = i / (LH / 4), k4 = i % (LH / 4);
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(hp + (long)items[slot] * LH) + k4);
+        *reinterpret_cast<float4*>(Hs + slot * L_HLD + k4 * 4) = v;
+      }
+      // gate inputs of the owned (unit, item) pairs, fetched while the hidden states land
+      float gxv[IPT][4];
+      int rowv[IPT];
+#pragma unroll
+      for (int m = 0; m < IPT; m++) {
+        const int slot = il + 16 * m;
+        rowv[m] = -1;
+        if (slot < na) {
+          const int b = items[slot];
+          const int T = a.len[b];
+          const int t = dir == 0 ? s : T - 1 - s;
+          rowv[m] = a.start[b] + t;
+          const float* gp = a.gx + (long)rowv[m] * a.ldgx + dir * 4 * LH + unit;
+#pragma unroll
+          for (int q = 0; q < 4; q++) gxv[m][q] = gp[q * LH];
         }
       }
-      if (valid) {
-        const int T = a.len[b];
-        const int t = dir == 0 ? s : T - 1 - s;
-        const long row = (long)a.start[b] + t;
-        const float* gx = a.gx + row * a.ldgx + dir * 4 * LH;
-        const float gi = gx[j] + (acc[0] + bh[0]);
-        const float gf = gx[LH + j] + (acc[1] + bh[1]);
-        const float gg = gx[2 * LH + j] + (acc[2] + bh[2]);
-        const float go = gx[3 * LH + j] + (acc[3] + bh[3]);
+      __syncthreads();
+      float acc[IPT][4];
+#pragma unroll
+      for (int m = 0; m < IPT; m++)
+#pragma unroll
+        for (int q = 0; q < 4; q++) acc[m][q] = 0.0f;
+      const float* wrow = Ws + uu * 4 * LH;
+#pragma unroll 2
+      for (int k = 0; k < LH; k += 4) {
+        float4 w[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) w[q] = *reinterpret_cast<const float4*>(wrow + q * LH + k);
+#pragma unroll
+        for (int m = 0; m < IPT; m++) {
+          if (il + 16 * m < na) {
+            const float4 h = *reinterpret_cast<const float4*>(Hs + (il + 16 * m) * L_HLD + k);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              acc[m][q] = fmaf(w[q].x, h.x, acc[m][q]);
+              acc[m][q] = fmaf(w[q].y, h.y, acc[m][q]);
+              acc[m][q] = fmaf(w[q].z, h.z, acc[m][q]);
+              acc[m][q] = fmaf(w[q].w, h.w, acc[m][q]);
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < IPT; m++) {
+        if (rowv[m] < 0) continue;
+        const float gi = gxv[m][0] + (acc[m][0] + bh[0]);
+        const float gf = gxv[m][1] + (acc[m][1] + bh[1]);
+        const float gg = gxv[m][2] + (acc[m][2] + bh[2]);
+        const float go = gxv[m][3] + (acc[m][3] + bh[3]);
         const float ig = 1.0f / (1.0f + expf(-gi));
         const float fg = 1.0f / (1.0f + expf(-gf));
         const float cg = tanhf(gg);
         const float og = 1.0f / (1.0f + expf(-go));
-        float* cp = a.cst + ((long)dir * a.B + b) * LH + j;
-        const float c = fg * (*cp) + ig * cg;
-        *cp = c;
-        const float h = og * tanhf(c);
-        hn[(long)b * LH + j] = h;
-        a.out[row * a.ldo + dir * LH + j] = h;
+        c[m] = fg * c[m] + ig * cg;
+        const float h = og * tanhf(c[m]);
+        hn[(long)items[il + 16 * m] * LH + unit] = h;
+        a.out[(long)rowv[m] * a.ldo + dir * LH + unit] = h;
       }
     }
+    // step barrier over the 16 CTAs of this (direction, group)
     __syncthreads();
     if (tid == 0) {
       __threadfence();
-      atomicAdd(a.bar + dir, 1u);
-      const unsigned target = (unsigned)(s + 1) * L_CTAS_PER_DIR;
+      atomicAdd(bar, 1u);
+      const unsigned target = (unsigned)(s + 1) * L_UBLK;
       const unsigned long long t0 = globaltimer_ns();
       int ab = 0;
-      while (ld_acquire_u32(a.bar + dir) < target) {
+      while (ld_acquire_u32(bar) < target) {
         if (*(volatile int*)a.err) {
           ab = 1;
           break;
@@ -361,7 +399,6 @@ __global__ void __launch_bounds__(256) lstm_kernel(LstmArgs a) {
           ab = 1;
           break;
         }
-        __nanosleep(64);
       }
       __threadfence();
       s_abort = ab;
@@ -374,12 +411,19 @@ __global__ void __launch_bounds__(256) lstm_kernel(LstmArgs a) {
 cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st) {
   cudaError_t e;
   if ((e = cudaMemsetAsync(a.hbuf, 0, sizeof(float) * 4L * a.B * LH, st)) != cudaSuccess) return e;
-  if ((e = cudaMemsetAsync(a.cst, 0, sizeof(float) * 2L * a.B * LH, st)) != cudaSuccess) return e;
-  if ((e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned) * 2, st)) != cudaSuccess) return e;
+  if ((e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned) * 2 * a.G, st)) != cudaSuccess) return e;
   if (a.Tmax == 0) return cudaSuccess;
+  if (a.G < 1 || a.G > LSTM_MAX_GROUPS || a.IPG < 1 || a.IPG > LSTM_MAX_IPG) return cudaErrorInvalidValue;
+  const size_t smem = sizeof(float) * (L_UNITS * 4 * LH + (size_t)a.IPG * L_HLD);
   LstmArgs args = a;
   void* params[] = {&args};
-  return cudaLaunchCooperativeKernel((const void*)lstm_kernel, dim3(2 * L_CTAS_PER_DIR), dim3(256), params, 0, st);
+  const int ipt = (a.IPG + 15) / 16;
+  const void* fn = ipt <= 1   ? (const void*)lstm_kernel<1>
+                   : ipt <= 2 ? (const void*)lstm_kernel<2>
+                   : ipt <= 4 ? (const void*)lstm_kernel<4>
+                              : (const void*)lstm_kernel<9>;
+  if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
+  return cudaLaunchCooperativeKernel(fn, dim3(2 * a.G * L_UBLK), dim3(256), params, smem, st);
 }
 
 // ------------------------------------------------------------------------------ AdaIN statistics

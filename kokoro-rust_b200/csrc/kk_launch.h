@@ -44,23 +44,27 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
                                  float* ctx, int ldc, cudaStream_t st);
 
 // ---- LSTM recurrence (persistent, one cooperative launch per BiLSTM)
+// Items (sorted longest-first) are dealt round-robin into G <= 4 groups of at most IPG <= 144
+// items; CTA (direction, group, unit block) owns 16 hidden units = 64 rows of W_hh in shared
+// memory and the group's hidden states; only the 16 CTAs of one (direction, group) synchronise.
 struct LstmArgs {
-  const float* gx;  // [rows][ldgx]: dir d gate g unit j at column d*4H + g*H + j (includes b_ih)
+  const float* gx;    // [rows][ldgx]: dir d gate g unit j at column d*4H + g*H + j (includes b_ih)
   int ldgx;
-  const float* whh;  // [2][4H][H]
-  const float* bhh;  // [2][4H]
-  float* out;        // [rows][ldo]: dir d unit j at column d*H + j
+  const float* whh;   // [2][4H][H]
+  const float* bhh;   // [2][4H]
+  float* out;         // [rows][ldo]: dir d unit j at column d*H + j
   int ldo;
-  const int* start;  // [B] first row of item b
-  const int* len;    // [B]
-  const int* order;  // [B] items by length, descending
-  const int* act;    // [Tmax] number of items still running at step s
-  int B, Tmax;
-  float* hbuf;       // [2][2][B][H] double-buffered hidden state (zeroed by the launcher)
-  float* cst;        // [2][B][H] cell state (zeroed by the launcher)
-  unsigned* bar;     // [2] step-barrier counters (zeroed by the launcher)
-  int* err;          // set to 1 when a barrier wait times out
+  const int* start;   // [B] first row of item b
+  const int* len;     // [B]
+  const int* gitems;  // [G][IPG] items of each group, longest first (-1 = none)
+  const int* gact;    // [G][Tmax] items of group g still running at step s
+  int B, Tmax, G, IPG;
+  float* hbuf;        // [2][2][B][H] double-buffered hidden state (zeroed by the launcher)
+  unsigned* bar;      // [2][G] step-barrier counters (zeroed by the launcher)
+  int* err;           // set to 1 when a barrier wait times out
 };
+constexpr int LSTM_MAX_GROUPS = 4;
+constexpr int LSTM_MAX_IPG = 144;
 cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st);
 
 // ---- AdaIN statistics: per (item, channel) mean / rstd over the item's span (biased variance,
