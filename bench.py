@@ -170,6 +170,7 @@ def main():
     ap.add_argument("--precision", default=os.environ.get("KK_PRECISION", "bf16"), choices=["bf16", "fp32"])
     ap.add_argument("--cpu-lines", type=int, default=3, help="lines in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--launch-log", default=None, help="write every profiled launch (class, ms, FLOPs, bytes) as CSV")
     ap.add_argument("--items", type=int, default=32, help="config2: utterances per batch")
     ap.add_argument("--frames", type=int, default=400, help="config2: frames per utterance")
     args = ap.parse_args()
@@ -264,6 +265,7 @@ def main():
         wall = time.perf_counter() - w0
     launches = eng.launch_count() - l0
     prof = eng.profile()
+    plog = eng.profile_launches()
     eng.set_option(kk.engine.KK_OPT_PROFILE, 0)
     t = torch.tensor([dev_ms, audio_s], dtype=torch.float64, device=f"cuda:{local_rank}")
     if world > 1:
@@ -309,6 +311,21 @@ def main():
                     "frac": achieved / peak, "traffic": None, "launches": n_l, "avg_launch_ms": ms / max(n_l, 1),
                     "peak_source": "MEASURED_PEAKS.json bf16_tflops_sustained (kernel timed inside a long step)",
                     "share_of_step": ms / dev_ms}
+            # per-launch floor max(FLOPs / tensor peak, algorithmic bytes / HBM peak): many of the
+            # 128/256-channel k=3 layers move more bytes than their FLOPs can cover
+            hbm = peaks.get("hbm_gbs") or 6650.0
+            recs = [r for r in plog if r[0] == conv_cls]
+            floor_ms = sum(max(r[2] / (peak * 1e12), r[3] / (hbm * 1e9)) * 1e3 for r in recs)
+            hbm_ms = sum(r[1] for r in recs if r[3] / (hbm * 1e9) > r[2] / (peak * 1e12))
+            tot = sum(r[1] for r in recs)
+            roof["mixed_floor"] = {"floor_ms": floor_ms, "ms": tot, "frac": floor_ms / max(tot, 1e-9),
+                                   "hbm_bound_time_share": hbm_ms / max(tot, 1e-9),
+                                   "bytes": sum(r[3] for r in recs), "hbm_peak_gbs": hbm}
+        if args.launch_log:
+            with open(args.launch_log, "w") as f:
+                f.write("class,ms,flops,bytes\n")
+                for r in plog:
+                    f.write(f"{r[0]},{r[1]:.6f},{r[2]:.6g},{r[3]:.6g}\n")
         cpu = None
         if not args.no_cpu_baseline and args.workload == "config4":
             threads = torch.get_num_threads()

@@ -164,7 +164,49 @@ KK_API kk_status kk_last_times(kk_engine* e, double out[4]);
  */
 KK_API int kk_profile_entry(kk_engine* e, int i, char* name, int name_cap, int64_t* launches, double* ms,
                             double* flops);
+/*
+ * Launch i (0-based) of the launches profiled since the last kk_profile_reset: its class, device
+ * time (ms), algorithmic FLOPs and algorithmic bytes (each input row read once, each output row
+ * written once, residual rows read once, weights once). i < 0 returns the number of launches.
+ * No counterpart in the reference (diagnostics of this engine).
+ */
+KK_API int kk_profile_launch(kk_engine* e, int i, char* cls, int cls_cap, double* ms, double* flops,
+                             double* bytes);
 KK_API void kk_profile_reset(kk_engine* e);
+
+/*
+ * kk_conv_selftest -- diagnostics: one 1-D convolution through the bf16 tcgen05 kernel on host
+ * buffers (allocates and frees its own device memory; synchronous). No counterpart in the
+ * reference: it exists so the kernel can be tested on its own against an fp32 convolution.
+ *
+ *  x      [rows_in or ceil(rows_in / 2) with up2][ldx] f32 input rows
+ *  w      [cout][cin][K] f32 (torch Conv1d layout); bias [cout] or NULL
+ *  coef   [n_items][cin] (A, B) pairs, AdaIN folded to x * A + B (in_mode 2 and 3)
+ *  alpha  [cin] Snake alpha (in_mode 3)
+ *  sc     [rows_out][ldsc] shortcut rows (out_mode 2)
+ *  y      [rows_out][ldy] in/out (read for out_mode 1)
+ *  stat   NULL, or [n_items][cout][2] f64: per (item, channel) sum and sum of squares of y
+ */
+typedef struct kk_conv_case {
+  int cin, cout, K, dil, pad;
+  int rows_in;   /* input-domain rows (after the optional nearest x2 upsample) */
+  int ldx;
+  int up2;       /* 1: input-domain row t reads x row t / 2 */
+  int in_mode;   /* 0 as is, 1 gap rows -> 0, 2 leaky(AdaIN), 3 Snake(AdaIN), 4 leaky + gap mask */
+  float slope;
+  int rows_out, ldy;
+  int out_mode;  /* 0 y = acc + bias, 1 y += acc + bias, 2 y = (acc + bias + sc) * oscale, 3 gelu */
+  float oscale;
+  int ldsc;
+  int n_items;
+  const int* item_in;   /* [rows_in] item of each input-domain row, -1 = gap */
+  const int* item_out;  /* [rows_out] item of each output row, -1 = gap */
+} kk_conv_case;
+KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x, const float* w,
+                                  const float* bias, const float* coef, const float* alpha, const float* sc,
+                                  float* y, double* stat);
+/* Message of the last kk_conv_selftest failure on this thread. */
+KK_API const char* kk_conv_selftest_error(void);
 
 /* Bytes of device memory the engine currently holds (weights + arena). */
 KK_API int64_t kk_device_bytes(const kk_engine* e);

@@ -258,6 +258,7 @@ struct Engine {
   bool tc_ok = false;
   bool noalloc_active = false;  // inside kk_decode_batch_noalloc: no events, no pinned staging
   const char* tc_trace_dir = getenv("KK_TC_TRACE_DIR");  // diagnostics: per-launch pipeline cycle accounting
+  const bool prof_shapes = getenv("KK_PROFILE_SHAPES") != nullptr;  // diagnostics: conv shape in the class name
   int cur_B = 0;  // items of the batch being run
   // timing: events on the engine stream (begin, compute begin, compute end, end)
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
@@ -267,8 +268,13 @@ struct Engine {
   struct ProfRec {
     int cls;
     cudaEvent_t a, b;
-    double flops;
+    double flops, bytes;
   };
+  struct ProfLaunch {  // one timed launch since the last profile reset
+    int cls;
+    double ms, flops, bytes;
+  };
+  std::vector<ProfLaunch> prof_log;
   std::vector<ProfRec> prof_pending;
   std::vector<cudaEvent_t> ev_pool;
   size_t ev_used = 0;
@@ -303,7 +309,7 @@ struct Engine {
   cudaEvent_t pool_event();
   int prof_class(const char* name);
   void prof_begin(cudaEvent_t* a);
-  void prof_end(cudaEvent_t a, const char* cls, double flops);
+  void prof_end(cudaEvent_t a, const char* cls, double flops, double bytes = 0.0);
   void prof_collect();
   void times_begin();
   void times_compute_begin();
@@ -380,11 +386,11 @@ void Engine::prof_begin(cudaEvent_t* a) {
   KK_CUDA(cudaEventRecord(*a, st));
 }
 
-void Engine::prof_end(cudaEvent_t a, const char* cls, double flops) {
+void Engine::prof_end(cudaEvent_t a, const char* cls, double flops, double bytes) {
   if (!profile || !a) return;
   cudaEvent_t b = pool_event();
   KK_CUDA(cudaEventRecord(b, st));
-  prof_pending.push_back({prof_class(cls), a, b, flops});
+  prof_pending.push_back({prof_class(cls), a, b, flops, bytes});
 }
 
 // Called after the stream is synchronised: fold the recorded launch intervals into the profile.
@@ -395,6 +401,7 @@ void Engine::prof_collect() {
     prof_launches[r.cls]++;
     prof_ms[r.cls] += ms;
     prof_flops[r.cls] += r.flops;
+    prof_log.push_back({r.cls, (double)ms, r.flops, r.bytes});
   }
   prof_pending.clear();
   ev_used = 0;
@@ -739,7 +746,14 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   cudaEvent_t e0;
   prof_begin(&e0);
   const double flops = 2.0 * c.macs_per_row * a.L_out;
-  if (precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc)) {
+  // algorithmic bytes: f32 input rows read once, output rows written once (read too when
+  // accumulated into), shortcut rows read once, weights once (bf16 image or f32)
+  const bool res = a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS;
+  const bool tc_path = precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc);
+  const double in_rows = a.in_up2 ? (double)((a.L_in + 1) / 2) : (double)a.L_in;
+  const double bytes = 4.0 * (in_rows * a.cin + (double)a.L_out * a.cout * (res ? 2 : 1)) +
+                       (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
+  if (tc_path) {
     unsigned long long* tr = nullptr;
     if (tc_trace_dir) {
       tr = ar.get<unsigned long long>(16);
@@ -759,10 +773,17 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
         fclose(f);
       }
     }
-    prof_end(e0, "conv_tcgen05", flops);
+    if (prof_shapes) {
+      char tag[96];
+      snprintf(tag, sizeof(tag), "conv_tcgen05 k%d d%d %d>%d L%d in%d out%d st%d", a.K, a.dil, a.cin, a.cout, a.L_out,
+               a.in_mode, a.out_mode, a.stat ? 1 : 0);
+      prof_end(e0, tag, flops, bytes);
+    } else {
+      prof_end(e0, "conv_tcgen05", flops, bytes);
+    }
   } else {
     check(launch_conv_simt(a, st), "conv(simt)");
-    prof_end(e0, "conv_simt", flops);
+    prof_end(e0, "conv_simt", flops, bytes);
   }
 }
 
@@ -1702,12 +1723,30 @@ int kk_profile_entry(kk_engine* h, int i, char* name, int name_cap, int64_t* lau
   return n;
 }
 
+int kk_profile_launch(kk_engine* h, int i, char* cls, int cls_cap, double* ms, double* flops, double* bytes) {
+  if (!h) return -1;
+  kk::Engine& e = *h->e;
+  const int n = (int)e.prof_log.size();
+  if (i < 0) return n;
+  if (i >= n) return -1;
+  const auto& r = e.prof_log[i];
+  if (cls && cls_cap > 0) {
+    strncpy(cls, e.prof_names[r.cls].c_str(), (size_t)cls_cap - 1);
+    cls[cls_cap - 1] = 0;
+  }
+  if (ms) *ms = r.ms;
+  if (flops) *flops = r.flops;
+  if (bytes) *bytes = r.bytes;
+  return n;
+}
+
 void kk_profile_reset(kk_engine* h) {
   if (!h) return;
   kk::Engine& e = *h->e;
   std::fill(e.prof_launches.begin(), e.prof_launches.end(), 0);
   std::fill(e.prof_ms.begin(), e.prof_ms.end(), 0.0);
   std::fill(e.prof_flops.begin(), e.prof_flops.end(), 0.0);
+  e.prof_log.clear();
 }
 
 int64_t kk_device_bytes(const kk_engine* h) { return h ? (int64_t)(h->e->wbytes + h->e->ar.bytes()) : 0; }

@@ -1,0 +1,97 @@
+// Diagnostics entry point: one 1-D convolution through the tcgen05 kernel on caller buffers, so the
+// kernel can be checked on its own against an fp32 reference (every prologue / epilogue mode, odd
+// channel counts, ragged item layouts). Not part of the model path.
+#include <cuda_runtime.h>
+#include <string.h>
+#include <string>
+#include <vector>
+
+#include "../../include/kokoro_b200.h"
+#include "kk_common.cuh"
+#include "kk_tc.h"
+
+namespace {
+
+thread_local std::string g_selftest_error;
+
+struct DevBuf {
+  void* p = nullptr;
+  ~DevBuf() {
+    if (p) cudaFree(p);
+  }
+};
+
+kk_status fail(kk_status s, const std::string& m) {
+  g_selftest_error = m;
+  return s;
+}
+
+}  // namespace
+
+extern "C" KK_API const char* kk_conv_selftest_error(void) { return g_selftest_error.c_str(); }
+
+extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x,
+                                             const float* w, const float* bias, const float* coef,
+                                             const float* alpha, const float* sc, float* y, double* stat) {
+  using namespace kk;
+  if (!c || !x || !w || !y) return fail(KK_ERR_INVALID_ARG, "null argument");
+  if (c->cin < 1 || c->cout < 1 || c->K < 1 || c->dil < 1 || c->rows_in < 1 || c->rows_out < 1 ||
+      c->ldx < c->cin || c->ldy < c->cout || c->n_items < 1 || !c->item_in || !c->item_out)
+    return fail(KK_ERR_INVALID_ARG, "bad shape");
+  const bool affine = c->in_mode == IN_ADAIN_LEAKY || c->in_mode == IN_ADAIN_SNAKE;
+  if (affine && !coef) return fail(KK_ERR_INVALID_ARG, "AdaIN modes need coef");
+  if (c->in_mode == IN_ADAIN_SNAKE && !alpha) return fail(KK_ERR_INVALID_ARG, "Snake needs alpha");
+  if (c->out_mode == OUT_PLUS && (!sc || c->ldsc < c->cout)) return fail(KK_ERR_INVALID_ARG, "PLUS needs sc");
+  if (cudaSetDevice(cuda_ordinal) != cudaSuccess || !tc_available())
+    return fail(KK_ERR_CUDA, "no compute-capability-10 device");
+  cudaStream_t st = nullptr;
+  const long xrows = c->up2 ? (c->rows_in + 1) / 2 : c->rows_in;
+  DevBuf dx, dw, db, dcoef, dal, dsc, dy, dst, dii, dio, derr;
+  auto put = [&](DevBuf& b, const void* h, size_t n) -> bool {
+    if (cudaMalloc(&b.p, n) != cudaSuccess) return false;
+    return cudaMemcpy(b.p, h, n, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  bool ok = put(dx, x, sizeof(float) * xrows * c->ldx) && put(dy, y, sizeof(float) * (size_t)c->rows_out * c->ldy) &&
+            put(dii, c->item_in, sizeof(int) * c->rows_in) && put(dio, c->item_out, sizeof(int) * c->rows_out);
+  if (ok && bias) ok = put(db, bias, sizeof(float) * c->cout);
+  if (ok && affine) ok = put(dcoef, coef, sizeof(float) * 2 * (size_t)c->n_items * c->cin);
+  if (ok && alpha) ok = put(dal, alpha, sizeof(float) * c->cin);
+  if (ok && c->out_mode == OUT_PLUS) ok = put(dsc, sc, sizeof(float) * (size_t)c->rows_out * c->ldsc);
+  if (ok && stat) ok = cudaMalloc(&dst.p, sizeof(double) * 2 * (size_t)c->n_items * c->cout) == cudaSuccess &&
+                       cudaMemset(dst.p, 0, sizeof(double) * 2 * (size_t)c->n_items * c->cout) == cudaSuccess;
+  if (ok) ok = cudaMalloc(&derr.p, sizeof(int)) == cudaSuccess && cudaMemset(derr.p, 0, sizeof(int)) == cudaSuccess;
+  if (!ok) return fail(KK_ERR_OOM, "device allocation / copy failed");
+
+  TcWeights t;
+  cudaError_t e = tc_make_weights(w, c->cin, c->cout, c->K, &t);
+  if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+  DevBuf dimg;
+  dimg.p = t.w;
+
+  ConvArgs a;
+  memset(&a, 0, sizeof(a));
+  a.x = (const float*)dx.p, a.ldx = c->ldx, a.cin = c->cin, a.L_in = c->rows_in;
+  a.in_mode = c->in_mode, a.in_up2 = c->up2, a.slope = c->slope;
+  a.coef = (const float2*)dcoef.p, a.alpha = (const float*)dal.p;
+  a.din = Dom{(const int*)dii.p, 0, 0, 0, c->rows_in};
+  a.w = nullptr, a.bias = (const float*)db.p, a.cout = c->cout, a.K = c->K, a.dil = c->dil, a.pad = c->pad,
+  a.stride = 1;
+  a.y = (float*)dy.p, a.ldy = c->ldy, a.L_out = c->rows_out, a.out_mode = c->out_mode;
+  a.sc = (const float*)dsc.p, a.ldsc = c->ldsc, a.oscale = c->oscale;
+  a.stat = (double*)dst.p;
+  a.dout = Dom{(const int*)dio.p, 0, 0, 0, c->rows_out};
+  if (!tc_supported(a, t)) return fail(KK_ERR_INVALID_ARG, "shape not supported by the tcgen05 kernel");
+  e = tc_conv(a, t, (int*)derr.p, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+  int errh = 0;
+  if (cudaMemcpy(&errh, derr.p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(KK_ERR_CUDA, "error flag read failed");
+  if (errh) return fail(KK_ERR_TIMEOUT, "a tcgen05 pipeline wait timed out");
+  if (cudaMemcpy(y, dy.p, sizeof(float) * (size_t)c->rows_out * c->ldy, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(KK_ERR_CUDA, "output copy failed");
+  if (stat && cudaMemcpy(stat, dst.p, sizeof(double) * 2 * (size_t)c->n_items * c->cout, cudaMemcpyDeviceToHost) !=
+                  cudaSuccess)
+    return fail(KK_ERR_CUDA, "statistics copy failed");
+  return KK_OK;
+}

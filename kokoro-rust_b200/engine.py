@@ -50,8 +50,53 @@ _SIGS = {
     "kk_launch_count": (ctypes.c_int64, [_P]),
     "kk_last_times": (ctypes.c_int, [_P, _P]),
     "kk_profile_entry": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_int, _P, _P, _P]),
+    "kk_profile_launch": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_int, _P, _P, _P]),
     "kk_profile_reset": (None, [_P]),
+    "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_conv_selftest_error": (ctypes.c_char_p, []),
 }
+
+
+class ConvCase(ctypes.Structure):
+    """kk_conv_case of include/kokoro_b200.h."""
+    _fields_ = [("cin", ctypes.c_int), ("cout", ctypes.c_int), ("K", ctypes.c_int), ("dil", ctypes.c_int),
+                ("pad", ctypes.c_int), ("rows_in", ctypes.c_int), ("ldx", ctypes.c_int), ("up2", ctypes.c_int),
+                ("in_mode", ctypes.c_int), ("slope", ctypes.c_float), ("rows_out", ctypes.c_int),
+                ("ldy", ctypes.c_int), ("out_mode", ctypes.c_int), ("oscale", ctypes.c_float),
+                ("ldsc", ctypes.c_int), ("n_items", ctypes.c_int), ("item_in", _P), ("item_out", _P)]
+
+
+def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1, up2=0, in_mode=0,
+                  slope=0.2, out_mode=0, oscale=1.0, bias=None, coef=None, alpha=None, sc=None, y=None,
+                  n_items=None, want_stats=False):
+    """One convolution through the tcgen05 kernel (kk_conv_selftest). x [rows][ldx] f32, w torch
+    layout [cout][cin][K]; returns y [rows_out][ldy] (and [n_items][cout][2] statistics)."""
+    lib = load_library()
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    cout, cin, K = w.shape
+    item_in = np.ascontiguousarray(item_in, np.int32)
+    item_out = np.ascontiguousarray(item_out, np.int32)
+    n_items = int(n_items if n_items is not None else max(item_in.max(), item_out.max()) + 1)
+    y = np.ascontiguousarray(np.zeros((rows_out, cout), np.float32) if y is None else y, np.float32)
+    c = ConvCase(cin, cout, K, dil, pad, len(item_in), x.shape[1], up2, in_mode, slope, rows_out, y.shape[1],
+                 out_mode, oscale, 0 if sc is None else sc.shape[1], n_items,
+                 item_in.ctypes.data, item_out.ctypes.data)
+    keep = []
+
+    def ptr(a):
+        if a is None:
+            return None
+        a = np.ascontiguousarray(a, np.float32)
+        keep.append(a)
+        return a.ctypes.data
+    stat = np.zeros((n_items, cout, 2), np.float64) if want_stats else None
+    st = lib.kk_conv_selftest(ordinal, ctypes.byref(c), x.ctypes.data, w.ctypes.data, ptr(bias), ptr(coef),
+                              ptr(alpha), ptr(sc), y.ctypes.data, None if stat is None else stat.ctypes.data)
+    if st != KK_OK:
+        raise KokoroError(st, lib.kk_conv_selftest_error().decode())
+    return (y, stat) if want_stats else y
+
 
 _lib = None
 
@@ -162,6 +207,18 @@ class GpuKokoro:
             la, ms, fl = ctypes.c_int64(), ctypes.c_double(), ctypes.c_double()
             self.lib.kk_profile_entry(self.h, i, name, 64, ctypes.byref(la), ctypes.byref(ms), ctypes.byref(fl))
             res[name.value.decode()] = (int(la.value), float(ms.value), float(fl.value))
+        return res
+
+    def profile_launches(self) -> List[tuple]:
+        """[(class, device ms, algorithmic FLOPs, algorithmic bytes)] per launch profiled since the
+        last reset."""
+        n = self.lib.kk_profile_launch(self.h, -1, None, 0, None, None, None)
+        res = []
+        name = ctypes.create_string_buffer(64)
+        ms, fl, by = ctypes.c_double(), ctypes.c_double(), ctypes.c_double()
+        for i in range(max(n, 0)):
+            self.lib.kk_profile_launch(self.h, i, name, 64, ctypes.byref(ms), ctypes.byref(fl), ctypes.byref(by))
+            res.append((name.value.decode(), float(ms.value), float(fl.value), float(by.value)))
         return res
 
     def profile_reset(self):
