@@ -184,8 +184,13 @@ KK_API void kk_profile_reset(kk_engine* e);
  *  coef   [n_items][cin] (A, B) pairs, AdaIN folded to x * A + B (in_mode 2 and 3)
  *  alpha  [cin] Snake alpha (in_mode 3)
  *  sc     [rows_out][ldsc] shortcut rows (out_mode 2)
- *  y      [rows_out][ldy] in/out (read for out_mode 1)
+ *  y      [rows_out][ldy] in/out (read for out_mode 1); x, y and sc need 16-byte aligned rows
+ *         (row strides a multiple of 4 floats); columns cout .. round_up(cout, 4) - 1 of y may be
+ *         overwritten (the kernel writes whole 16-byte units)
  *  stat   NULL, or [n_items][cout][2] f64: per (item, channel) sum and sum of squares of y
+ *  timing_iters, ms_per_iter   when timing_iters > 0: the launch is repeated that many times more
+ *         on the same device buffers and the mean device time per launch (CUDA events on the
+ *         launching stream) is written to *ms_per_iter; y and stat then hold the repeated result
  */
 typedef struct kk_conv_case {
   int cin, cout, K, dil, pad;
@@ -204,7 +209,7 @@ typedef struct kk_conv_case {
 } kk_conv_case;
 KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x, const float* w,
                                   const float* bias, const float* coef, const float* alpha, const float* sc,
-                                  float* y, double* stat);
+                                  float* y, double* stat, int timing_iters, double* ms_per_iter);
 /* Message of the last kk_conv_selftest failure on this thread. */
 KK_API const char* kk_conv_selftest_error(void);
 

@@ -240,6 +240,11 @@ static const int DILS[3] = {1, 3, 5};
 // [x | asr_res | f0 | n] (1090 channels).
 static const int X0_LD = 516;
 static const int CAT_LD = 1092;
+// Row strides of the spectrum (22 channels) and of conv_post's output (22 channels), padded to
+// 16 bytes so the tensor-core convolutions can move them with TMA.
+static const int SPEC_LD = 24;
+static const int POST_LD = 24;
+static inline int ld16(int c) { return (c + 3) & ~3; }  // row stride of a c-channel f32 buffer
 
 struct Engine {
   int dev = 0;
@@ -641,18 +646,20 @@ void Engine::load(const Checkpoint& ck) {
   m.noise0 = load_conv(ck, g + ".noise_convs.0", 22, 256, 12, 1, 3, 6, true);
   if (precision == KK_PRECISION_BF16 && tc_ok) {
     // Conv1d(22 -> 256, k12, stride 6, pad 3) over the spectrum rows equals a 2-tap stride-1 conv
-    // over "6-frame rows" X'[q] = spec rows 6q-3 .. 6q+2 (132 channels: frame j, channel c at
-    // j*22 + c): y[o] = W'_0 X'[o] + W'_1 X'[o+1] with W'_m[co][j*22 + c] = W[co][c][6m + j].
-    // With 3 zero rows ahead of the spectrum, X' is a plain strided view (row stride 132 floats).
+    // over "6-frame rows" X'[q] = spec rows 6q-3 .. 6q+2 (6 * SPEC_LD channels: frame j, channel c
+    // at j * SPEC_LD + c; the 2 padding channels of each frame are zero in the spectrum and get zero
+    // weights): y[o] = W'_0 X'[o] + W'_1 X'[o+1] with W'_m[co][j * SPEC_LD + c] = W[co][c][6m + j].
+    // With 3 zero rows ahead of the spectrum, X' is a plain strided view (row stride 6 * SPEC_LD).
     auto w = ck.conv_weight(g + ".noise_convs.0", {256, 22, 12});
     auto b = ck.get(g + ".noise_convs.0.bias", {256});
-    std::vector<float> w2((size_t)256 * 132 * 2);
+    const int cv = 6 * SPEC_LD;
+    std::vector<float> w2((size_t)256 * cv * 2, 0.0f);
     for (int co = 0; co < 256; co++)
       for (int mm = 0; mm < 2; mm++)
         for (int j = 0; j < 6; j++)
           for (int c = 0; c < 22; c++)
-            w2[((size_t)co * 132 + j * 22 + c) * 2 + mm] = w[((size_t)co * 22 + c) * 12 + 6 * mm + j];
-    m.noise0_rows = conv_from(w2, b.data(), 132, 256, 2, 1, 0, 1);
+            w2[((size_t)co * cv + j * SPEC_LD + c) * 2 + mm] = w[((size_t)co * 22 + c) * 12 + 6 * mm + j];
+    m.noise0_rows = conv_from(w2, b.data(), cv, 256, 2, 1, 0, 1);
     m.noise0_rows.macs_per_row = (double)22 * 256 * 12;
   }
   m.noise1 = load_conv(ck, g + ".noise_convs.1", 22, 128, 1, 1, 0, 1, true);
@@ -852,12 +859,13 @@ void Engine::resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, co
   float* h = ar.get<float>((size_t)dout.L * R.dout);
   ConvArgs a = ca(R.c1);
   if (R.up) {
-    float* p = ar.get<float>((size_t)dout.L * R.din);
+    const int ldp = ld16(R.din);
+    float* p = ar.get<float>((size_t)dout.L * ldp);
     ConvArgs pro = ca(R.c1);
     pro.x = x, pro.ldx = ldx, pro.cin = R.din, pro.din = din;
     adain_args(pro, R.n1, m1, r1, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
-    check(launch_adain_pool(x, R.din, din.L, pro, R.pool_w, R.pool_b, p, st), "adain_pool");
-    a.x = p, a.ldx = R.din, a.in_mode = IN_MASK, a.din = dout, a.L_in = dout.L;
+    check(launch_adain_pool(x, R.din, din.L, pro, R.pool_w, R.pool_b, p, ldp, st), "adain_pool");
+    a.x = p, a.ldx = ldp, a.in_mode = IN_MASK, a.din = dout, a.L_in = dout.L;
   } else {
     a.x = x, a.ldx = ldx, a.din = din, a.L_in = din.L;
     adain_args(a, R.n1, m1, r1, gb, ldgb, IN_ADAIN_LEAKY, 0.2f, nullptr);
@@ -1012,13 +1020,13 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   check(launch_har_source(f0, pp, L2, items, col_item_n, LN, seeds_d, noise_d, noise_off_d, m.lw, m.lb, har, st),
         "har_source");
   // spectrum rows with 3 zero rows in front and 8 behind (the 6-frame-row view of noise_convs.0)
-  float* spec_pad = ar.get<float>((size_t)(L120 + 11) * 22);
-  float* spec = spec_pad + 3 * 22;
-  KK_CUDA(cudaMemsetAsync(spec_pad, 0, sizeof(float) * 3 * 22, st));
-  KK_CUDA(cudaMemsetAsync(spec + (size_t)L120 * 22, 0, sizeof(float) * 8 * 22, st));
-  check(launch_stft(har, items, d120, spec, 22, st), "stft");
+  float* spec_pad = ar.get<float>((size_t)(L120 + 11) * SPEC_LD);
+  float* spec = spec_pad + 3 * SPEC_LD;
+  KK_CUDA(cudaMemsetAsync(spec_pad, 0, sizeof(float) * 3 * SPEC_LD, st));
+  KK_CUDA(cudaMemsetAsync(spec + (size_t)L120 * SPEC_LD, 0, sizeof(float) * 8 * SPEC_LD, st));
+  check(launch_stft(har, items, d120, spec, SPEC_LD, st), "stft");
   dump("har", har, 600LL * LN, 1, 1);
-  dump("spec", spec, L120, 22, 22);
+  dump("spec", spec, L120, 22, SPEC_LD);
   stage_sync("source");
   // ---- generator stage 0 (2N -> 20N, C 256)
   float* y0 = ar.get<float>((size_t)L20 * 256);
@@ -1030,11 +1038,13 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     if (m.noise0_rows.w) {
       // gap rows of the spectrum are zero (stft), so the 6-frame-row view needs no masking
       ConvArgs a = ca(m.noise0_rows);
-      a.x = spec_pad, a.ldx = 132, a.in_mode = IN_NOMASK, a.L_in = L20 + 1, a.y = xs, a.ldy = 256, a.L_out = L20;
+      a.x = spec_pad, a.ldx = 6 * SPEC_LD, a.in_mode = IN_NOMASK, a.L_in = L20 + 1, a.y = xs, a.ldy = 256,
+      a.L_out = L20;
       run_conv(m.noise0_rows, a);
     } else {
       ConvArgs a = ca(m.noise0);
-      a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256, a.L_out = L20;
+      a.x = spec, a.ldx = SPEC_LD, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256,
+      a.L_out = L20;
       run_conv(m.noise0, a);
     }
     snake(m.noise_res[0], xs, xsr, d20, gb_dec, ldgb, items, B, max_n);
@@ -1065,7 +1075,8 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     float* xs = ar.get<float>((size_t)L120 * 128);
     float* xsr = ar.get<float>((size_t)L120 * 128);
     ConvArgs a = ca(m.noise1);
-    a.x = spec, a.ldx = 22, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 128, a.L_out = L120;
+    a.x = spec, a.ldx = SPEC_LD, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 128,
+    a.L_out = L120;
     run_conv(m.noise1, a);
     snake(m.noise_res[1], xs, xsr, d120, gb_dec, ldgb, items, B, max_n);
     float* u1 = xs;  // noise-conv output no longer needed
@@ -1088,17 +1099,17 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   }
   stage_sync("generator stage 1");
   // ---- conv_post + iSTFT
-  float* post = ar.get<float>((size_t)L120 * 22);
+  float* post = ar.get<float>((size_t)L120 * POST_LD);
   {
     ConvArgs a = ca(m.post);
     a.x = x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
-    a.y = post, a.ldy = 22, a.L_out = L120;
+    a.y = post, a.ldy = POST_LD, a.L_out = L120;
     run_conv(m.post, a);
   }
   float* audio = ar.get<float>((size_t)600 * LN);
-  check(launch_istft(post, 22, items, d120, col_item_n, LN, audio, st), "istft");
+  check(launch_istft(post, POST_LD, items, d120, col_item_n, LN, audio, st), "istft");
   times_compute_end();
-  dump("post", post, L120, 22, 22);
+  dump("post", post, L120, 22, POST_LD);
   dump("audio", audio, 600LL * LN, 1, 1);
   stage_sync("istft");
   return audio;

@@ -536,7 +536,8 @@ __device__ __forceinline__ float pool_in(const ConvArgs& p, const float* x, int 
   return prologue(p, x[(long)i * p.ldx + c], b, c);
 }
 
-__global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, const float* pw, const float* pb, float* y) {
+__global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, const float* pw, const float* pb, float* y,
+                                  int ldy) {
   long idx = blockIdx.x * (long)blockDim.x + threadIdx.x;
   if (idx >= 2L * L * C) return;
   int o = (int)(idx / C), c = (int)(idx % C);
@@ -547,13 +548,13 @@ __global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, cons
     acc = fmaf(pw[c * 3 + 2], pool_in(p, x, L, (o - 1) >> 1, c), acc);
     acc = fmaf(pw[c * 3 + 0], pool_in(p, x, L, (o + 1) >> 1, c), acc);
   }
-  y[idx] = acc;
+  y[(long)o * ldy + c] = acc;
 }
 
 cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw, const float* pb,
-                              float* y, cudaStream_t st) {
+                              float* y, int ldy, cudaStream_t st) {
   long n = 2L * L * C;
-  adain_pool_kernel<<<nblk(n, 256), 256, 0, st>>>(x, C, L, pro, pw, pb, y);
+  adain_pool_kernel<<<nblk(n, 256), 256, 0, st>>>(x, C, L, pro, pw, pb, y, ldy);
   return cudaGetLastError();
 }
 
@@ -757,6 +758,7 @@ __global__ void stft_kernel(const float* har, const ItemTab* items, Dom d120, fl
   int R = blockIdx.x * blockDim.x + threadIdx.x;
   if (R >= d120.L) return;
   float* out = spec + (long)R * lds;
+  for (int k = 22; k < lds; k++) out[k] = 0.0f;  // row padding (read by the 6-frame-row view)
   int b = dom_item(d120, R);
   if (b < 0) {
     for (int k = 0; k < 22; k++) out[k] = 0.0f;

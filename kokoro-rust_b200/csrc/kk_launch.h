@@ -85,9 +85,9 @@ cudaError_t launch_adain_coef(const float* mean, const float* rstd, const float*
                               const float* gb, int ldgb, int B, int C, float2* coef, cudaStream_t st);
 
 // AdaIN + leaky ReLU (0.2) followed by the depthwise ConvTranspose1d(k3, s2, p1, op1) "pool"
-// (adain_apply_seg + dw_convT_k3s2, kernels/kokoro.cu:152-167, 317-334): x [L][C] -> y [2L][C]
+// (adain_apply_seg + dw_convT_k3s2, kernels/kokoro.cu:152-167, 317-334): x [L][C] -> y [2L][ldy]
 cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw,
-                              const float* pb, float* y, cudaStream_t st);
+                              const float* pb, float* y, int ldy, cudaStream_t st);
 
 // durations_from_logits (src/model.rs:90-99) per token row: dur = max(1, rne(sum sigmoid / speed))
 cudaError_t launch_durations(const float* logits, int ldl, const int* row_item, const float* speed,

@@ -2,6 +2,8 @@
 // kernel can be checked on its own against an fp32 reference (every prologue / epilogue mode, odd
 // channel counts, ragged item layouts). Not part of the model path.
 #include <cuda_runtime.h>
+#include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 #include <string>
 #include <vector>
@@ -32,7 +34,8 @@ extern "C" KK_API const char* kk_conv_selftest_error(void) { return g_selftest_e
 
 extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x,
                                              const float* w, const float* bias, const float* coef,
-                                             const float* alpha, const float* sc, float* y, double* stat) {
+                                             const float* alpha, const float* sc, float* y, double* stat,
+                                             int timing_iters, double* ms_per_iter) {
   using namespace kk;
   if (!c || !x || !w || !y) return fail(KK_ERR_INVALID_ARG, "null argument");
   if (c->cin < 1 || c->cout < 1 || c->K < 1 || c->dil < 1 || c->rows_in < 1 || c->rows_out < 1 ||
@@ -81,9 +84,39 @@ extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_cas
   a.stat = (double*)dst.p;
   a.dout = Dom{(const int*)dio.p, 0, 0, 0, c->rows_out};
   if (!tc_supported(a, t)) return fail(KK_ERR_INVALID_ARG, "shape not supported by the tcgen05 kernel");
-  e = tc_conv(a, t, (int*)derr.p, st);
+  // KK_TC_TRACE=1 (diagnostics): per-role cycle accounting of CTA 0, printed to stderr
+  DevBuf dtr;
+  if (getenv("KK_TC_TRACE") && cudaMalloc(&dtr.p, 16 * sizeof(unsigned long long)) == cudaSuccess)
+    cudaMemset(dtr.p, 0, 16 * sizeof(unsigned long long));
+  e = tc_conv(a, t, (int*)derr.p, st, (unsigned long long*)dtr.p);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+  if (dtr.p) {
+    unsigned long long h[16];
+    if (cudaMemcpy(h, dtr.p, sizeof(h), cudaMemcpyDeviceToHost) == cudaSuccess) {
+      fprintf(stderr, "tc_trace K=%d dil=%d cin=%d cout=%d L=%d in=%d out=%d |", a.K, a.dil, a.cin, a.cout, a.L_out,
+              a.in_mode, a.out_mode);
+      for (int i = 0; i < 16; i++) fprintf(stderr, " %llu", h[i]);
+      fprintf(stderr, "\n");
+    }
+  }
+  if (timing_iters > 0 && ms_per_iter) {
+    // repeated launches on the same buffers (out_mode 1 keeps accumulating; the first result is
+    // the one returned below only when timing_iters == 0)
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaEventRecord(e0, st);
+    for (int i = 0; i < timing_iters && e == cudaSuccess; i++) e = tc_conv(a, t, (int*)derr.p, st);
+    cudaEventRecord(e1, st);
+    if (e == cudaSuccess) e = cudaEventSynchronize(e1);
+    float ms = 0;
+    cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+    *ms_per_iter = ms / timing_iters;
+  }
   int errh = 0;
   if (cudaMemcpy(&errh, derr.p, sizeof(int), cudaMemcpyDeviceToHost) != cudaSuccess)
     return fail(KK_ERR_CUDA, "error flag read failed");

@@ -5,25 +5,31 @@
 //   A_k,cb[co, ci] (weights, bf16, K-major)  x  B_k,cb[t, ci] (activations, bf16, K-major)
 // issued as tcgen05.mma.cta_group::1.kind::f16 with M = 128, N = 256, K = 16.
 //
-// Operand staging (no tensor maps, no swizzle; canonical no-swizzle K-major layout of 8-row x
-// 16-byte core matrices):
+// Operand staging (canonical no-swizzle K-major layout of 8-row x 16-byte core matrices):
 //  * weights: a load-time image of 16 KB blocks [co tile][cb][tap], each block laid out exactly as
 //    its shared-memory operand (LBO 2048 B between 8-channel chunks, SBO 128 B between 8-row
-//    groups), streamed with one cp.async.bulk per block into a 4-stage ring;
-//  * activations: 8 producer warps read the f32 input rows of the tile's window
-//    [t0 - pad, t0 + 256 + (K-1)*dil - pad), apply the layer's prologue (gap masking,
-//    AdaIN + leaky ReLU, AdaIN + Snake, leaky ReLU, nearest x2 upsample) and store bf16 in a
-//    time-contiguous layout: chunk j (8 channels) holds all window rows at 16 B per row. Because
-//    the rows of a chunk are contiguous, the B operand of tap k is the same window with its start
-//    address moved by k * dil rows: the window is staged once per channel block and reused by every
-//    tap (this is the implicit GEMM; no im2col, no per-tap reload).
-//  * accumulators: two 256-column TMEM buffers, so the epilogue (4 warps, tcgen05.ld 32x32b) of one
-//    tile overlaps the MMAs of the next; the epilogue applies bias / residual / shortcut / gelu and
-//    writes time-major f32 rows (32 lanes = 32 consecutive channels: coalesced 128-byte stores).
+//    groups), streamed with one cp.async.bulk per block into a 3-stage ring;
+//  * input rows: a loader warp streams the f32 rows of each tile's window
+//    [t0 - pad, t0 + 256 + (K-1)*dil - pad) with TMA tensor loads (boxes of 32 rows x 64 channels,
+//    8 KB; rows and channels outside the tensor read as zero) into a ring of up to 6 stages, so
+//    HBM latency is covered by the ring depth rather than by registers;
+//  * activations: 4 producer warps read the boxes from shared memory, apply the layer's prologue
+//    (gap masking, AdaIN + leaky ReLU, AdaIN + Snake, leaky ReLU, nearest x2 upsample) and store
+//    bf16 in a time-contiguous layout: chunk j (8 channels) holds all window rows at 16 B per row.
+//    Because the rows of a chunk are contiguous, the B operand of tap k is the same window with its
+//    start address moved by k * dil rows: the window is staged once per channel block and reused by
+//    every tap (implicit GEMM; no im2col, no per-tap reload). Within a 64-channel block, chunk j
+//    holds channels 4j..4j+3 and 32+4j..32+4j+3 (the weight image uses the same order), so the 8
+//    lanes that convert one box row read 128 contiguous bytes (no bank conflicts);
+//  * accumulators: two 256-column TMEM buffers, so the epilogue of one tile overlaps the MMAs of
+//    the next. 8 epilogue warps (two per TMEM lane quarter, each owning 128 of the tile's 256 time
+//    rows) apply bias / residual / shortcut / gelu and the fused AdaIN statistics, stage 16-row x
+//    32-channel boxes in shared memory and write them with TMA tensor stores; residual rows arrive
+//    by TMA tensor loads two boxes ahead.
 //
-// Warp roles (14 warps): 0 weight loader + TMEM owner, 1 MMA issuer (one elected lane), 2-5
-// epilogue, 6-13 activation producers. Persistent CTAs walk the tiles in time-fastest order so
-// the CTAs running together share one co tile's weights in L2.
+// Warp roles (20 warps): 0 weight loader + TMEM owner, 1 MMA issuer (one elected lane), 2 input
+// loader, 3 idle, 4-11 epilogue, 12-19 activation producers. Persistent CTAs walk the tiles in
+// time-fastest order so the CTAs running together share one co tile's weights in L2.
 //
 // Every mbarrier wait is bounded (1 s of %globaltimer): on expiry the CTA records the failure in
 // the engine's error flag, drains its own bulk copies (bounded), releases its TMEM and returns.
@@ -40,16 +46,24 @@ namespace kk {
 constexpr int TC_M = 128;
 constexpr int TC_N = 256;
 constexpr int TC_KB = 64;
-constexpr int TC_WST = 3;
-constexpr int TC_XST_MAX = 4;  // activation-window ring stages (3 when shared memory allows)
+constexpr int TC_WST = 3;                        // weight ring stages
+constexpr int TC_XST = 2;                        // activation-window stages
+constexpr int TC_RST_MAX = 6;                    // input-box ring stages (fewer when shared memory is short)
+constexpr int TC_BOX_ROWS = 32;
+constexpr int TC_INBOX = TC_BOX_ROWS * TC_KB * 4;  // 8 KB f32 input box
 constexpr int TC_MAX_WIN = 512;
-constexpr int TC_EC = 16;                       // epilogue chunk: 16 time rows x 32 channels per warp
-constexpr int TC_RES_DEPTH = 4;                 // residual chunks in flight per epilogue warp
-constexpr int TC_EBOX = TC_EC * 32 * 4;         // 2 KB: one warp's chunk (TMA box 32 channels x 16 rows)
+constexpr int TC_EC = 16;                        // epilogue chunk: 16 time rows x 32 channels per warp
+constexpr int TC_RES_DEPTH = 2;                  // residual chunks in flight per epilogue warp
+constexpr int TC_EBOX = TC_EC * 32 * 4;          // 2 KB: one warp's chunk (TMA box 32 channels x 16 rows)
+constexpr int TC_NEPI = 8;                       // epilogue warps
+constexpr int TC_NPROD = 8;                      // producer warps
+constexpr int TC_PROWS = TC_NPROD * 32 / 8;      // box rows converted at once (8 lanes per row)
+constexpr int TC_EROWS = TC_N / 2;               // time rows per epilogue warp
 // per epilogue warp: 2 staging chunks, TC_RES_DEPTH residual chunks, the item of each output row
-constexpr int TC_EPI_WARP_BYTES = 2 * TC_EBOX + TC_RES_DEPTH * TC_EBOX + 256 * 4;
-constexpr int TC_THREADS = 448;
-constexpr int TC_WBLOCK = TC_M * TC_KB * 2;  // 16 KB weight block
+constexpr int TC_EPI_WARP_BYTES = 2 * TC_EBOX + TC_RES_DEPTH * TC_EBOX + TC_EROWS * 4;
+constexpr int TC_THREADS = (4 + TC_NEPI + TC_NPROD) * 32;
+constexpr int TC_WBLOCK = TC_M * TC_KB * 2;      // 16 KB weight block
+constexpr int TC_SMEM_MAX = 227 * 1024;
 constexpr unsigned long long TC_TIMEOUT_NS = 1000000000ull;
 
 // ------------------------------------------------------------------------------ PTX wrappers
@@ -82,12 +96,26 @@ __device__ __forceinline__ bool mbar_try(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps in hardware until
+// the phase completes or about 0.5 ms pass, instead of spinning and taking issue slots from the
+// warps that do the work.
+__device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(b)), "r"(parity), "r"(500000u)
+      : "memory");
+  return ok != 0;
+}
 // Bounded wait: returns false (and raises the CTA abort flag + engine error flag) on expiry.
 __device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = tc_now();
   while (true) {
-    if (mbar_try(b, parity)) return true;
+    if (mbar_try_sleep(b, parity)) return true;
     if (*abort_flag) return false;
     if (tc_now() - t0 > TC_TIMEOUT_NS) {
       *abort_flag = 1;
@@ -202,9 +230,9 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 // ------------------------------------------------------------------------------ kernel
 
 struct TcArgs {
-  CUtensorMap ymap;   // output rows [L_out][cout] f32 (row stride ldy), box 128 channels x 16 rows
+  CUtensorMap xmap;   // input rows [L_x][cin] f32 (row stride ldx), box 64 channels x 32 rows
+  CUtensorMap ymap;   // output rows [L_out][cout] f32 (row stride ldy), box 32 channels x 16 rows
   CUtensorMap rmap;   // residual rows (y for OUT_ADD, sc for OUT_PLUS), same box
-  int tma_out;        // 1: epilogue writes through shared memory + TMA (16-byte aligned row stride)
   ConvArgs a;
   const __nv_bfloat16* wimg;
   int ncb;        // input-channel blocks of 64
@@ -212,7 +240,7 @@ struct TcArgs {
   int n_tt;       // time tiles of 256
   int win_rows;   // 256 + (K - 1) * dil
   int win_pad;    // window rows rounded to 8, + 1 (bank-conflict-free producer stores)
-  int xst;        // activation-window ring stages
+  int rst;        // input-box ring stages
   int* err;
   unsigned long long* trace;  // optional cycle accounting of CTA 0 (diagnostics), 16 counters
 };
@@ -221,28 +249,52 @@ struct TcArgs {
 enum TcTrace : int {
   TR_MMA_WAIT_ACC = 0, TR_MMA_WAIT_X = 1, TR_MMA_WAIT_W = 2, TR_MMA_TOTAL = 3,
   TR_LD_WAIT_W = 4, TR_LD_TOTAL = 5,
-  TR_PR_WAIT_X = 6, TR_PR_WORK = 7, TR_PR_ITEM = 8,
+  TR_PR_WAIT_X = 6, TR_PR_WORK = 7, TR_PR_WAIT_IN = 8,
   TR_EP_WAIT = 9, TR_EP_WORK = 10, TR_TILES = 11,
-  TR_EP_TMEM = 12, TR_EP_RES = 13, TR_EP_STBUF = 14, TR_EP_STATS = 15
+  TR_IN_WAIT = 12, TR_IN_TOTAL = 13, TR_EP_RES = 14, TR_EP_STBUF = 15
 };
 
+// First and last input row (of the tensor x) of a tile's window, and the number of input boxes.
+struct InSpan {
+  int base, xr0, nbox;
+};
+__device__ __forceinline__ InSpan in_span(const TcArgs& p, int tile, int up2) {
+  InSpan s;
+  s.base = (tile % p.n_tt) * TC_N - p.a.pad;
+  const int last = s.base + p.win_rows - 1;
+  s.xr0 = up2 ? (s.base >> 1) : s.base;
+  const int xr1 = up2 ? (last >> 1) : last;
+  s.nbox = (xr1 - s.xr0) / TC_BOX_ROWS + 1;
+  return s;
+}
+
+// IM / UP / OM: the layer's input mode, nearest x2 upsample and output mode as compile-time
+// constants (branch-free producer and epilogue loops); IM = -1 is the generic instance that reads
+// all three from the arguments.
+template <int IM, int UP, int OM>
 __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_constant__ TcArgs p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   const ConvArgs& a = p.a;
-  uint8_t* wbuf = smem;                                       // TC_WST x 16 KB
+  const int in_mode = IM >= 0 ? IM : a.in_mode;
+  const int in_up2 = IM >= 0 ? UP : a.in_up2;
+  const int out_mode_k = IM >= 0 ? OM : a.out_mode;
   const uint32_t xbytes = 8u * p.win_pad * 16u;
-  const int XST = p.xst;
-  uint8_t* xbuf = smem + TC_WST * TC_WBLOCK;                  // XST x xbytes
-  uint8_t* epi = xbuf + XST * xbytes;                         // 4 x TC_EPI_WARP_BYTES (epilogue warps)
-  uint64_t* bars = (uint64_t*)(epi + 4 * TC_EPI_WARP_BYTES);
+  const int RST = p.rst;
+  uint8_t* wbuf = smem;                                       // TC_WST x 16 KB
+  uint8_t* xbuf = wbuf + TC_WST * TC_WBLOCK;                  // TC_XST x xbytes
+  uint8_t* inring = xbuf + TC_XST * xbytes;                   // RST x 8 KB
+  uint8_t* epi = inring + RST * TC_INBOX;                     // TC_NEPI x TC_EPI_WARP_BYTES
+  uint64_t* bars = (uint64_t*)(epi + TC_NEPI * TC_EPI_WARP_BYTES);
   uint64_t* w_full = bars;
-  uint64_t* w_empty = bars + TC_WST;
-  uint64_t* x_full = bars + 2 * TC_WST;
-  uint64_t* x_empty = x_full + TC_XST_MAX;
-  uint64_t* acc_full = x_empty + TC_XST_MAX;
+  uint64_t* w_empty = w_full + TC_WST;
+  uint64_t* in_full = w_empty + TC_WST;
+  uint64_t* in_empty = in_full + TC_RST_MAX;
+  uint64_t* x_full = in_empty + TC_RST_MAX;
+  uint64_t* x_empty = x_full + TC_XST;
+  uint64_t* acc_full = x_empty + TC_XST;
   uint64_t* acc_empty = acc_full + 2;
-  uint64_t* res_full = acc_empty + 2;                         // [4 warps][TC_RES_DEPTH]
-  uint32_t* tmem_slot = (uint32_t*)(res_full + 4 * TC_RES_DEPTH);
+  uint64_t* res_full = acc_empty + 2;                         // [TC_NEPI][TC_RES_DEPTH]
+  uint32_t* tmem_slot = (uint32_t*)(res_full + TC_NEPI * TC_RES_DEPTH);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   int* ritem = (int*)(tmem_slot + 4);                         // item of each window row (producers)
 
@@ -255,15 +307,19 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       mbar_init(&w_full[i], 1);
       mbar_init(&w_empty[i], 1);
     }
-    for (int i = 0; i < XST; i++) {
-      mbar_init(&x_full[i], 8);
+    for (int i = 0; i < RST; i++) {
+      mbar_init(&in_full[i], 1);
+      mbar_init(&in_empty[i], TC_NPROD);
+    }
+    for (int i = 0; i < TC_XST; i++) {
+      mbar_init(&x_full[i], TC_NPROD);
       mbar_init(&x_empty[i], 1);
     }
     for (int i = 0; i < 2; i++) {
       mbar_init(&acc_full[i], 1);
-      mbar_init(&acc_empty[i], 4);
+      mbar_init(&acc_empty[i], TC_NEPI);
     }
-    for (int i = 0; i < 4 * TC_RES_DEPTH; i++) mbar_init(&res_full[i], 1);
+    for (int i = 0; i < TC_NEPI * TC_RES_DEPTH; i++) mbar_init(&res_full[i], 1);
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -322,8 +378,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         const uint32_t d = tmem + ab * TC_N;
         bool ok = true;
         for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
-          const int xs = xit % XST;
-          if (!mbar_wait_t(&x_full[xs], (xit / XST) & 1, abort_flag, p.err, trc ? &twx : nullptr)) {
+          const int xs = xit % TC_XST;
+          if (!mbar_wait_t(&x_full[xs], (xit / TC_XST) & 1, abort_flag, p.err, trc ? &twx : nullptr)) {
             ok = false;
             break;
           }
@@ -359,53 +415,96 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         p.trace[TR_TILES] = lt;
       }
     }
-  } else if (warp < 6) {
+  } else if (warp == 2) {
+    // ---------------------------------------------------------------- input loader
+    if (lane == 0) {
+      unsigned long long tw = 0;
+      unsigned long long* tr = (p.trace && blockIdx.x == 0) ? &tw : nullptr;
+      const long long t_start = clock64();
+      uint32_t it = 0;
+      int sl = 0;
+      uint32_t ph = 0;  // ring slot and phase parity of box `it`
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const InSpan sp = in_span(p, tile, in_up2);
+        for (int cb = 0; cb < p.ncb && ok; cb++)
+          for (int i = 0; i < sp.nbox; i++, it++) {
+            if (!mbar_wait_t(&in_empty[sl], ph ^ 1, abort_flag, p.err, tr)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(&in_full[sl], TC_INBOX);
+            tma_load_2d(inring + sl * TC_INBOX, &p.xmap, cb * TC_KB, sp.xr0 + i * TC_BOX_ROWS, &in_full[sl]);
+            if (++sl == RST) sl = 0, ph ^= 1;
+          }
+      }
+      if (tr) {
+        p.trace[TR_IN_WAIT] = tw;
+        p.trace[TR_IN_TOTAL] = (unsigned long long)(clock64() - t_start);
+      }
+      if (*abort_flag) {
+        const uint32_t first = it > (uint32_t)RST ? it - RST : 0;
+        for (uint32_t j = first; j < it; j++) {
+          const unsigned long long t0 = tc_now();
+          while (!mbar_try(&in_full[j % RST], (j / RST) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+          }
+        }
+      }
+    }
+  } else if (warp >= 4 && warp < 4 + TC_NEPI) {
     // ---------------------------------------------------------------- epilogue
-    // Each of the 4 epilogue warps owns the 32 channels of its TMEM lane quarter end to end: its
-    // own staging chunks, TMA store boxes (32 channels x 16 rows), residual ring and row-item
-    // table, so the warps never wait for one another.
-    const int q = warp & 3;  // TMEM lane quarter this warp may access
-    const int ew = warp - 2;
+    // Warp ew owns the 32 channels of TMEM lane quarter q = warp % 4 for time rows
+    // [hrow, hrow + 128) of each tile, end to end: its own staging chunks, TMA store boxes
+    // (32 channels x 16 rows), residual ring and row-item table, so the warps never wait for one
+    // another. When all 128 rows belong to one item (the common case: items span thousands of
+    // rows in the frame domains) the statistics accumulate in registers for the whole tile.
+    const int ew = warp - 4;
+    const int q = warp & 3;
+    const int hrow = (ew >> 2) * TC_EROWS;
     float* stg = (float*)(epi + ew * TC_EPI_WARP_BYTES);         // [2][16][32]
     float* rsb = stg + 2 * TC_EC * 32;                            // [TC_RES_DEPTH][16][32]
-    int* eit = (int*)(rsb + TC_RES_DEPTH * TC_EC * 32);           // [256]
+    int* eit = (int*)(rsb + TC_RES_DEPTH * TC_EC * 32);           // [128]
     uint64_t* rbar = res_full + ew * TC_RES_DEPTH;
-    const bool trc = p.trace && blockIdx.x == 0 && warp == 2 && lane == 0;
+    constexpr int NCH = TC_EROWS / TC_EC;
+    const bool trc = p.trace && blockIdx.x == 0 && ew == 0 && lane == 0;
     unsigned long long tew = 0;
-    long long t_tmem = 0, t_res = 0, t_stbuf = 0, t_stats = 0;
+    long long t_res = 0, t_stbuf = 0;
     const long long t_start = clock64();
     uint32_t rcons = 0, riss = 0;  // residual chunks consumed / issued by this warp
-    const int out_mode = a.out_mode, L_out = a.L_out;
-    const long ldy = a.ldy;
-    float* __restrict__ y = a.y;
+    const int out_mode = out_mode_k, L_out = a.L_out;
     const float oscale = a.oscale;
     const bool need_res = out_mode == OUT_ADD || out_mode == OUT_PLUS;
     double* const stat = a.stat;
     uint32_t lt = 0;
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
+    bool bad = false;
+    for (int tile = blockIdx.x; tile < ntiles && !bad; tile += gridDim.x, lt++) {
       const int ab = lt & 1;
       const int cot = tile / p.n_tt, tt = tile % p.n_tt;
       const int co0 = cot * TC_M + q * 32;
       const int co = co0 + lane;
-      const int t0 = tt * TC_N;
+      const int t0 = tt * TC_N + hrow;
       const bool co_ok = co < a.cout;
       const float bias = (co_ok && a.bias) ? a.bias[co] : 0.0f;
       // residual chunks of this tile start loading before the accumulator is ready
-      if (p.tma_out && need_res && lane == 0) {
+      if (need_res && lane == 0) {
         for (int c = 0; c < TC_RES_DEPTH; c++, riss++) {
           const int sl = riss % TC_RES_DEPTH;
           mbar_arrive_expect_tx(&rbar[sl], TC_EBOX);
           tma_load_2d(rsb + sl * TC_EC * 32, &p.rmap, co0, t0 + c * TC_EC, &rbar[sl]);
         }
       }
+      int s_item = -1;
+      bool single = false;
       if (stat) {
-        for (int rr = lane; rr < TC_N; rr += 32) {
+        for (int rr = lane; rr < TC_EROWS; rr += 32) {
           const int t = t0 + rr;
           eit[rr] = t < L_out ? dom_item(a.dout, t) : -1;
         }
         __syncwarp();
+        // item spans are contiguous runs, so equal end rows mean one item covers all 128 rows
+        single = eit[0] >= 0 && eit[0] == eit[TC_EROWS - 1];
+        if (single) s_item = eit[0];
       }
-      int s_item = -1;
       float s_sum = 0.0f, s_sq = 0.0f;
       auto s_flush = [&]() {
         if (s_item >= 0 && co_ok) {
@@ -416,136 +515,86 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         s_sum = 0.0f;
         s_sq = 0.0f;
       };
-      auto s_chunk = [&](int r0, const float* vals, int n) {  // statistics of rows r0 .. r0 + n - 1
-        const int b0 = eit[r0], b1 = eit[r0 + n - 1];
-        if (b0 == b1 && b0 >= 0) {  // one item spans the chunk (item spans are contiguous)
-          if (b0 != s_item) {
+      auto s_chunk = [&](int r0, const float* vals) {  // statistics of rows r0 .. r0 + TC_EC - 1
+        for (int jj = 0; jj < TC_EC; jj++) {
+          const int b = eit[r0 + jj];
+          if (b != s_item) {
             s_flush();
-            s_item = b0;
+            s_item = b;
           }
-          for (int jj = 0; jj < n; jj++) {
+          if (b >= 0) {
             s_sum += vals[jj];
             s_sq = fmaf(vals[jj], vals[jj], s_sq);
-          }
-        } else {
-          for (int jj = 0; jj < n; jj++) {
-            const int b = eit[r0 + jj];
-            if (b != s_item) {
-              s_flush();
-              s_item = b;
-            }
-            if (b >= 0) {
-              s_sum += vals[jj];
-              s_sq = fmaf(vals[jj], vals[jj], s_sq);
-            }
           }
         }
       };
       if (!mbar_wait_t(&acc_full[ab], (lt >> 1) & 1, abort_flag, p.err, trc ? &tew : nullptr)) break;
       tc_fence_after();
-      if (p.tma_out) {
-        bool bad = false;
-        for (int sc = 0; sc < TC_N / 64 && !bad; sc++) {
-          float v[64];
+      constexpr int ELD = 32;  // accumulator columns per tcgen05.ld
+      for (int sc = 0; sc < TC_EROWS / ELD && !bad; sc++) {
+        float v[ELD];
+        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + hrow + sc * ELD, v);
+        if (sc == TC_EROWS / ELD - 1) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_empty[ab]);  // this warp's half of the accumulator is read
+        }
+#pragma unroll
+        for (int sub = 0; sub < ELD / TC_EC; sub++) {
+          const int c = sc * (ELD / TC_EC) + sub;
+          const float* rr = rsb;
           long long tq = trc ? clock64() : 0;
-          tmem_ld64(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + sc * 64, v);
-          if (trc) t_tmem += clock64() - tq;
-          if (sc == TC_N / 64 - 1) {
-            tc_fence_before();
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&acc_empty[ab]);  // accumulator fully read
+          if (need_res) {
+            const int sl = rcons % TC_RES_DEPTH;
+            if (!mbar_wait(&rbar[sl], (rcons / TC_RES_DEPTH) & 1, abort_flag, p.err)) bad = true;
+            rr = rsb + sl * TC_EC * 32;
           }
+          if (trc) t_res += clock64() - tq, tq = clock64();
+          float* sb = stg + (c & 1) * TC_EC * 32;
+          if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
+          __syncwarp();
+          if (trc) t_stbuf += clock64() - tq;
+          float vals[TC_EC];
 #pragma unroll
-          for (int sub = 0; sub < 64 / TC_EC; sub++) {
-            const int c = sc * (64 / TC_EC) + sub;
-            const float* rr = rsb;
-            long long tq = trc ? clock64() : 0;
-            if (need_res) {
-              const int sl = rcons % TC_RES_DEPTH;
-              if (!mbar_wait(&rbar[sl], (rcons / TC_RES_DEPTH) & 1, abort_flag, p.err)) bad = true;
-              rr = rsb + sl * TC_EC * 32;
-            }
-            if (trc) t_res += clock64() - tq, tq = clock64();
-            float* sb = stg + (c & 1) * TC_EC * 32;
-            if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
-            __syncwarp();
-            if (trc) t_stbuf += clock64() - tq;
-            float vals[TC_EC];
+          for (int jj = 0; jj < TC_EC; jj++) {
+            float r = v[sub * TC_EC + jj] + bias;
+            if (out_mode == OUT_ADD) r = rr[jj * 32 + lane] + r;
+            else if (out_mode == OUT_PLUS) r = (r + rr[jj * 32 + lane]) * oscale;
+            else if (out_mode == OUT_GELU) r = gelu_new(r);
+            vals[jj] = r;
+            sb[jj * 32 + lane] = r;
+          }
+          if (stat) {
+            if (single) {
 #pragma unroll
-            for (int jj = 0; jj < TC_EC; jj++) {
-              float r = v[sub * TC_EC + jj] + bias;
-              if (out_mode == OUT_ADD) r = rr[jj * 32 + lane] + r;
-              else if (out_mode == OUT_PLUS) r = (r + rr[jj * 32 + lane]) * oscale;
-              else if (out_mode == OUT_GELU) r = gelu_new(r);
-              vals[jj] = r;
-              sb[jj * 32 + lane] = r;
-            }
-            if (trc) tq = clock64();
-            if (stat) s_chunk(c * TC_EC, vals, TC_EC);
-            if (trc) t_stats += clock64() - tq;
-            fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) {
-              tma_store_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
-              bulk_commit();
-            }
-            if (need_res) {  // every lane has read this residual slot: refill it
-              if (lane == 0 && c + TC_RES_DEPTH < TC_N / TC_EC) {
-                const int sl = riss % TC_RES_DEPTH;
-                mbar_arrive_expect_tx(&rbar[sl], TC_EBOX);
-                tma_load_2d(rsb + sl * TC_EC * 32, &p.rmap, co0, t0 + (c + TC_RES_DEPTH) * TC_EC, &rbar[sl]);
+              for (int jj = 0; jj < TC_EC; jj++) {
+                s_sum += vals[jj];
+                s_sq = fmaf(vals[jj], vals[jj], s_sq);
               }
-              if (c + TC_RES_DEPTH < TC_N / TC_EC) riss++;
-              rcons++;
+            } else {
+              s_chunk(c * TC_EC, vals);
             }
           }
-        }
-        if (stat) s_flush();
-        if (bad) break;
-        continue;
-      }
-      // direct stores (row stride not 16-byte aligned): residual loads one 32-row chunk ahead
-      const bool need_res_d = co_ok && need_res;
-      const float* __restrict__ rsrc = out_mode == OUT_ADD ? a.y : a.sc;
-      const long rld = out_mode == OUT_ADD ? a.ldy : a.ldsc;
-      float res[32];
-#pragma unroll
-      for (int jj = 0; jj < 32; jj++) {
-        const int t = t0 + jj;
-        res[jj] = (need_res_d && t < L_out) ? rsrc[(long)t * rld + co] : 0.0f;
-      }
-      for (int c0 = 0; c0 < TC_N; c0 += 32) {
-        float v[32];
-        tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + ab * TC_N + c0, v);
-#pragma unroll
-        for (int jj = 0; jj < 32; jj++) {
-          float r = v[jj] + bias;
-          if (out_mode == OUT_ADD) r = res[jj] + r;
-          else if (out_mode == OUT_PLUS) r = (r + res[jj]) * oscale;
-          else if (out_mode == OUT_GELU) r = gelu_new(r);
-          v[jj] = r;
-        }
-        if (c0 + 32 < TC_N) {
-#pragma unroll
-          for (int jj = 0; jj < 32; jj++) {
-            const int t = t0 + c0 + 32 + jj;
-            res[jj] = (need_res_d && t < L_out) ? rsrc[(long)t * rld + co] : 0.0f;
+          fence_proxy_async();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
+            bulk_commit();
+          }
+          if (need_res) {  // every lane has read this residual slot: refill it
+            if (lane == 0 && c + TC_RES_DEPTH < NCH) {
+              const int sl = riss % TC_RES_DEPTH;
+              mbar_arrive_expect_tx(&rbar[sl], TC_EBOX);
+              tma_load_2d(rsb + sl * TC_EC * 32, &p.rmap, co0, t0 + (c + TC_RES_DEPTH) * TC_EC, &rbar[sl]);
+            }
+            if (c + TC_RES_DEPTH < NCH) riss++;
+            rcons++;
           }
         }
-        if (co_ok) {
-          float* __restrict__ yp = y + (long)(t0 + c0) * ldy + co;
-#pragma unroll
-          for (int jj = 0; jj < 32; jj++)
-            if (t0 + c0 + jj < L_out) yp[(long)jj * ldy] = v[jj];
-        }
-        if (stat) s_chunk(c0, v, 32);
       }
       if (stat) s_flush();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&acc_empty[ab]);
     }
-    if (p.tma_out && lane == 0) {
+    if (lane == 0) {
       for (uint32_t k = rcons; k < riss; k++) {  // residual loads still in flight (abort path)
         const unsigned long long t0 = tc_now();
         while (!mbar_try(&rbar[k % TC_RES_DEPTH], (k / TC_RES_DEPTH) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
@@ -556,138 +605,145 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     if (trc) {
       p.trace[TR_EP_WAIT] = tew;
       p.trace[TR_EP_WORK] = (unsigned long long)(clock64() - t_start) - tew;
-      p.trace[TR_EP_TMEM] = t_tmem;
       p.trace[TR_EP_RES] = t_res;
       p.trace[TR_EP_STBUF] = t_stbuf;
-      p.trace[TR_EP_STATS] = t_stats;
     }
-  } else {
+  } else if (warp >= 4 + TC_NEPI) {
     // ---------------------------------------------------------------- activation producers
     // At each tile the producers first resolve the item of every window row into shared memory
-    // (one lookup per row, shared by all channel blocks). Thread (row lane rl = ptid / 8, chunk
-    // j = ptid % 8) then converts 8 channels of rows rl, rl + 32, ...: four rows are loaded
-    // before any is used, and the item's AdaIN coefficients stay in registers until it changes.
-    const int ptid = threadIdx.x - 6 * 32;  // 0..255
-    const int j = ptid & 7, rl = ptid >> 3;
-    const float* __restrict__ xg = a.x;
-    const long ldx = a.ldx;
-    const int cin = a.cin, L_in = a.L_in, up2 = a.in_up2, win_rows = p.win_rows;
+    // (one lookup per row, shared by all channel blocks). Then, box by box, thread (box row
+    // prow = ptid / 8, chunk j = ptid % 8) converts 8 channels of one input row;
+    // with the x2 upsample each input row feeds two window rows. The item's AdaIN coefficients stay
+    // in registers until the item changes.
+    const int ptid = threadIdx.x - (4 + TC_NEPI) * 32;  // 0 .. TC_NPROD * 32 - 1
+    const int j = ptid & 7, prow = ptid >> 3;
+    const int cin = a.cin, L_in = a.L_in, up2 = in_up2, win_rows = p.win_rows;
     const float2* __restrict__ coef = a.coef;
     const float slope = a.slope;
-    const bool vec_ok = (ldx % 4 == 0) && ((((uintptr_t)xg) & 15) == 0);
-    const bool affine = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE;
-    const bool snake = a.in_mode == IN_ADAIN_SNAKE;
-    const bool leaky_on = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_LEAKY_MASK;
+    const bool affine = in_mode == IN_ADAIN_LEAKY || in_mode == IN_ADAIN_SNAKE;
+    const bool snake = in_mode == IN_ADAIN_SNAKE;
+    const bool leaky_on = in_mode == IN_ADAIN_LEAKY || in_mode == IN_LEAKY_MASK;
     uint32_t xit = 0;
+    int in_sl = 0;
+    uint32_t in_ph = 0;  // input ring slot and phase parity of the next box
     const bool trc = p.trace && blockIdx.x == 0 && ptid == 0;
     unsigned long long tpw = 0, tpi = 0;
     const long long t_start = clock64();
-    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x) {
-      const int tt = tile % p.n_tt;
-      const int base = tt * TC_N - a.pad;
-      const long long ti0 = clock64();
-      asm volatile("bar.sync 1, 256;" ::: "memory");  // previous tile's windows are all written
-      for (int r = ptid; r < win_rows; r += 256) {
-        const int g = base + r;
-        ritem[r] = (g < 0 || g >= L_in) ? -1 : (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, g));
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+      const InSpan sp = in_span(p, tile, in_up2);
+      asm volatile("bar.sync 1, %0;" ::"n"(TC_NPROD * 32) : "memory");  // previous tile's windows are all written
+      for (int r = ptid; r < win_rows; r += TC_NPROD * 32) {
+        const int g = sp.base + r;
+        ritem[r] = (g < 0 || g >= L_in) ? -1 : (in_mode == IN_NOMASK ? 0 : dom_item(a.din, g));
       }
-      asm volatile("bar.sync 1, 256;" ::: "memory");
-      if (trc) tpi += (unsigned long long)(clock64() - ti0);
-      bool ok = true;
-      for (int cb = 0; cb < p.ncb; cb++, xit++) {
-        const int xs = xit % XST;
-        if (!mbar_wait_t(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
+      asm volatile("bar.sync 1, %0;" ::"n"(TC_NPROD * 32) : "memory");
+      for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
+        const int xs = xit % TC_XST;
+        if (!mbar_wait_t(&x_empty[xs], ((xit / TC_XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
           ok = false;
           break;
         }
         uint8_t* xb = xbuf + xs * xbytes + (size_t)j * 16 * p.win_pad;
-        const int c0 = cb * TC_KB + j * 8;
-        const bool ch_ok = c0 < cin;
-        const int nch = ch_ok ? min(8, cin - c0) : 0;
+        // this thread's 8 channels: chA .. chA + 3 and chA + 32 .. chA + 35
+        const int chA = cb * TC_KB + 4 * j;
+        int chs[8];
+#pragma unroll
+        for (int e = 0; e < 8; e++) chs[e] = chA + (e < 4 ? e : 28 + e);
         float al[8], ial[8], ca[8], cbb[8];
         int cached = -1;
         if (snake) {
 #pragma unroll
           for (int e = 0; e < 8; e++) {
-            al[e] = e < nch ? a.alpha[c0 + e] : 1.0f;
+            al[e] = chs[e] < cin ? a.alpha[chs[e]] : 1.0f;
             ial[e] = 1.0f / al[e];
           }
         }
-        for (int r = rl; r < win_rows; r += 128) {
-          float v[4][8];
-          int b[4];
+        // prologue of one window row r from the 8 input values v, stored as bf16
+        auto emit = [&](int r, const float (&v)[8]) {
+          const int b = ritem[r];
+          float o[8];
+          if (b < 0) {
 #pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int rr = r + 32 * u;
-            b[u] = (rr < win_rows && ch_ok) ? ritem[rr] : -1;
+            for (int e = 0; e < 8; e++) o[e] = 0.0f;
+          } else if (affine) {
+            if (b != cached) {
+              cached = b;
 #pragma unroll
-            for (int e = 0; e < 8; e++) v[u][e] = 0.0f;
-            if (b[u] >= 0) {
-              const int g = base + rr;
-              const float* src = xg + (long)(up2 ? (g >> 1) : g) * ldx + c0;
-              if (vec_ok && nch == 8) {
-                const float4 u0 = __ldg(reinterpret_cast<const float4*>(src));
-                const float4 u1 = __ldg(reinterpret_cast<const float4*>(src + 4));
-                v[u][0] = u0.x, v[u][1] = u0.y, v[u][2] = u0.z, v[u][3] = u0.w;
-                v[u][4] = u1.x, v[u][5] = u1.y, v[u][6] = u1.z, v[u][7] = u1.w;
+              for (int e = 0; e < 8; e++) {
+                const float2 q2 = chs[e] < cin ? coef[(long)b * cin + chs[e]] : make_float2(0.0f, 0.0f);
+                ca[e] = q2.x, cbb[e] = q2.y;
+              }
+            }
+            // packed f32x2 arithmetic (each lane rounds exactly like the scalar fmaf / multiply)
+#pragma unroll
+            for (int e = 0; e < 8; e += 2) {
+              float2 t = __ffma2_rn(make_float2(v[e], v[e + 1]), make_float2(ca[e], ca[e + 1]),
+                                    make_float2(cbb[e], cbb[e + 1]));
+              if (snake) {
+                const float2 arg = __fmul2_rn(make_float2(al[e], al[e + 1]), t);
+                const float2 sn = make_float2(__sinf(arg.x), __sinf(arg.y));
+                t = __ffma2_rn(make_float2(ial[e], ial[e + 1]), __fmul2_rn(sn, sn), t);
               } else {
-#pragma unroll
-                for (int e = 0; e < 8; e++)
-                  if (e < nch) v[u][e] = __ldg(src + e);
+                t.x = leaky(t.x, slope);
+                t.y = leaky(t.y, slope);
               }
+              o[e] = t.x;
+              o[e + 1] = t.y;
+            }
+          } else if (leaky_on) {
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = leaky(v[e], slope);
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) o[e] = v[e];
+          }
+          uint4 pk;
+          __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]);
+          __nv_bfloat162 h1 = __floats2bfloat162_rn(o[2], o[3]);
+          __nv_bfloat162 h2 = __floats2bfloat162_rn(o[4], o[5]);
+          __nv_bfloat162 h3 = __floats2bfloat162_rn(o[6], o[7]);
+          memcpy(&pk.x, &h0, 4);
+          memcpy(&pk.y, &h1, 4);
+          memcpy(&pk.z, &h2, 4);
+          memcpy(&pk.w, &h3, 4);
+          *reinterpret_cast<uint4*>(xb + (size_t)r * 16) = pk;
+        };
+        for (int i = 0; i < sp.nbox; i++) {
+          const int sl = in_sl;
+          if (!mbar_wait_t(&in_full[sl], in_ph, abort_flag, p.err, trc ? &tpi : nullptr)) {
+            ok = false;
+            break;
+          }
+          if (++in_sl == RST) in_sl = 0, in_ph ^= 1;
+          const float* box = (const float*)(inring + sl * TC_INBOX);
+#pragma unroll
+          for (int hh = 0; hh < TC_BOX_ROWS / TC_PROWS; hh++) {
+            const int br = prow + TC_PROWS * hh;
+            const float4 lo = *reinterpret_cast<const float4*>(box + br * TC_KB + 4 * j);
+            const float4 hi = *reinterpret_cast<const float4*>(box + br * TC_KB + 32 + 4 * j);
+            const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+            if (!up2) {
+              const int r = i * TC_BOX_ROWS + br;
+              if (r < win_rows) emit(r, v);
+            } else {
+              const int r0 = 2 * (sp.xr0 + i * TC_BOX_ROWS + br) - sp.base;
+              if (r0 >= 0 && r0 < win_rows) emit(r0, v);
+              if (r0 + 1 >= 0 && r0 + 1 < win_rows) emit(r0 + 1, v);
             }
           }
-#pragma unroll
-          for (int u = 0; u < 4; u++) {
-            const int rr = r + 32 * u;
-            if (rr >= win_rows) break;
-            if (b[u] >= 0) {
-              if (affine) {
-                if (b[u] != cached) {
-                  cached = b[u];
-#pragma unroll
-                  for (int e = 0; e < 8; e++) {
-                    const float2 q2 = e < nch ? coef[(long)cached * cin + c0 + e] : make_float2(0.0f, 0.0f);
-                    ca[e] = q2.x, cbb[e] = q2.y;
-                  }
-                }
-#pragma unroll
-                for (int e = 0; e < 8; e++) {
-                  float t = fmaf(v[u][e], ca[e], cbb[e]);
-                  if (snake) {
-                    const float sn = __sinf(al[e] * t);
-                    t = fmaf(ial[e], sn * sn, t);
-                  } else {
-                    t = leaky(t, slope);
-                  }
-                  v[u][e] = t;
-                }
-              } else if (leaky_on) {
-#pragma unroll
-                for (int e = 0; e < 8; e++) v[u][e] = leaky(v[u][e], slope);
-              }
-            }
-            uint4 pk;
-            __nv_bfloat162 h0 = __floats2bfloat162_rn(v[u][0], v[u][1]);
-            __nv_bfloat162 h1 = __floats2bfloat162_rn(v[u][2], v[u][3]);
-            __nv_bfloat162 h2 = __floats2bfloat162_rn(v[u][4], v[u][5]);
-            __nv_bfloat162 h3 = __floats2bfloat162_rn(v[u][6], v[u][7]);
-            memcpy(&pk.x, &h0, 4);
-            memcpy(&pk.y, &h1, 4);
-            memcpy(&pk.z, &h2, 4);
-            memcpy(&pk.w, &h3, 4);
-            *reinterpret_cast<uint4*>(xb + (size_t)rr * 16) = pk;
-          }
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&in_empty[sl]);  // this warp has read the box
         }
+        if (!ok) break;
         fence_proxy_async();
         __syncwarp();
         if (lane == 0) mbar_arrive(&x_full[xs]);
       }
-      if (!ok) break;
     }
     if (trc) {
       p.trace[TR_PR_WAIT_X] = tpw;
-      p.trace[TR_PR_ITEM] = tpi;
+      p.trace[TR_PR_WAIT_IN] = tpi;
       p.trace[TR_PR_WORK] = (unsigned long long)(clock64() - t_start) - tpw - tpi;
     }
   }
@@ -716,6 +772,13 @@ static inline uint16_t f2bf(float f) {
   return (uint16_t)(u >> 16);
 }
 
+// Channel (within its 64-channel block) at K position kp of the operand: chunk kp / 8 holds
+// channels 4 * chunk .. + 3 and 32 + 4 * chunk .. + 3 (the producers' conversion order).
+static inline int block_channel(int kp) {
+  const int j = kp >> 3, e = kp & 7;
+  return e < 4 ? 4 * j + e : 32 + 4 * j + (e - 4);
+}
+
 cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights* out) {
   const int n_cot = (cout + TC_M - 1) / TC_M, ncb = (cin + TC_KB - 1) / TC_KB;
   const size_t n = (size_t)n_cot * ncb * K * (TC_M * TC_KB);
@@ -727,11 +790,11 @@ cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights*
         for (int r = 0; r < TC_M; r++) {
           const int co = cot * TC_M + r;
           if (co >= cout) continue;
-          for (int c = 0; c < TC_KB; c++) {
-            const int ci = cb * TC_KB + c;
+          for (int kp = 0; kp < TC_KB; kp++) {
+            const int ci = cb * TC_KB + block_channel(kp);
             if (ci >= cin) continue;
-            // chunk j = c / 8 at 2048 B, row group r / 8 at 128 B, row r % 8 at 16 B, element c % 8
-            const size_t off = (size_t)(c >> 3) * 1024 + (size_t)(r >> 3) * 64 + (size_t)(r & 7) * 8 + (c & 7);
+            // chunk kp / 8 at 2048 B, row group r / 8 at 128 B, row r % 8 at 16 B, element kp % 8
+            const size_t off = (size_t)(kp >> 3) * 1024 + (size_t)(r >> 3) * 64 + (size_t)(r & 7) * 8 + (kp & 7);
             blk[off] = f2bf(w[((size_t)co * cin + ci) * K + k]);
           }
         }
@@ -751,20 +814,68 @@ cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights*
   return cudaSuccess;
 }
 
+static size_t tc_smem(int win_pad, int rst) {
+  return (size_t)TC_WST * TC_WBLOCK + (size_t)TC_XST * 8 * win_pad * 16 + (size_t)rst * TC_INBOX +
+         (size_t)TC_NEPI * TC_EPI_WARP_BYTES +
+         (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST + 4 + TC_NEPI * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
+}
+
+static inline int win_pad_of(int K, int dil) { return ((TC_N + (K - 1) * dil + 7) / 8) * 8 + 1; }
+
+// Input-box ring depth that fits next to the other buffers (0 when even 2 stages do not fit).
+static int ring_stages(int win_pad) {
+  for (int r = TC_RST_MAX; r >= 2; r--)
+    if (tc_smem(win_pad, r) <= (size_t)TC_SMEM_MAX) return r;
+  return 0;
+}
+
+static bool rows_ok(const void* base, long ld) { return base && ld % 4 == 0 && (((uintptr_t)base) & 15) == 0; }
+
 bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (a.stride != 1 || a.K != t.K || a.cin != t.cin || a.cout != t.cout) return false;
   if (a.L_out < 64) return false;  // tiny row counts (per-item style projections) stay on SIMT
   if ((a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && !a.coef) return false;
   if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
+  if (ring_stages(win_pad_of(a.K, a.dil)) == 0) return false;
+  // every global operand moves by TMA: 16-byte aligned bases and row strides
+  if (!rows_ok(a.x, a.ldx) || !rows_ok(a.y, a.ldy)) return false;
+  if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
   return true;
 }
 
-static size_t tc_smem(int win_pad, int xst) {
-  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + 4 * TC_EPI_WARP_BYTES +
-         (2 * TC_WST + 2 * TC_XST_MAX + 4 + 4 * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
-}
-
 static int g_num_sms[64] = {0};
+static unsigned g_attr_set[64] = {0};  // per device: instances whose shared-memory limit is raised
+
+typedef void (*TcKernelFn)(const TcArgs);
+// Instances for the (input mode, x2 upsample, output mode) combinations the model uses; any other
+// combination runs the generic instance.
+static TcKernelFn pick_kernel(int im, int up, int om, int* idx) {
+  static const struct {
+    int im, up, om;
+    TcKernelFn fn;
+  } table[] = {
+      {IN_ADAIN_SNAKE, 0, OUT_STORE, tc_conv_kernel<IN_ADAIN_SNAKE, 0, OUT_STORE>},
+      {IN_ADAIN_SNAKE, 0, OUT_ADD, tc_conv_kernel<IN_ADAIN_SNAKE, 0, OUT_ADD>},
+      {IN_ADAIN_SNAKE, 0, OUT_PLUS, tc_conv_kernel<IN_ADAIN_SNAKE, 0, OUT_PLUS>},
+      {IN_NOMASK, 0, OUT_STORE, tc_conv_kernel<IN_NOMASK, 0, OUT_STORE>},
+      {IN_NOMASK, 0, OUT_PLUS, tc_conv_kernel<IN_NOMASK, 0, OUT_PLUS>},
+      {IN_NOMASK, 0, OUT_GELU, tc_conv_kernel<IN_NOMASK, 0, OUT_GELU>},
+      {IN_ADAIN_LEAKY, 0, OUT_STORE, tc_conv_kernel<IN_ADAIN_LEAKY, 0, OUT_STORE>},
+      {IN_ADAIN_LEAKY, 0, OUT_PLUS, tc_conv_kernel<IN_ADAIN_LEAKY, 0, OUT_PLUS>},
+      {IN_LEAKY_MASK, 0, OUT_STORE, tc_conv_kernel<IN_LEAKY_MASK, 0, OUT_STORE>},
+      {IN_LEAKY_MASK, 0, OUT_PLUS, tc_conv_kernel<IN_LEAKY_MASK, 0, OUT_PLUS>},
+      {IN_MASK, 0, OUT_STORE, tc_conv_kernel<IN_MASK, 0, OUT_STORE>},
+      {IN_MASK, 1, OUT_STORE, tc_conv_kernel<IN_MASK, 1, OUT_STORE>},
+  };
+  const int n = (int)(sizeof(table) / sizeof(table[0]));
+  for (int i = 0; i < n; i++)
+    if (table[i].im == im && table[i].up == up && table[i].om == om) {
+      *idx = i;
+      return table[i].fn;
+    }
+  *idx = n;
+  return tc_conv_kernel<-1, 0, -1>;
+}
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -786,13 +897,15 @@ static EncodeTiledFn encode_fn() {
   return fn;
 }
 
-// f32 rows [rows][cols] with row stride ld floats; box = 32 columns x 16 rows, no swizzle.
-static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long cols, long ld) {
+// f32 rows [rows][cols] with row stride ld floats; box = box_cols x box_rows, no swizzle; elements
+// outside the tensor read as zero.
+static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long cols, long ld, int box_cols,
+                          int box_rows) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || (ld % 4) != 0 || (((uintptr_t)base) & 15) != 0 || rows <= 0 || cols <= 0) return false;
+  if (!fn || !rows_ok(base, ld) || rows <= 0 || cols <= 0) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
   cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
-  cuuint32_t box[2] = {32u, (cuuint32_t)TC_EC};
+  cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
   return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
@@ -800,36 +913,44 @@ static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long col
 }
 
 cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_t st, unsigned long long* trace) {
+  if (!tc_supported(a, t)) return cudaErrorInvalidValue;
   TcArgs p;
   memset(&p, 0, sizeof(p));
   p.trace = trace;
-  p.tma_out = make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy) ? 1 : 0;
-  if (p.tma_out && a.out_mode == OUT_ADD) p.tma_out = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy) ? 1 : 0;
-  if (p.tma_out && a.out_mode == OUT_PLUS) p.tma_out = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc) ? 1 : 0;
+  const long x_rows = a.in_up2 ? (a.L_in + 1) / 2 : a.L_in;
+  bool maps = make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, TC_BOX_ROWS) &&
+              make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
+  if (maps && a.out_mode == OUT_ADD) maps = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
+  if (maps && a.out_mode == OUT_PLUS) maps = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc, 32, TC_EC);
+  if (!maps) return cudaErrorInvalidValue;
   p.a = a;
   p.wimg = (const __nv_bfloat16*)t.w;
   p.ncb = t.cin_pad / TC_KB;
   p.n_cot = t.cout_pad / TC_M;
   p.n_tt = (a.L_out + TC_N - 1) / TC_N;
   p.win_rows = TC_N + (a.K - 1) * a.dil;
-  p.win_pad = ((p.win_rows + 7) / 8) * 8 + 1;
+  p.win_pad = win_pad_of(a.K, a.dil);
   p.err = err;
-  p.xst = 3;
-  while (p.xst > 2 && tc_smem(p.win_pad, p.xst) > 227 * 1024) p.xst--;
-  const size_t smem = tc_smem(p.win_pad, p.xst);
+  p.rst = ring_stages(p.win_pad);
+  const size_t smem = tc_smem(p.win_pad, p.rst);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && g_num_sms[dev] == 0) {
     int n = 0;
     cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
     g_num_sms[dev] = n;
-    cudaError_t e = cudaFuncSetAttribute(tc_conv_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 227 * 1024);
-    if (e != cudaSuccess) return e;
   }
-  if (smem > 227 * 1024) return cudaErrorInvalidValue;
+  int ci = 0;
+  const TcKernelFn fn = pick_kernel(a.in_mode, a.in_up2, a.out_mode, &ci);
+  if (dev < 64 && !(g_attr_set[dev] & (1u << ci))) {
+    cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
+    if (e != cudaSuccess) return e;
+    g_attr_set[dev] |= 1u << ci;
+  }
   const int ntiles = p.n_cot * p.n_tt;
-  const int grid = ntiles < g_num_sms[dev < 64 ? dev : 0] ? ntiles : g_num_sms[dev < 64 ? dev : 0];
-  tc_conv_kernel<<<grid, TC_THREADS, smem, st>>>(p);
+  const int nsm = g_num_sms[dev < 64 ? dev : 0];
+  const int grid = ntiles < nsm ? ntiles : nsm;
+  fn<<<grid, TC_THREADS, smem, st>>>(p);
   return cudaGetLastError();
 }
 

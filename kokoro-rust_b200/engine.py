@@ -52,7 +52,7 @@ _SIGS = {
     "kk_profile_entry": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_int, _P, _P, _P]),
     "kk_profile_launch": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_char_p, ctypes.c_int, _P, _P, _P]),
     "kk_profile_reset": (None, [_P]),
-    "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int, _P]),
     "kk_conv_selftest_error": (ctypes.c_char_p, []),
 }
 
@@ -68,9 +68,10 @@ class ConvCase(ctypes.Structure):
 
 def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1, up2=0, in_mode=0,
                   slope=0.2, out_mode=0, oscale=1.0, bias=None, coef=None, alpha=None, sc=None, y=None,
-                  n_items=None, want_stats=False):
+                  n_items=None, want_stats=False, timing_iters=0):
     """One convolution through the tcgen05 kernel (kk_conv_selftest). x [rows][ldx] f32, w torch
-    layout [cout][cin][K]; returns y [rows_out][ldy] (and [n_items][cout][2] statistics)."""
+    layout [cout][cin][K]; returns y [rows_out][ldy] (and [n_items][cout][2] statistics); with
+    timing_iters > 0 returns (result, device ms per launch)."""
     lib = load_library()
     x = np.ascontiguousarray(x, np.float32)
     w = np.ascontiguousarray(w, np.float32)
@@ -91,11 +92,14 @@ def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1
         keep.append(a)
         return a.ctypes.data
     stat = np.zeros((n_items, cout, 2), np.float64) if want_stats else None
+    ms = ctypes.c_double(0.0)
     st = lib.kk_conv_selftest(ordinal, ctypes.byref(c), x.ctypes.data, w.ctypes.data, ptr(bias), ptr(coef),
-                              ptr(alpha), ptr(sc), y.ctypes.data, None if stat is None else stat.ctypes.data)
+                              ptr(alpha), ptr(sc), y.ctypes.data, None if stat is None else stat.ctypes.data,
+                              timing_iters, ctypes.byref(ms))
     if st != KK_OK:
         raise KokoroError(st, lib.kk_conv_selftest_error().decode())
-    return (y, stat) if want_stats else y
+    res = (y, stat) if want_stats else y
+    return (res, ms.value) if timing_iters > 0 else res
 
 
 _lib = None

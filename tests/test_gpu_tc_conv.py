@@ -96,7 +96,7 @@ CASES = [
     ("linear_768_2048_gelu", 768, 2048, 1, 1, IN_NOMASK, OUT_GELU, 0, False, 0, 0),
     ("adain_leaky_up2_514_1024_stats", 514, 1024, 3, 1, IN_ADAIN_LEAKY, OUT_STORE, 1, True, 2, 0),
     ("mask_1090_512_stats", 1090, 512, 3, 1, IN_MASK, OUT_STORE, 0, True, 2, 0),
-    ("leaky_k7_128_22_direct_store", 128, 22, 7, 1, IN_LEAKY_MASK, OUT_STORE, 0, False, 0, 0),
+    ("leaky_k7_128_22_padded_rows", 128, 22, 7, 1, IN_LEAKY_MASK, OUT_STORE, 0, False, 0, 6),
     ("mask_k1_22_128", 22, 128, 1, 1, IN_MASK, OUT_STORE, 0, False, 2, 0),
     ("k2_132_256", 132, 256, 2, 1, IN_NOMASK, OUT_STORE, 0, False, 0, 4),
 ]
@@ -120,7 +120,7 @@ def test_tc_conv_matches_fp64_on_bf16_operands(kk, case):
     coef = np.stack([1.0 + 0.3 * rng.standard_normal((n_items, cin)), 0.2 * rng.standard_normal((n_items, cin))],
                     -1).astype(np.float32)
     alpha = (1.0 + 0.5 * rng.random(cin)).astype(np.float32)
-    sc = rng.standard_normal((rows_out, cout + 2)).astype(np.float32) if out_mode == OUT_PLUS else None
+    sc = rng.standard_normal((rows_out, cout + 4)).astype(np.float32) if out_mode == OUT_PLUS else None
     y0 = rng.standard_normal((rows_out, cout + ldy_extra)).astype(np.float32)
     oscale = float(1 / np.sqrt(2.0))
     res = E.conv_selftest(0, x=x, w=w, item_in=items_in, item_out=items_out, rows_out=rows_out, pad=pad, dil=dil,
@@ -136,13 +136,27 @@ def test_tc_conv_matches_fp64_on_bf16_operands(kk, case):
     tol_rel = 1e-4 if in_mode == IN_ADAIN_SNAKE else 2e-5
     assert rel <= tol_rel, (name, rel)
     assert err.max() <= 2e-3 * rms, (name, err.max(), rms)
-    if ldy_extra:  # columns past cout untouched
-        np.testing.assert_array_equal(y[:, cout:], y0[:, cout:])
+    if ldy_extra:  # columns from cout rounded up to 16 bytes on are untouched (TMA writes 16-byte units)
+        c16 = (cout + 3) // 4 * 4
+        np.testing.assert_array_equal(y[:, c16:], y0[:, c16:])
     if stats:
         for b in range(n_items):
             rows = got[items_out == b]
             np.testing.assert_allclose(st[b, :, 0], rows.sum(0), rtol=1e-4, atol=1e-4 * np.abs(rows).sum(0).max())
             np.testing.assert_allclose(st[b, :, 1], (rows ** 2).sum(0), rtol=1e-4)
+
+
+def test_tc_conv_rejects_unaligned_row_strides(kk):
+    """Every operand moves by TMA, so row strides must be multiples of 16 bytes."""
+    import kokoro_rust_b200.engine as E
+    tab = np.zeros(300, np.int32)
+    w = np.zeros((22, 64, 3), np.float32)
+    with pytest.raises(E.KokoroError, match="not supported"):
+        E.conv_selftest(0, x=np.zeros((300, 64), np.float32), w=w, item_in=tab, item_out=tab, rows_out=300, pad=1,
+                        y=np.zeros((300, 22), np.float32))
+    with pytest.raises(E.KokoroError, match="not supported"):
+        E.conv_selftest(0, x=np.zeros((300, 66), np.float32), w=w, item_in=tab, item_out=tab, rows_out=300, pad=1,
+                        y=np.zeros((300, 24), np.float32))
 
 
 def test_tc_conv_rejects_tiny_row_counts(kk):
