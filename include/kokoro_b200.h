@@ -210,7 +210,15 @@ typedef struct kk_conv_case {
 KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x, const float* w,
                                   const float* bias, const float* coef, const float* alpha, const float* sc,
                                   float* y, double* stat, int timing_iters, double* ms_per_iter);
-/* Message of the last kk_conv_selftest failure on this thread. */
+/*
+ * kk_attention_selftest -- diagnostics: the BF16 mode's tcgen05 multi-head attention (12 heads of
+ * 64) on host buffers. qkv [sum T][2304] rows [q | k | v] of n_items items of tok_len[i] in
+ * [1, 512] rows each, concatenated; ctx [sum T][768] receives softmax(Q K^T / 8) V per item and
+ * head. No counterpart in the reference (kernel-level test of src/gpu_batch.rs:429-442's math).
+ */
+KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len, const float* qkv,
+                                       float* ctx);
+/* Message of the last kk_conv_selftest / kk_attention_selftest failure on this thread. */
 KK_API const char* kk_conv_selftest_error(void);
 
 /* Bytes of device memory the engine currently holds (weights + arena). */

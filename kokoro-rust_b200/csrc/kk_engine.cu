@@ -1240,11 +1240,32 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     linear(m.map_in, emb, 128, LT, h, 768);
     int max_t = 0;
     for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
+    // tensor-core attention: (item, first query row) per 128-query tile, in length buckets
+    const bool attn_tc = precision == KK_PRECISION_BF16 && tc_ok;
+    int n_work[3] = {0, 0, 0};
+    const int2* work_d = nullptr;
+    if (attn_tc) {
+      std::vector<int2> wl[3];
+      for (int b = 0; b < B; b++) {
+        const int T = ids_len[b];
+        const int k = T <= 128 ? 0 : (T <= 256 ? 1 : 2);
+        for (int q0 = 0; q0 < T; q0 += 128) wl[k].push_back(make_int2(b, q0));
+      }
+      std::vector<int2> all;
+      for (int k = 0; k < 3; k++) {
+        n_work[k] = (int)wl[k].size();
+        all.insert(all.end(), wl[k].begin(), wl[k].end());
+      }
+      work_d = upload(all.data(), all.size());
+    }
     for (int layer = 0; layer < 12; layer++) {
       linear(m.qkv, h, 768, LT, qkv, 2304);
       cudaEvent_t e0;
       prof_begin(&e0);
-      check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
+      if (attn_tc)
+        check(launch_attention_tc(qkv, 2304, items_d, work_d, n_work, ctx, 768, err_flag, st), "attention(tcgen05)");
+      else
+        check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
       double af = 0;
       for (int b = 0; b < B; b++) af += 4.0 * 12 * 64 * (double)ids_len[b] * ids_len[b];
       prof_end(e0, "attention", af);

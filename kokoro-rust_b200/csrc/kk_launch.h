@@ -42,6 +42,11 @@ cudaError_t launch_cat_style(const int* row_item, int rows, int d, const float* 
 // Per-item multi-head attention over token rows, fp32 online softmax (src/gpu_batch.rs:429-442).
 cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* items, int B, int max_len,
                                  float* ctx, int ldc, cudaStream_t st);
+// The same attention on tcgen05 tensor cores (bf16 Q, K, V and P, fp32 accumulation and softmax).
+// work: (item, first query row) per 128-query tile, grouped by item length into the buckets
+// T <= 128, T <= 256 and T <= 512 of n_work[0..2] entries. err receives 3 if an MMA wait expires.
+cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
+                                const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st);
 
 // ---- LSTM recurrence (persistent, one cooperative launch per BiLSTM)
 // Items (sorted longest-first) are dealt round-robin into G <= 4 groups of at most IPG <= 144

@@ -10,6 +10,7 @@
 
 #include "../../include/kokoro_b200.h"
 #include "kk_common.cuh"
+#include "kk_launch.h"
 #include "kk_tc.h"
 
 namespace {
@@ -126,5 +127,51 @@ extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_cas
   if (stat && cudaMemcpy(stat, dst.p, sizeof(double) * 2 * (size_t)c->n_items * c->cout, cudaMemcpyDeviceToHost) !=
                   cudaSuccess)
     return fail(KK_ERR_CUDA, "statistics copy failed");
+  return KK_OK;
+}
+
+extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len,
+                                                  const float* qkv, float* ctx) {
+  using namespace kk;
+  if (n_items < 1 || !tok_len || !qkv || !ctx) return fail(KK_ERR_INVALID_ARG, "null argument");
+  std::vector<ItemTab> items(n_items);
+  std::vector<int2> wl[3];
+  int rows = 0;
+  for (int b = 0; b < n_items; b++) {
+    const int T = tok_len[b];
+    if (T < 1 || T > 512) return fail(KK_ERR_INVALID_ARG, "item length outside [1, 512]");
+    items[b] = ItemTab{rows, T, 0, 0};
+    const int k = T <= 128 ? 0 : (T <= 256 ? 1 : 2);
+    for (int q0 = 0; q0 < T; q0 += 128) wl[k].push_back(make_int2(b, q0));
+    rows += T;
+  }
+  std::vector<int2> all;
+  int n_work[3];
+  for (int k = 0; k < 3; k++) {
+    n_work[k] = (int)wl[k].size();
+    all.insert(all.end(), wl[k].begin(), wl[k].end());
+  }
+  if (cudaSetDevice(cuda_ordinal) != cudaSuccess || !tc_available())
+    return fail(KK_ERR_CUDA, "no compute-capability-10 device");
+  DevBuf dq, dc, di, dw, derr;
+  auto put = [&](DevBuf& b, const void* h, size_t n) -> bool {
+    if (cudaMalloc(&b.p, n) != cudaSuccess) return false;
+    return cudaMemcpy(b.p, h, n, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  bool ok = put(dq, qkv, sizeof(float) * rows * 2304) && put(di, items.data(), sizeof(ItemTab) * n_items) &&
+            put(dw, all.data(), sizeof(int2) * all.size()) &&
+            cudaMalloc(&dc.p, sizeof(float) * rows * 768) == cudaSuccess &&
+            cudaMemset(dc.p, 0, sizeof(float) * rows * 768) == cudaSuccess &&
+            cudaMalloc(&derr.p, sizeof(int)) == cudaSuccess && cudaMemset(derr.p, 0, sizeof(int)) == cudaSuccess;
+  if (!ok) return fail(KK_ERR_OOM, "device allocation / copy failed");
+  cudaError_t e = launch_attention_tc((const float*)dq.p, 2304, (const ItemTab*)di.p, (const int2*)dw.p, n_work,
+                                      (float*)dc.p, 768, (int*)derr.p, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+  int errh = 0;
+  cudaMemcpy(&errh, derr.p, sizeof(int), cudaMemcpyDeviceToHost);
+  if (errh) return fail(KK_ERR_TIMEOUT, "a tcgen05 attention wait timed out");
+  if (cudaMemcpy(ctx, dc.p, sizeof(float) * rows * 768, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(KK_ERR_CUDA, "output copy failed");
   return KK_OK;
 }

@@ -54,6 +54,7 @@ _SIGS = {
     "kk_profile_reset": (None, [_P]),
     "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int, _P]),
     "kk_conv_selftest_error": (ctypes.c_char_p, []),
+    "kk_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P]),
 }
 
 
@@ -100,6 +101,19 @@ def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1
         raise KokoroError(st, lib.kk_conv_selftest_error().decode())
     res = (y, stat) if want_stats else y
     return (res, ms.value) if timing_iters > 0 else res
+
+
+def attention_selftest(ordinal: int, tok_len, qkv):
+    """The BF16 mode's tensor-core attention (kk_attention_selftest): qkv [sum T][2304] f32 of items
+    of tok_len rows each; returns ctx [sum T][768]."""
+    lib = load_library()
+    tl = np.ascontiguousarray(tok_len, np.int32)
+    qkv = np.ascontiguousarray(qkv, np.float32)
+    ctx = np.zeros((qkv.shape[0], 768), np.float32)
+    st = lib.kk_attention_selftest(ordinal, len(tl), tl.ctypes.data, qkv.ctypes.data, ctx.ctypes.data)
+    if st != KK_OK:
+        raise KokoroError(st, lib.kk_conv_selftest_error().decode())
+    return ctx
 
 
 _lib = None
