@@ -936,39 +936,34 @@ void Engine::lstm(const Lstm& L, const float* x, int ldx, int rows, const std::v
   std::vector<int> order(B);
   std::iota(order.begin(), order.end(), 0);
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return len[a] > len[b]; });
-  const int* start_d = upload(start.data(), B);
-  const int* len_d = upload(len.data(), B);
-  // items beyond one launch's capacity (4 groups x 144) run in further launches
-  const int cap = LSTM_MAX_GROUPS * LSTM_MAX_IPG;
-  for (int first = 0; first < B; first += cap) {
-    const int nb = std::min(cap, B - first);
-    const int G = std::max(1, std::min(LSTM_MAX_GROUPS, (nb + 35) / 36));
-    const int IPG = (nb + G - 1) / G;
-    const int Tmax = len[order[first]];
-    std::vector<int> gitems((size_t)G * IPG, -1), gact((size_t)G * std::max(Tmax, 1), 0);
-    for (int r = 0; r < nb; r++) gitems[(size_t)(r % G) * IPG + r / G] = order[first + r];  // round-robin
-    for (int g = 0; g < G; g++)
-      for (int s2 = 0; s2 < Tmax; s2++) {
-        int n = 0;
-        while (n < IPG && gitems[(size_t)g * IPG + n] >= 0 && len[gitems[(size_t)g * IPG + n]] > s2) n++;
-        gact[(size_t)g * Tmax + s2] = n;
-      }
-    LstmArgs a;
-    a.gx = gx, a.ldgx = 2048, a.whh = L.whh, a.bhh = L.bhh, a.out = out, a.ldo = ldo;
-    a.start = start_d, a.len = len_d;
-    a.gitems = upload(gitems.data(), gitems.size());
-    a.gact = upload(gact.data(), gact.size());
-    a.B = B, a.Tmax = Tmax, a.G = G, a.IPG = IPG;
-    a.hbuf = ar.get<float>((size_t)4 * B * 256);
-    a.bar = ar.get<unsigned>((size_t)2 * G);
-    a.err = err_flag;
-    cudaEvent_t e0;
-    prof_begin(&e0);
-    check(launch_lstm(a, st), "lstm");
-    long long steps = 0;
-    for (int r = 0; r < nb; r++) steps += len[order[first + r]];
-    prof_end(e0, "lstm_recurrence", 2.0 * 2 * 1024 * 256 * (double)steps);
+  // groups of LSTM_IPG consecutive items of the longest-first order (one cluster per group and
+  // direction; clusters are independent, so any number of groups is valid)
+  const int IPG = LSTM_IPG;
+  const int G = (B + IPG - 1) / IPG;
+  const int Tmax = B ? len[order[0]] : 0;
+  std::vector<int> gstart((size_t)G * IPG, 0), glen((size_t)G * IPG, 0), gact((size_t)G * std::max(Tmax, 1), 0);
+  for (int r = 0; r < B; r++) {
+    gstart[r] = start[order[r]];
+    glen[r] = len[order[r]];
   }
+  for (int g = 0; g < G; g++)
+    for (int s2 = 0; s2 < Tmax; s2++) {
+      int n = 0;
+      while (n < IPG && glen[(size_t)g * IPG + n] > s2) n++;
+      gact[(size_t)g * Tmax + s2] = n;
+    }
+  LstmArgs a;
+  a.gx = gx, a.ldgx = 2048, a.whh = L.whh, a.bhh = L.bhh, a.out = out, a.ldo = ldo;
+  a.gstart = upload(gstart.data(), gstart.size());
+  a.glen = upload(glen.data(), glen.size());
+  a.gact = upload(gact.data(), gact.size());
+  a.G = G, a.IPG = IPG, a.Tmax = Tmax;
+  cudaEvent_t e0;
+  prof_begin(&e0);
+  check(launch_lstm(a, st), "lstm");
+  long long steps = 0;
+  for (int r = 0; r < B; r++) steps += len[r];
+  prof_end(e0, "lstm_recurrence", 2.0 * 2 * 1024 * 256 * (double)steps);
   ar.rewind(mk);
 }
 

@@ -255,177 +255,6 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
   return cudaGetLastError();
 }
 
-// ------------------------------------------------------------------------------ LSTM
-
-constexpr int LH = 256;            // hidden units per direction
-constexpr int L_UNITS = 16;        // hidden units owned by one CTA (all four gates: 64 rows of W_hh)
-constexpr int L_UBLK = LH / L_UNITS;
-constexpr int L_HLD = LH + 4;      // row stride of the staged hidden states (floats)
-constexpr unsigned long long L_TIMEOUT_NS = 2000000000ull;
-
-__device__ __forceinline__ unsigned ld_acquire_u32(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-__device__ __forceinline__ unsigned long long globaltimer_ns() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-  return t;
-}
-
-// Bidirectional LSTM recurrence for all items of a batch (kernels/kokoro.cu:400-450 semantics:
-// gates = gx + (W_hh h + b_hh), order i, f, g, o; fp32 throughout). CTA (dir, group, unit block):
-// W_hh rows of its 16 units (4 gates) stay in shared memory for the whole sequence; each step the
-// group's active hidden states are staged once (float4, L2), thread (unit, item lane) computes the
-// four gate dot products of its unit for items lane, lane + 16, ... with float4 register blocking,
-// keeps the cell states of those (unit, item) pairs in registers, and writes the new hidden state.
-// One bounded barrier per step over the 16 CTAs of (dir, group): a wait longer than 2 s sets *err
-// and every CTA returns.
-template <int IPT>
-__global__ void __launch_bounds__(256, 1) lstm_kernel(const LstmArgs a) {
-  extern __shared__ __align__(16) float lsm[];
-  float* Ws = lsm;                       // [16 units][4 gates][256]
-  float* Hs = lsm + L_UNITS * 4 * LH;    // [IPG][L_HLD]
-  __shared__ int s_abort;
-  const int per_dir = a.G * L_UBLK;
-  const int dir = blockIdx.x / per_dir;
-  const int g = (blockIdx.x / L_UBLK) % a.G;
-  const int u0 = (blockIdx.x % L_UBLK) * L_UNITS;
-  const int tid = threadIdx.x, uu = tid >> 4, il = tid & 15;
-  const int unit = u0 + uu;
-  for (int i = tid; i < L_UNITS * 4 * LH / 4; i += 256) {
-    const int row = i / (LH / 4), k4 = i % (LH / 4);
-    const int u = row >> 2, gate = row & 3;
-    reinterpret_cast<float4*>(Ws)[i] =
-        reinterpret_cast<const float4*>(a.whh + ((long)dir * 4 * LH + gate * LH + u0 + u) * LH)[k4];
-  }
-  float bh[4];
-#pragma unroll
-  for (int q = 0; q < 4; q++) bh[q] = a.bhh[dir * 4 * LH + q * LH + unit];
-  const int* items = a.gitems + g * a.IPG;
-  const int* act = a.gact + (long)g * a.Tmax;
-  unsigned* bar = a.bar + dir * a.G + g;
-  float c[IPT];
-#pragma unroll
-  for (int m = 0; m < IPT; m++) c[m] = 0.0f;
-  __syncthreads();
-  for (int s = 0; s < a.Tmax; s++) {
-    const int na = act[s];
-    if (na == 0) return;  // the group's items are done (same for all 16 CTAs of the group)
-    {
-      const float* hp = a.hbuf + ((long)(s & 1) * 2 + dir) * (long)a.B * LH;
-      float* hn = a.hbuf + ((long)((s + 1) & 1) * 2 + dir) * (long)a.B * LH;
-      for (int i = tid; i < na * (LH / 4); i += 256) {
-        const int slot = i / (LH / 4), k4 = i % (LH / 4);
-        const float4 v = __ldcg(reinterpret_cast<const float4*>(hp + (long)items[slot] * LH) + k4);
-        *reinterpret_cast<float4*>(Hs + slot * L_HLD + k4 * 4) = v;
-      }
-      // gate inputs of the owned (unit, item) pairs, fetched while the hidden states land
-      float gxv[IPT][4];
-      int rowv[IPT];
-#pragma unroll
-      for (int m = 0; m < IPT; m++) {
-        const int slot = il + 16 * m;
-        rowv[m] = -1;
-        if (slot < na) {
-          const int b = items[slot];
-          const int T = a.len[b];
-          const int t = dir == 0 ? s : T - 1 - s;
-          rowv[m] = a.start[b] + t;
-          const float* gp = a.gx + (long)rowv[m] * a.ldgx + dir * 4 * LH + unit;
-#pragma unroll
-          for (int q = 0; q < 4; q++) gxv[m][q] = gp[q * LH];
-        }
-      }
-      __syncthreads();
-      float acc[IPT][4];
-#pragma unroll
-      for (int m = 0; m < IPT; m++)
-#pragma unroll
-        for (int q = 0; q < 4; q++) acc[m][q] = 0.0f;
-      const float* wrow = Ws + uu * 4 * LH;
-#pragma unroll 2
-      for (int k = 0; k < LH; k += 4) {
-        float4 w[4];
-#pragma unroll
-        for (int q = 0; q < 4; q++) w[q] = *reinterpret_cast<const float4*>(wrow + q * LH + k);
-#pragma unroll
-        for (int m = 0; m < IPT; m++) {
-          if (il + 16 * m < na) {
-            const float4 h = *reinterpret_cast<const float4*>(Hs + (il + 16 * m) * L_HLD + k);
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              acc[m][q] = fmaf(w[q].x, h.x, acc[m][q]);
-              acc[m][q] = fmaf(w[q].y, h.y, acc[m][q]);
-              acc[m][q] = fmaf(w[q].z, h.z, acc[m][q]);
-              acc[m][q] = fmaf(w[q].w, h.w, acc[m][q]);
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int m = 0; m < IPT; m++) {
-        if (rowv[m] < 0) continue;
-        const float gi = gxv[m][0] + (acc[m][0] + bh[0]);
-        const float gf = gxv[m][1] + (acc[m][1] + bh[1]);
-        const float gg = gxv[m][2] + (acc[m][2] + bh[2]);
-        const float go = gxv[m][3] + (acc[m][3] + bh[3]);
-        const float ig = 1.0f / (1.0f + expf(-gi));
-        const float fg = 1.0f / (1.0f + expf(-gf));
-        const float cg = tanhf(gg);
-        const float og = 1.0f / (1.0f + expf(-go));
-        c[m] = fg * c[m] + ig * cg;
-        const float h = og * tanhf(c[m]);
-        hn[(long)items[il + 16 * m] * LH + unit] = h;
-        a.out[(long)rowv[m] * a.ldo + dir * LH + unit] = h;
-      }
-    }
-    // step barrier over the 16 CTAs of this (direction, group)
-    __syncthreads();
-    if (tid == 0) {
-      __threadfence();
-      atomicAdd(bar, 1u);
-      const unsigned target = (unsigned)(s + 1) * L_UBLK;
-      const unsigned long long t0 = globaltimer_ns();
-      int ab = 0;
-      while (ld_acquire_u32(bar) < target) {
-        if (*(volatile int*)a.err) {
-          ab = 1;
-          break;
-        }
-        if (globaltimer_ns() - t0 > L_TIMEOUT_NS) {
-          atomicExch(a.err, 1);
-          ab = 1;
-          break;
-        }
-      }
-      __threadfence();
-      s_abort = ab;
-    }
-    __syncthreads();
-    if (s_abort) return;
-  }
-}
-
-cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st) {
-  cudaError_t e;
-  if ((e = cudaMemsetAsync(a.hbuf, 0, sizeof(float) * 4L * a.B * LH, st)) != cudaSuccess) return e;
-  if ((e = cudaMemsetAsync(a.bar, 0, sizeof(unsigned) * 2 * a.G, st)) != cudaSuccess) return e;
-  if (a.Tmax == 0) return cudaSuccess;
-  if (a.G < 1 || a.G > LSTM_MAX_GROUPS || a.IPG < 1 || a.IPG > LSTM_MAX_IPG) return cudaErrorInvalidValue;
-  const size_t smem = sizeof(float) * (L_UNITS * 4 * LH + (size_t)a.IPG * L_HLD);
-  LstmArgs args = a;
-  void* params[] = {&args};
-  const int ipt = (a.IPG + 15) / 16;
-  const void* fn = ipt <= 1   ? (const void*)lstm_kernel<1>
-                   : ipt <= 2 ? (const void*)lstm_kernel<2>
-                   : ipt <= 4 ? (const void*)lstm_kernel<4>
-                              : (const void*)lstm_kernel<9>;
-  if ((e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)) != cudaSuccess) return e;
-  return cudaLaunchCooperativeKernel(fn, dim3(2 * a.G * L_UBLK), dim3(256), params, smem, st);
-}
-
 // ------------------------------------------------------------------------------ AdaIN statistics
 
 __global__ void stats_partial_kernel(const float* x, int ldx, int C, const ItemTab* items, int scale, int plus1,

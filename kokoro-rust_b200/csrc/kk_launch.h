@@ -48,10 +48,9 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
 cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
                                 const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st);
 
-// ---- LSTM recurrence (persistent, one cooperative launch per BiLSTM)
-// Items (sorted longest-first) are dealt round-robin into G <= 4 groups of at most IPG <= 144
-// items; CTA (direction, group, unit block) owns 16 hidden units = 64 rows of W_hh in shared
-// memory and the group's hidden states; only the 16 CTAs of one (direction, group) synchronise.
+// ---- LSTM recurrence (one launch per BiLSTM, thread-block clusters; kk_lstm.cu)
+// Items sorted longest-first form G groups of LSTM_IPG; one cluster of 8 CTAs runs each
+// (group, direction).
 struct LstmArgs {
   const float* gx;    // [rows][ldgx]: dir d gate g unit j at column d*4H + g*H + j (includes b_ih)
   int ldgx;
@@ -59,17 +58,12 @@ struct LstmArgs {
   const float* bhh;   // [2][4H]
   float* out;         // [rows][ldo]: dir d unit j at column d*H + j
   int ldo;
-  const int* start;   // [B] first row of item b
-  const int* len;     // [B]
-  const int* gitems;  // [G][IPG] items of each group, longest first (-1 = none)
-  const int* gact;    // [G][Tmax] items of group g still running at step s
-  int B, Tmax, G, IPG;
-  float* hbuf;        // [2][2][B][H] double-buffered hidden state (zeroed by the launcher)
-  unsigned* bar;      // [2][G] step-barrier counters (zeroed by the launcher)
-  int* err;           // set to 1 when a barrier wait times out
+  const int* gstart;  // [G][IPG] first row of each group member, longest first (unused slots 0)
+  const int* glen;    // [G][IPG] its length (unused slots 0)
+  const int* gact;    // [G][Tmax] members of group g still running at step s
+  int G, IPG, Tmax;
 };
-constexpr int LSTM_MAX_GROUPS = 4;
-constexpr int LSTM_MAX_IPG = 144;
+constexpr int LSTM_IPG = 32;
 cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st);
 
 // ---- AdaIN statistics: per (item, channel) mean / rstd over the item's span (biased variance,
