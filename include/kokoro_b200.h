@@ -188,7 +188,8 @@ KK_API void kk_profile_reset(kk_engine* e);
  *         (row strides a multiple of 4 floats); columns cout .. round_up(cout, 4) - 1 of y may be
  *         overwritten (the kernel writes whole 16-byte units)
  *  stat   NULL, or [n_items][cout][2] f64: per (item, channel) sum and sum of squares of y
- *  timing_iters, ms_per_iter   when timing_iters > 0: the launch is repeated that many times more
+ *  timing_iters, ms_per_iter   when timing_iters > 0: the launch (with its input transform on the
+ *         pre route) is repeated that many times more
  *         on the same device buffers and the mean device time per launch (CUDA events on the
  *         launching stream) is written to *ms_per_iter; y and stat then hold the repeated result
  */
@@ -206,6 +207,8 @@ typedef struct kk_conv_case {
   int n_items;
   const int* item_in;   /* [rows_in] item of each input-domain row, -1 = gap */
   const int* item_out;  /* [rows_out] item of each output row, -1 = gap */
+  int pre;              /* 1: transform the input once into bf16 window planes, then run the conv on
+                           them (the route of layers with more than 128 output channels) */
 } kk_conv_case;
 KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const float* x, const float* w,
                                   const float* bias, const float* coef, const float* alpha, const float* sc,

@@ -50,8 +50,14 @@ enum InMode : int {
   IN_MASK = 1,       // x, gap rows -> 0
   IN_ADAIN_LEAKY = 2,// leaky(AdaIN(x)), gap rows -> 0
   IN_ADAIN_SNAKE = 3,// snake(AdaIN(x)), gap rows -> 0
-  IN_LEAKY_MASK = 4  // leaky(x), gap rows -> 0
+  IN_LEAKY_MASK = 4, // leaky(x), gap rows -> 0
+  IN_PRE = 5         // tensor-core path: input already transformed into bf16 window planes (xpre)
 };
+
+// Zero rows around the bf16 window planes of IN_PRE inputs: a tile's window starts at most
+// (K-1)*dil/2 <= 25 rows before row 0 and ends at most 255 + (K-1)*dil rows past the last row.
+constexpr int PRE_PAD_FRONT = 32;
+constexpr int PRE_PAD_BACK = 320;
 
 enum OutMode : int {
   OUT_STORE = 0,     // y = acc + bias
@@ -91,6 +97,10 @@ struct ConvArgs {
   // sum and sum of squares, accumulated into stat[(b * cout + co) * 2 + {0, 1}] (f64, pre-zeroed)
   double* stat;
   Dom dout;           // domain of the output rows (item lookup for stat)
+  // IN_PRE: bf16 planes [64-channel block][8-channel chunk][pre_rows][8], row r of the input domain
+  // at plane row PRE_PAD_FRONT + r (chunk j holds channels 4j..4j+3 and 32+4j..32+4j+3)
+  const void* xpre;
+  long pre_rows;
 };
 
 __device__ __forceinline__ float leaky(float v, float s) { return v < 0.0f ? v * s : v; }

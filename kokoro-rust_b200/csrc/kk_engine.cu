@@ -245,6 +245,11 @@ static const int CAT_LD = 1092;
 static const int SPEC_LD = 24;
 static const int POST_LD = 24;
 static inline int ld16(int c) { return (c + 3) & ~3; }  // row stride of a c-channel f32 buffer
+// Layers with more output channels than this pre-transform their input once (IN_PRE) instead of
+// in the conv's producer warps (which redo it for every 128-channel output tile). Measured on B200:
+// at 256 channels the two routes are within 10% of each other (the extra bf16 pass costs about
+// what the second transform does); from 512 channels on the pre-transform route is 1.7x faster.
+static const int TC_PRE_MIN_COUT = 256;
 
 struct Engine {
   int dev = 0;
@@ -766,7 +771,22 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       tr = ar.get<unsigned long long>(16);
       KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
     }
-    check(tc_conv(a, c.tc, err_flag, st, tr), "conv(tcgen05)");
+    if (c.cout > TC_PRE_MIN_COUT) {
+      // several 128-channel output tiles share each input window: transform the input once into
+      // bf16 window planes instead of once per output tile
+      auto mk = ar.mark();
+      ConvArgs ap = a;
+      ap.pre_rows = PRE_PAD_FRONT + (long)a.L_in + PRE_PAD_BACK;
+      void* xpre = ar.get<uint8_t>((size_t)((a.cin + 63) / 64) * 8 * ap.pre_rows * 16);
+      check(launch_prologue_bf16(a, xpre, ap.pre_rows, st), "prologue_bf16");
+      ap.xpre = xpre;
+      ap.in_mode = IN_PRE;
+      ap.in_up2 = 0;
+      check(tc_conv(ap, c.tc, err_flag, st, tr), "conv(tcgen05)");
+      ar.rewind(mk);
+    } else {
+      check(tc_conv(a, c.tc, err_flag, st, tr), "conv(tcgen05)");
+    }
     if (tr) {
       unsigned long long h[16];
       KK_CUDA(cudaStreamSynchronize(st));

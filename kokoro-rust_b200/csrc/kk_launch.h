@@ -83,6 +83,12 @@ cudaError_t launch_stats_from_sums(const double* part, int C, const ItemTab* ite
 cudaError_t launch_adain_coef(const float* mean, const float* rstd, const float* nw, const float* nb,
                               const float* gb, int ldgb, int B, int C, float2* coef, cudaStream_t st);
 
+// The input transform of a convolution (a.in_mode over a.x, a.in_up2, a.din, AdaIN coef / alpha)
+// applied once, written as bf16 window planes for IN_PRE (layout in ConvArgs::xpre): pre_rows =
+// PRE_PAD_FRONT + a.L_in + PRE_PAD_BACK, planes = 8 * ceil(cin / 64); pad rows and channels past
+// cin are zero.
+cudaError_t launch_prologue_bf16(const ConvArgs& a, void* xpre, long pre_rows, cudaStream_t st);
+
 // AdaIN + leaky ReLU (0.2) followed by the depthwise ConvTranspose1d(k3, s2, p1, op1) "pool"
 // (adain_apply_seg + dw_convT_k3s2, kernels/kokoro.cu:152-167, 317-334): x [L][C] -> y [2L][ldy]
 cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw,

@@ -85,6 +85,17 @@ extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_cas
   a.stat = (double*)dst.p;
   a.dout = Dom{(const int*)dio.p, 0, 0, 0, c->rows_out};
   if (!tc_supported(a, t)) return fail(KK_ERR_INVALID_ARG, "shape not supported by the tcgen05 kernel");
+  DevBuf dpre;
+  if (c->pre) {
+    a.pre_rows = PRE_PAD_FRONT + (long)c->rows_in + PRE_PAD_BACK;
+    if (cudaMalloc(&dpre.p, (size_t)((c->cin + 63) / 64) * 8 * a.pre_rows * 16) != cudaSuccess)
+      return fail(KK_ERR_OOM, "device allocation failed");
+    e = launch_prologue_bf16(a, dpre.p, a.pre_rows, st);
+    if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+    a.xpre = dpre.p;
+    a.in_mode = IN_PRE;
+    a.in_up2 = 0;
+  }
   // KK_TC_TRACE=1 (diagnostics): per-role cycle accounting of CTA 0, printed to stderr
   DevBuf dtr;
   if (getenv("KK_TC_TRACE") && cudaMalloc(&dtr.p, 16 * sizeof(unsigned long long)) == cudaSuccess)
@@ -108,7 +119,15 @@ extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_cas
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
     cudaEventRecord(e0, st);
-    for (int i = 0; i < timing_iters && e == cudaSuccess; i++) e = tc_conv(a, t, (int*)derr.p, st);
+    for (int i = 0; i < timing_iters && e == cudaSuccess; i++) {
+      if (c->pre) {  // the input transform is part of every launch of the pre route
+        ConvArgs a0 = a;
+        a0.in_mode = c->in_mode, a0.in_up2 = c->up2;
+        e = launch_prologue_bf16(a0, dpre.p, a.pre_rows, st);
+        if (e != cudaSuccess) break;
+      }
+      e = tc_conv(a, t, (int*)derr.p, st);
+    }
     cudaEventRecord(e1, st);
     if (e == cudaSuccess) e = cudaEventSynchronize(e1);
     float ms = 0;

@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       mbar_init(&in_empty[i], TC_NPROD);
     }
     for (int i = 0; i < TC_XST; i++) {
-      mbar_init(&x_full[i], TC_NPROD);
+      mbar_init(&x_full[i], IM == IN_PRE ? 1 : TC_NPROD);  // IN_PRE: the loader's expect_tx arrival
       mbar_init(&x_empty[i], 1);
     }
     for (int i = 0; i < 2; i++) {
@@ -254,6 +254,39 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         p.trace[TR_MMA_WAIT_W] = tww;
         p.trace[TR_MMA_TOTAL] = (unsigned long long)(clock64() - t_start);
         p.trace[TR_TILES] = lt;
+      }
+    }
+  } else if (warp == 2 && IM == IN_PRE) {
+    // ---------------------------------------------------------------- window loader (IN_PRE)
+    // Each window chunk is a contiguous run of win_rows 16-byte plane rows: one bulk copy per
+    // chunk, straight into the MMA operand layout.
+    if (lane == 0) {
+      const uint8_t* planes = (const uint8_t*)a.xpre;
+      uint32_t xit = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+        const long row0 = (long)(tile % p.n_tt) * TC_N - a.pad + PRE_PAD_FRONT;
+        for (int cb = 0; cb < p.ncb; cb++, xit++) {
+          const int xs = xit % TC_XST;
+          if (!mbar_wait(&x_empty[xs], ((xit / TC_XST) & 1) ^ 1, abort_flag, p.err)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&x_full[xs], 8u * p.win_rows * 16u);
+          for (int j = 0; j < 8; j++)
+            bulk_g2s(xbuf + xs * xbytes + (size_t)j * 16 * p.win_pad,
+                     planes + ((size_t)(cb * 8 + j) * a.pre_rows + row0) * 16, (uint32_t)p.win_rows * 16u,
+                     &x_full[xs]);
+        }
+      }
+      if (*abort_flag && xit > 0) {
+        // drain this CTA's copies still in flight before the shared memory is released
+        const uint32_t first = xit > TC_XST ? xit - TC_XST : 0;
+        for (uint32_t jx = first; jx < xit; jx++) {
+          const unsigned long long t0 = tc_now();
+          while (!mbar_try(&x_full[jx % TC_XST], (jx / TC_XST) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+          }
+        }
       }
     }
   } else if (warp == 2) {
@@ -452,7 +485,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       p.trace[TR_EP_RES] = t_res;
       p.trace[TR_EP_STBUF] = t_stbuf;
     }
-  } else if (warp >= 4 + TC_NEPI) {
+  } else if (warp >= 4 + TC_NEPI && IM != IN_PRE) {
     // ---------------------------------------------------------------- activation producers
     // At each tile the producers first resolve the item of every window row into shared memory
     // (one lookup per row, shared by all channel blocks). Then, box by box, thread (box row
@@ -600,6 +633,116 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   }
 }
 
+// ------------------------------------------------------------------------------ IN_PRE prologue
+
+// Block (256 plane rows, 64-channel block cb); warp j converts plane cb * 8 + j (channels 4j..4j+3
+// and 32+4j..32+4j+3) of those rows, lane = row within each of 8 groups of 32. The 8 warps together
+// read each input row's 256 bytes once, at the same time (shared sectors hit L1), and each warp
+// writes 512 contiguous bytes of its plane per group. All 8 rows' item lookups and loads are issued
+// before any is used (8 rows in flight per thread: the pass is bound by memory latency otherwise);
+// the transform uses the producer warps' arithmetic, with the item's coefficients cached.
+__global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, uint4* __restrict__ out, long pre_rows) {
+  constexpr int R = 8;
+  const int pl = blockIdx.y * 8 + (threadIdx.x >> 5);
+  const long r0 = blockIdx.x * 256L + (threadIdx.x & 31);
+  const int cin = a.cin;
+  const int cA = (pl >> 3) * TC_KB + 4 * (pl & 7);  // channels cA .. cA + 3 and cA + 32 .. cA + 35
+  const bool vec = cA + 36 <= cin && (a.ldx % 4) == 0 && ((((uintptr_t)a.x) & 15) == 0);
+  const bool affine = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE;
+  const bool snake = a.in_mode == IN_ADAIN_SNAKE;
+  const bool leaky_on = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_LEAKY_MASK;
+  int bm[R];
+#pragma unroll
+  for (int m = 0; m < R; m++) {
+    const long g = r0 + 32 * m - PRE_PAD_FRONT;
+    bm[m] = (g >= 0 && g < a.L_in && r0 + 32 * m < pre_rows) ? (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)g))
+                                                             : -1;
+  }
+  float v[R][8];
+#pragma unroll
+  for (int m = 0; m < R; m++) {
+    const long g = r0 + 32 * m - PRE_PAD_FRONT;
+#pragma unroll
+    for (int e = 0; e < 8; e++) v[m][e] = 0.0f;
+    if (g >= 0 && g < a.L_in) {
+      const float* src = a.x + (long)(a.in_up2 ? (g >> 1) : g) * a.ldx;
+      if (vec) {
+        const float4 lo = __ldg(reinterpret_cast<const float4*>(src + cA));
+        const float4 hi = __ldg(reinterpret_cast<const float4*>(src + cA + 32));
+        v[m][0] = lo.x, v[m][1] = lo.y, v[m][2] = lo.z, v[m][3] = lo.w;
+        v[m][4] = hi.x, v[m][5] = hi.y, v[m][6] = hi.z, v[m][7] = hi.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int c = cA + (e < 4 ? e : 28 + e);
+          if (c < cin) v[m][e] = __ldg(src + c);
+        }
+      }
+    }
+  }
+  float al[8], ial[8];
+  if (snake) {
+#pragma unroll
+    for (int e = 0; e < 8; e++) {
+      const int c = cA + (e < 4 ? e : 28 + e);
+      al[e] = c < cin ? __ldg(a.alpha + c) : 1.0f;
+      ial[e] = 1.0f / al[e];
+    }
+  }
+  float2 q[8];
+  int cached = -1;
+#pragma unroll
+  for (int m = 0; m < R; m++) {
+    const long rr = r0 + 32 * m;
+    if (rr >= pre_rows) break;
+    const int b = bm[m];
+    float o8[8];
+    if (b < 0) {
+#pragma unroll
+      for (int e = 0; e < 8; e++) o8[e] = 0.0f;
+    } else if (affine) {
+      if (b != cached) {
+        cached = b;
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const int c = cA + (e < 4 ? e : 28 + e);
+          q[e] = c < cin ? __ldg(a.coef + (long)b * cin + c) : make_float2(0.0f, 0.0f);
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float t = fmaf(v[m][e], q[e].x, q[e].y);
+        if (snake) {
+          const float sn = __sinf(al[e] * t);
+          t = fmaf(ial[e], sn * sn, t);
+        } else {
+          t = leaky(t, a.slope);
+        }
+        o8[e] = t;
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; e++) o8[e] = leaky_on ? leaky(v[m][e], a.slope) : v[m][e];
+    }
+    uint4 pk;
+    __nv_bfloat162 h0 = __floats2bfloat162_rn(o8[0], o8[1]);
+    __nv_bfloat162 h1 = __floats2bfloat162_rn(o8[2], o8[3]);
+    __nv_bfloat162 h2 = __floats2bfloat162_rn(o8[4], o8[5]);
+    __nv_bfloat162 h3 = __floats2bfloat162_rn(o8[6], o8[7]);
+    memcpy(&pk.x, &h0, 4);
+    memcpy(&pk.y, &h1, 4);
+    memcpy(&pk.z, &h2, 4);
+    memcpy(&pk.w, &h3, 4);
+    out[(long)pl * pre_rows + rr] = pk;
+  }
+}
+
+cudaError_t launch_prologue_bf16(const ConvArgs& a, void* xpre, long pre_rows, cudaStream_t st) {
+  const int ncb = (a.cin + TC_KB - 1) / TC_KB;
+  prologue_bf16_kernel<<<dim3((unsigned)((pre_rows + 255) / 256), ncb), 256, 0, st>>>(a, (uint4*)xpre, pre_rows);
+  return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------------------ host side
 
 bool tc_available() {
@@ -682,7 +825,7 @@ bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
   if (ring_stages(win_pad_of(a.K, a.dil)) == 0) return false;
   // every global operand moves by TMA: 16-byte aligned bases and row strides
-  if (!rows_ok(a.x, a.ldx) || !rows_ok(a.y, a.ldy)) return false;
+  if ((a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) || !rows_ok(a.y, a.ldy)) return false;
   if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
   return true;
 }
@@ -710,6 +853,10 @@ static TcKernelFn pick_kernel(int im, int up, int om, int* idx) {
       {IN_LEAKY_MASK, 0, OUT_PLUS, tc_conv_kernel<IN_LEAKY_MASK, 0, OUT_PLUS>},
       {IN_MASK, 0, OUT_STORE, tc_conv_kernel<IN_MASK, 0, OUT_STORE>},
       {IN_MASK, 1, OUT_STORE, tc_conv_kernel<IN_MASK, 1, OUT_STORE>},
+      {IN_PRE, 0, OUT_STORE, tc_conv_kernel<IN_PRE, 0, OUT_STORE>},
+      {IN_PRE, 0, OUT_ADD, tc_conv_kernel<IN_PRE, 0, OUT_ADD>},
+      {IN_PRE, 0, OUT_PLUS, tc_conv_kernel<IN_PRE, 0, OUT_PLUS>},
+      {IN_PRE, 0, OUT_GELU, tc_conv_kernel<IN_PRE, 0, OUT_GELU>},
   };
   const int n = (int)(sizeof(table) / sizeof(table[0]));
   for (int i = 0; i < n; i++)
@@ -762,7 +909,9 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   memset(&p, 0, sizeof(p));
   p.trace = trace;
   const long x_rows = a.in_up2 ? (a.L_in + 1) / 2 : a.L_in;
-  bool maps = make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, TC_BOX_ROWS) &&
+  const bool pre = a.in_mode == IN_PRE;
+  if (pre && (!a.xpre || (((uintptr_t)a.xpre) & 15) != 0)) return cudaErrorInvalidValue;
+  bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, TC_BOX_ROWS)) &&
               make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
   if (maps && a.out_mode == OUT_ADD) maps = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
   if (maps && a.out_mode == OUT_PLUS) maps = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc, 32, TC_EC);
@@ -775,7 +924,7 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   p.win_rows = TC_N + (a.K - 1) * a.dil;
   p.win_pad = win_pad_of(a.K, a.dil);
   p.err = err;
-  p.rst = ring_stages(p.win_pad);
+  p.rst = pre ? 0 : ring_stages(p.win_pad);
   const size_t smem = tc_smem(p.win_pad, p.rst);
   int dev = 0;
   cudaGetDevice(&dev);
@@ -785,7 +934,7 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
     g_num_sms[dev] = n;
   }
   int ci = 0;
-  const TcKernelFn fn = pick_kernel(a.in_mode, a.in_up2, a.out_mode, &ci);
+  const TcKernelFn fn = pick_kernel(a.in_mode, pre ? 0 : a.in_up2, a.out_mode, &ci);
   if (dev < 64 && !(g_attr_set[dev] & (1u << ci))) {
     cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, TC_SMEM_MAX);
     if (e != cudaSuccess) return e;

@@ -64,12 +64,13 @@ class ConvCase(ctypes.Structure):
                 ("pad", ctypes.c_int), ("rows_in", ctypes.c_int), ("ldx", ctypes.c_int), ("up2", ctypes.c_int),
                 ("in_mode", ctypes.c_int), ("slope", ctypes.c_float), ("rows_out", ctypes.c_int),
                 ("ldy", ctypes.c_int), ("out_mode", ctypes.c_int), ("oscale", ctypes.c_float),
-                ("ldsc", ctypes.c_int), ("n_items", ctypes.c_int), ("item_in", _P), ("item_out", _P)]
+                ("ldsc", ctypes.c_int), ("n_items", ctypes.c_int), ("item_in", _P), ("item_out", _P),
+                ("pre", ctypes.c_int)]
 
 
 def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1, up2=0, in_mode=0,
                   slope=0.2, out_mode=0, oscale=1.0, bias=None, coef=None, alpha=None, sc=None, y=None,
-                  n_items=None, want_stats=False, timing_iters=0):
+                  n_items=None, want_stats=False, timing_iters=0, pre=0):
     """One convolution through the tcgen05 kernel (kk_conv_selftest). x [rows][ldx] f32, w torch
     layout [cout][cin][K]; returns y [rows_out][ldy] (and [n_items][cout][2] statistics); with
     timing_iters > 0 returns (result, device ms per launch)."""
@@ -83,7 +84,7 @@ def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1
     y = np.ascontiguousarray(np.zeros((rows_out, cout), np.float32) if y is None else y, np.float32)
     c = ConvCase(cin, cout, K, dil, pad, len(item_in), x.shape[1], up2, in_mode, slope, rows_out, y.shape[1],
                  out_mode, oscale, 0 if sc is None else sc.shape[1], n_items,
-                 item_in.ctypes.data, item_out.ctypes.data)
+                 item_in.ctypes.data, item_out.ctypes.data, pre)
     keep = []
 
     def ptr(a):

@@ -1,5 +1,7 @@
 """The bf16 tcgen05 convolution kernel on its own, through kk_conv_selftest, against a float64
-convolution of the same bf16-rounded operands.
+convolution of the same bf16-rounded operands, on both input routes: the producer warps transform
+the input inside the conv ("fused"), or a prologue kernel writes bf16 window planes that the conv
+bulk-copies ("pre", the route of layers with more than 128 output channels).
 
 The kernel stages its input as bf16 after the layer's prologue (gap mask, AdaIN folded to
 x * A + B, leaky ReLU or Snake, nearest x2 upsample) and its weights as bf16, accumulates in fp32
@@ -102,8 +104,9 @@ CASES = [
 ]
 
 
+@pytest.mark.parametrize("pre", [0, 1], ids=["fused", "pre"])
 @pytest.mark.parametrize("case", CASES, ids=[c[0] for c in CASES])
-def test_tc_conv_matches_fp64_on_bf16_operands(kk, case):
+def test_tc_conv_matches_fp64_on_bf16_operands(kk, case, pre):
     import kokoro_rust_b200.engine as E
     name, cin, cout, K, dil, in_mode, out_mode, up2, stats, ldx_extra, ldy_extra = case
     rng = np.random.default_rng(zlib.crc32(name.encode()))
@@ -125,7 +128,7 @@ def test_tc_conv_matches_fp64_on_bf16_operands(kk, case):
     oscale = float(1 / np.sqrt(2.0))
     res = E.conv_selftest(0, x=x, w=w, item_in=items_in, item_out=items_out, rows_out=rows_out, pad=pad, dil=dil,
                           up2=up2, in_mode=in_mode, slope=0.2, out_mode=out_mode, oscale=oscale, bias=bias,
-                          coef=coef, alpha=alpha, sc=sc, y=y0.copy(), n_items=n_items, want_stats=stats)
+                          coef=coef, alpha=alpha, sc=sc, y=y0.copy(), n_items=n_items, want_stats=stats, pre=pre)
     y, st = res if stats else (res, None)
     ref = reference(x, w, bias, items_in, rows_out, pad, dil, up2, in_mode, 0.2, out_mode, oscale, coef, alpha, sc,
                     y0)
