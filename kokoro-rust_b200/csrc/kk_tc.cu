@@ -48,7 +48,7 @@ constexpr int TC_M = 128;
 constexpr int TC_N = 256;
 constexpr int TC_KB = 64;
 constexpr int TC_WST = 3;                        // weight ring stages
-constexpr int TC_XST = 2;                        // activation-window stages
+constexpr int TC_XST_MAX = 4;                    // activation-window stages (2 on the fused route)
 constexpr int TC_RST_MAX = 6;                    // input-box ring stages (fewer when shared memory is short)
 constexpr int TC_BOX_ROWS = 32;
 constexpr int TC_INBOX = TC_BOX_ROWS * TC_KB * 4;  // 8 KB f32 input box
@@ -81,7 +81,8 @@ struct TcArgs {
   int n_tt;       // time tiles of 256
   int win_rows;   // 256 + (K - 1) * dil
   int win_pad;    // window rows rounded to 8, + 1 (bank-conflict-free producer stores)
-  int rst;        // input-box ring stages
+  int rst;        // input-box ring stages (0 on the pre-transform route)
+  int xst;        // activation-window stages
   int* err;
   unsigned long long* trace;  // optional cycle accounting of CTA 0 (diagnostics), 16 counters
 };
@@ -122,8 +123,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   const uint32_t xbytes = 8u * p.win_pad * 16u;
   const int RST = p.rst;
   uint8_t* wbuf = smem;                                       // TC_WST x 16 KB
-  uint8_t* xbuf = wbuf + TC_WST * TC_WBLOCK;                  // TC_XST x xbytes
-  uint8_t* inring = xbuf + TC_XST * xbytes;                   // RST x 8 KB
+  const int XST = p.xst;
+  uint8_t* xbuf = wbuf + TC_WST * TC_WBLOCK;                  // XST x xbytes
+  uint8_t* inring = xbuf + XST * xbytes;                      // RST x 8 KB
   uint8_t* epi = inring + RST * TC_INBOX;                     // TC_NEPI x TC_EPI_WARP_BYTES
   uint64_t* bars = (uint64_t*)(epi + TC_NEPI * TC_EPI_WARP_BYTES);
   uint64_t* w_full = bars;
@@ -131,8 +133,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   uint64_t* in_full = w_empty + TC_WST;
   uint64_t* in_empty = in_full + TC_RST_MAX;
   uint64_t* x_full = in_empty + TC_RST_MAX;
-  uint64_t* x_empty = x_full + TC_XST;
-  uint64_t* acc_full = x_empty + TC_XST;
+  uint64_t* x_empty = x_full + TC_XST_MAX;
+  uint64_t* acc_full = x_empty + TC_XST_MAX;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* res_full = acc_empty + 2;                         // [TC_NEPI][TC_RES_DEPTH]
   uint32_t* tmem_slot = (uint32_t*)(res_full + TC_NEPI * TC_RES_DEPTH);
@@ -152,7 +154,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       mbar_init(&in_full[i], 1);
       mbar_init(&in_empty[i], TC_NPROD);
     }
-    for (int i = 0; i < TC_XST; i++) {
+    for (int i = 0; i < XST; i++) {
       mbar_init(&x_full[i], IM == IN_PRE ? 1 : TC_NPROD);  // IN_PRE: the loader's expect_tx arrival
       mbar_init(&x_empty[i], 1);
     }
@@ -219,8 +221,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         const uint32_t d = tmem + ab * TC_N;
         bool ok = true;
         for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
-          const int xs = xit % TC_XST;
-          if (!mbar_wait_t(&x_full[xs], (xit / TC_XST) & 1, abort_flag, p.err, trc ? &twx : nullptr)) {
+          const int xs = xit % XST;
+          if (!mbar_wait_t(&x_full[xs], (xit / XST) & 1, abort_flag, p.err, trc ? &twx : nullptr)) {
             ok = false;
             break;
           }
@@ -267,8 +269,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
         const long row0 = (long)(tile % p.n_tt) * TC_N - a.pad + PRE_PAD_FRONT;
         for (int cb = 0; cb < p.ncb; cb++, xit++) {
-          const int xs = xit % TC_XST;
-          if (!mbar_wait(&x_empty[xs], ((xit / TC_XST) & 1) ^ 1, abort_flag, p.err)) {
+          const int xs = xit % XST;
+          if (!mbar_wait(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err)) {
             ok = false;
             break;
           }
@@ -281,10 +283,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       }
       if (*abort_flag && xit > 0) {
         // drain this CTA's copies still in flight before the shared memory is released
-        const uint32_t first = xit > TC_XST ? xit - TC_XST : 0;
+        const uint32_t first = xit > (uint32_t)XST ? xit - XST : 0;
         for (uint32_t jx = first; jx < xit; jx++) {
           const unsigned long long t0 = tc_now();
-          while (!mbar_try(&x_full[jx % TC_XST], (jx / TC_XST) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
+          while (!mbar_try(&x_full[jx % XST], (jx / XST) & 1) && tc_now() - t0 < TC_TIMEOUT_NS) {
           }
         }
       }
@@ -516,8 +518,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       }
       asm volatile("bar.sync 1, %0;" ::"n"(TC_NPROD * 32) : "memory");
       for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
-        const int xs = xit % TC_XST;
-        if (!mbar_wait_t(&x_empty[xs], ((xit / TC_XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
+        const int xs = xit % XST;
+        if (!mbar_wait_t(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
           ok = false;
           break;
         }
@@ -801,10 +803,10 @@ cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights*
   return cudaSuccess;
 }
 
-static size_t tc_smem(int win_pad, int rst) {
-  return (size_t)TC_WST * TC_WBLOCK + (size_t)TC_XST * 8 * win_pad * 16 + (size_t)rst * TC_INBOX +
+static size_t tc_smem(int win_pad, int rst, int xst = 2) {
+  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + (size_t)rst * TC_INBOX +
          (size_t)TC_NEPI * TC_EPI_WARP_BYTES +
-         (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST + 4 + TC_NEPI * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
+         (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST_MAX + 4 + TC_NEPI * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
 }
 
 static inline int win_pad_of(int K, int dil) { return ((TC_N + (K - 1) * dil + 7) / 8) * 8 + 1; }
@@ -925,7 +927,10 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   p.win_pad = win_pad_of(a.K, a.dil);
   p.err = err;
   p.rst = pre ? 0 : ring_stages(p.win_pad);
-  const size_t smem = tc_smem(p.win_pad, p.rst);
+  p.xst = 2;
+  if (pre)  // no input ring: spend its shared memory on deeper window staging
+    while (p.xst < TC_XST_MAX && tc_smem(p.win_pad, 0, p.xst + 1) <= (size_t)TC_SMEM_MAX) p.xst++;
+  const size_t smem = tc_smem(p.win_pad, p.rst, p.xst);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && g_num_sms[dev] == 0) {
