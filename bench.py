@@ -322,6 +322,14 @@ def main():
             floor_ms = sum(max(r[2] / (peak * 1e12), r[3] / (hbm * 1e9)) * 1e3 for r in recs)
             hbm_ms = sum(r[1] for r in recs if r[3] / (hbm * 1e9) > r[2] / (peak * 1e12))
             tot = sum(r[1] for r in recs)
+            # DRAM bytes per conv launch from the committed full-size ncu capture of one forward
+            try:
+                for ln in open(os.path.join(ROOT, "profiles", "traffic_conv_config4.md")):
+                    if ln.startswith("traffic_bytes_per_launch:") and args.workload == "config4":
+                        roof["traffic"] = float(ln.split(":")[1])
+                        roof["traffic_source"] = "profiles/traffic_conv_config4.md (ncu, one forward, per launch)"
+            except OSError:
+                pass
             roof["mixed_floor"] = {"floor_ms": floor_ms, "ms": tot, "frac": floor_ms / max(tot, 1e-9),
                                    "hbm_bound_time_share": hbm_ms / max(tot, 1e-9),
                                    "bytes": sum(r[3] for r in recs), "hbm_peak_gbs": hbm}
