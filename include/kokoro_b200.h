@@ -221,7 +221,17 @@ KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const
  */
 KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len, const float* qkv,
                                        float* ctx);
-/* Message of the last kk_conv_selftest / kk_attention_selftest failure on this thread. */
+/*
+ * kk_lstm_selftest -- diagnostics: one bidirectional LSTM recurrence (hidden 256) over 1 to 32
+ * items, on host buffers. tc = 0: the fp32 cluster kernel (both precision modes' semantics);
+ * tc = 1: the BF16 mode's tcgen05 recurrence. gx [sum len][2048] gate inputs (W_ih x + b_ih;
+ * direction d, gate g (i, f, g, o), unit j at column d*1024 + g*256 + j), whh [2][1024][256],
+ * bhh [2][1024]; out [sum len][512] receives h (direction d, unit j at d*256 + j). No counterpart in
+ * the reference (kernel-level test of kernels/kokoro.cu:400-450's recurrence).
+ */
+KK_API kk_status kk_lstm_selftest(int cuda_ordinal, int tc, int n_items, const int32_t* len, const float* gx,
+                                  const float* whh, const float* bhh, float* out);
+/* Message of the last kk_conv_selftest / kk_attention_selftest / kk_lstm_selftest failure on this thread. */
 KK_API const char* kk_conv_selftest_error(void);
 
 /* Bytes of device memory the engine currently holds (weights + arena). */

@@ -978,6 +978,8 @@ void Engine::lstm(const Lstm& L, const float* x, int ldx, int rows, const std::v
   a.glen = upload(glen.data(), glen.size());
   a.gact = upload(gact.data(), gact.size());
   a.G = G, a.IPG = IPG, a.Tmax = Tmax;
+  a.tc = precision == KK_PRECISION_BF16 && tc_ok;
+  a.err = err_flag;
   cudaEvent_t e0;
   prof_begin(&e0);
   check(launch_lstm(a, st), "lstm");

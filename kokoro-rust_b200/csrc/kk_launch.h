@@ -62,6 +62,8 @@ struct LstmArgs {
   const int* glen;    // [G][IPG] its length (unused slots 0)
   const int* gact;    // [G][Tmax] members of group g still running at step s
   int G, IPG, Tmax;
+  int tc;             // 1: tcgen05 recurrence (BF16 mode: bf16 hi/lo split operands, fp32 accumulation)
+  int* err;           // tc: set to 4 if an MMA completion wait expires
 };
 constexpr int LSTM_IPG = 32;
 cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st);

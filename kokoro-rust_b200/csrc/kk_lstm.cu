@@ -20,7 +20,11 @@
 #include <stdio.h>
 #include <stdlib.h>
 
+#include <cuda_bf16.h>
+#include <string.h>
+
 #include "kk_launch.h"
+#include "kk_tc_ptx.cuh"
 
 namespace kk {
 
@@ -194,9 +198,221 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
   }
 }
 
+// ------------------------------------------------------------------------------ tcgen05 variant
+//
+// BF16 precision mode. Same clusters, groups and cell arithmetic; the recurrent product of a step,
+// G[128 gate rows][32 items] = W_hh[rows of this CTA's 32 units][256] x H[256][32 items], runs on
+// the tensor cores with both operands split into bf16 pairs (x = hi + lo, hi = bf16(x),
+// lo = bf16(x - hi)): G = Wh Hh + Wh Hl + Wl Hh accumulated in fp32 in TMEM (48 MMAs of
+// M 128 x N 32 x K 16; the dropped Wl Hl term is below 2^-16 relative). A rows are ordered
+// unit * 4 + gate, so the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane
+// transpose through shared memory hands each thread one unit's four gates for 4 items. The new h
+// is split into bf16 hi / lo and pushed straight into every CTA's B operand of the next step.
+
+constexpr int LT_ROWS = 128;                   // gate rows per CTA (32 units x 4 gates)
+constexpr int LT_KC = LC_H / 8;                // 8-element K chunks of the recurrent product
+constexpr int LT_ABYTES = LT_KC * LT_ROWS * 16;  // one bf16 W image (64 KB)
+constexpr int LT_BBYTES = LT_KC * LC_IPG * 16;   // one bf16 H image (16 KB)
+constexpr int LT_GXLD = 17;                    // transpose staging row (floats)
+constexpr uint32_t LT_IDESC = idesc_bf16(LT_ROWS, LC_IPG);
+
+__host__ __device__ constexpr size_t lt_smem() {
+  return 2 * (size_t)LT_ABYTES + 4 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
+}
+
+__device__ __forceinline__ uint32_t bf16_bits(float x) {
+  __nv_bfloat16 h = __float2bfloat16_rn(x);
+  unsigned short u;
+  memcpy(&u, &h, 2);
+  return u;
+}
+
+__global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_kernel(const LstmArgs a) {
+  extern __shared__ __align__(1024) uint8_t sm8[];
+  uint8_t* Ahi = sm8;
+  uint8_t* Alo = Ahi + LT_ABYTES;
+  uint8_t* Bb = Alo + LT_ABYTES;                                  // [2 stages][hi, lo] H images
+  float* Tile = reinterpret_cast<float*>(Bb + 4 * LT_BBYTES);     // [32 items][LC_TLD] new h (f32)
+  float* Gx = Tile + LC_IPG * LC_TLD;                             // [8 warps][32 lanes][LT_GXLD]
+  __shared__ uint64_t bar;
+  __shared__ uint32_t tslot;
+  __shared__ int bad;
+  const int rank = (int)cl_rank();
+  const int cl = blockIdx.x / LC_CL;
+  const int dir = cl & 1, g = cl >> 1;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // W_hh rows of this CTA's units as bf16 hi / lo operand images (K-major, 8-row x 16-byte cores)
+  {
+    const float* W = a.whh + (size_t)dir * 4 * LC_H * LC_H;
+    for (int idx = tid; idx < LT_ROWS * LC_H; idx += 256) {
+      const int ar = idx >> 8, k = idx & 255;
+      const int u = rank * 32 + (ar >> 2), gate = ar & 3;
+      const float w = W[(size_t)(gate * LC_H + u) * LC_H + k];
+      const uint32_t hi = bf16_bits(w);
+      const float whi = __uint_as_float(hi << 16);
+      const uint32_t lo = bf16_bits(w - whi);
+      const size_t off = (size_t)(k >> 3) * (LT_ROWS * 16) + ar * 16 + (k & 7) * 2;
+      *reinterpret_cast<unsigned short*>(Ahi + off) = (unsigned short)hi;
+      *reinterpret_cast<unsigned short*>(Alo + off) = (unsigned short)lo;
+    }
+    for (int i = tid; i < 2 * LT_BBYTES / 16; i += 256) reinterpret_cast<uint4*>(Bb)[i] = make_uint4(0, 0, 0, 0);
+  }
+  // this thread's cells: unit ul (lane quarter q = warp % 4 holds units 8q .. 8q + 7), items i0 .. i0 + 3
+  const int q = warp & 3, hf = warp >> 2;
+  const int ul = 8 * q + (lane >> 2);
+  const int u = rank * 32 + ul;
+  const int i0 = hf * 16 + 4 * (lane & 3);
+  const int* gs = a.gstart + g * LC_IPG;
+  const int* gl = a.glen + g * LC_IPG;
+  int st_[4], ln_[4];
+#pragma unroll
+  for (int m = 0; m < 4; m++) st_[m] = gs[i0 + m], ln_[m] = gl[i0 + m];
+  float bh[4];
+#pragma unroll
+  for (int gt = 0; gt < 4; gt++) bh[gt] = a.bhh[dir * 4 * LC_H + gt * LC_H + u];
+  float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  // push role: item pi, part (0 hi, 1 lo), 8-unit chunk kc4 of this CTA's 32 units
+  const int pi = tid >> 3, part = (tid >> 2) & 1, kc4 = tid & 3;
+  const int pst = gs[pi], pln = gl[pi];
+
+  if (tid == 0) {
+    mbar_init(&bar, 1);
+    bad = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(smem_u32(&tslot))
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  fence_proxy_async();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  const int* act = a.gact + (long)g * a.Tmax;
+  volatile int abort_flag = 0;
+  cluster_sync();  // every CTA of the cluster is running and initialised before remote stores
+
+  for (int s = 0; s < a.Tmax; s++) {
+    const int na = act[s];
+    if (na == 0) break;  // same for the whole group, so for every CTA of the cluster
+    const int cur = s & 1;
+    // gate inputs of this thread's cells, loaded ahead of the product
+    float gxv[4][4];
+#pragma unroll
+    for (int m = 0; m < 4; m++) {
+#pragma unroll
+      for (int gt = 0; gt < 4; gt++) gxv[m][gt] = 0.0f;
+      if (i0 + m < na) {
+        const int t = dir == 0 ? s : ln_[m] - 1 - s;
+        const float* gp = a.gx + (long)(st_[m] + t) * a.ldgx + dir * 4 * LC_H + u;
+#pragma unroll
+        for (int gt = 0; gt < 4; gt++) gxv[m][gt] = __ldg(gp + gt * LC_H);
+      }
+    }
+    if (tid == 0 && !bad) {
+      fence_proxy_async();  // H images arrived through generic-proxy stores
+      tc_fence_after();
+      const uint32_t bh0 = smem_u32(Bb + (cur * 2 + 0) * LT_BBYTES), bl0 = smem_u32(Bb + (cur * 2 + 1) * LT_BBYTES);
+#pragma unroll
+      for (int kk = 0; kk < LT_KC / 2; kk++) {
+        const uint64_t ah = sdesc(smem_u32(Ahi) + kk * 2 * (LT_ROWS * 16), LT_ROWS * 16, 128);
+        const uint64_t al = sdesc(smem_u32(Alo) + kk * 2 * (LT_ROWS * 16), LT_ROWS * 16, 128);
+        const uint64_t bhd = sdesc(bh0 + kk * 2 * (LC_IPG * 16), LC_IPG * 16, 128);
+        const uint64_t bld = sdesc(bl0 + kk * 2 * (LC_IPG * 16), LC_IPG * 16, 128);
+        mma_bf16(tmem, ah, bhd, LT_IDESC, kk > 0);
+        mma_bf16(tmem, ah, bld, LT_IDESC, 1);
+        mma_bf16(tmem, al, bhd, LT_IDESC, 1);
+      }
+      mma_commit(&bar);
+    }
+    if (!bad && !mbar_wait(&bar, (uint32_t)(s & 1), &abort_flag, a.err)) bad = 1;
+    tc_fence_after();
+    __syncthreads();  // bad is uniform from here on
+    if (!bad) {
+      // lane (unit 8q + lane / 4, gate lane % 4) reads its 16 items of this half, then a 4-lane
+      // transpose gives each lane one unit's 4 gates for items i0 .. i0 + 3
+      float v[16];
+      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + hf * 16, v);
+      float* gw = Gx + warp * 32 * LT_GXLD;
+#pragma unroll
+      for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = v[j];
+      __syncwarp();
+#pragma unroll
+      for (int m = 0; m < 4; m++) {
+        if (i0 + m < na) {
+          float d[4];
+#pragma unroll
+          for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
+          const float ig = sigm(gxv[m][0] + (d[0] + bh[0]));
+          const float fg = sigm(gxv[m][1] + (d[1] + bh[1]));
+          const float cg = tanhf(gxv[m][2] + (d[2] + bh[2]));
+          const float og = sigm(gxv[m][3] + (d[3] + bh[3]));
+          c[m] = fg * c[m] + ig * cg;
+          Tile[(i0 + m) * LC_TLD + ul] = og * tanhf(c[m]);
+        }
+      }
+    }
+    tc_fence_before();
+    __syncthreads();  // Tile complete; TMEM and staging reads done
+    if (!bad && pi < na) {
+      const float* hp = Tile + pi * LC_TLD + 8 * kc4;
+      uint32_t w4[4];
+#pragma unroll
+      for (int e = 0; e < 8; e += 2) {
+        uint32_t b0, b1;
+        if (part == 0) {
+          b0 = bf16_bits(hp[e]), b1 = bf16_bits(hp[e + 1]);
+        } else {
+          b0 = bf16_bits(hp[e] - __uint_as_float(bf16_bits(hp[e]) << 16));
+          b1 = bf16_bits(hp[e + 1] - __uint_as_float(bf16_bits(hp[e + 1]) << 16));
+        }
+        w4[e >> 1] = b0 | (b1 << 16);
+      }
+      const float4 pk = make_float4(__uint_as_float(w4[0]), __uint_as_float(w4[1]), __uint_as_float(w4[2]),
+                                    __uint_as_float(w4[3]));
+      const int kc = 4 * rank + kc4;  // 8-unit chunk of the 256 hidden units
+      const uint32_t la = smem_u32(Bb + ((cur ^ 1) * 2 + part) * LT_BBYTES + kc * (LC_IPG * 16) + pi * 16);
+#pragma unroll
+      for (int r = 0; r < LC_CL; r++) st_cluster_v4(la, (uint32_t)r, pk);
+      if (part == 0) {
+        const int t = dir == 0 ? s : pln - 1 - s;
+        float* o = a.out + (long)(pst + t) * a.ldo + dir * LC_H + rank * 32 + 8 * kc4;
+        *reinterpret_cast<float4*>(o) = make_float4(hp[0], hp[1], hp[2], hp[3]);
+        *reinterpret_cast<float4*>(o + 4) = make_float4(hp[4], hp[5], hp[6], hp[7]);
+      }
+    }
+    fence_proxy_async();
+    cluster_sync();  // step s + 1 multiplies the H images every CTA just received
+  }
+  if (bad && tid == 0) atomicExch(a.err, 4);
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem) : "memory");
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_lstm(const LstmArgs& a, cudaStream_t st) {
+  if (a.Tmax == 0 || a.G == 0) return cudaSuccess;
+  if (a.IPG != LC_IPG) return cudaErrorInvalidValue;
+  if (a.tc) {
+    static bool attr_tc[64] = {false};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 64 && !attr_tc[dev]) {
+      cudaError_t e = cudaFuncSetAttribute(lstm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lt_smem());
+      if (e != cudaSuccess) return e;
+      attr_tc[dev] = true;
+    }
+    lstm_tc_kernel<<<dim3(a.G * 2 * LC_CL), dim3(256), lt_smem(), st>>>(a);
+    return cudaGetLastError();
+  }
   if (a.Tmax == 0 || a.G == 0) return cudaSuccess;
   if (a.IPG != LC_IPG) return cudaErrorInvalidValue;
   const size_t smem = sizeof(float) * (2 * LC_IPG * LC_HROW + LC_IPG * LC_TLD + 8 * 128);

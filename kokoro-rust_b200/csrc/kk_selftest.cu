@@ -6,6 +6,7 @@
 #include <stdlib.h>
 #include <string.h>
 #include <string>
+#include <algorithm>
 #include <vector>
 
 #include "../../include/kokoro_b200.h"
@@ -191,6 +192,61 @@ extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items,
   cudaMemcpy(&errh, derr.p, sizeof(int), cudaMemcpyDeviceToHost);
   if (errh) return fail(KK_ERR_TIMEOUT, "a tcgen05 attention wait timed out");
   if (cudaMemcpy(ctx, dc.p, sizeof(float) * rows * 768, cudaMemcpyDeviceToHost) != cudaSuccess)
+    return fail(KK_ERR_CUDA, "output copy failed");
+  return KK_OK;
+}
+
+extern "C" KK_API kk_status kk_lstm_selftest(int cuda_ordinal, int tc, int n_items, const int32_t* len,
+                                             const float* gx, const float* whh, const float* bhh, float* out) {
+  using namespace kk;
+  if (n_items < 1 || n_items > LSTM_IPG || !len || !gx || !whh || !bhh || !out)
+    return fail(KK_ERR_INVALID_ARG, "bad arguments (1 to 32 items)");
+  int rows = 0, Tmax = 0;
+  std::vector<int> gstart(LSTM_IPG, 0), glen(LSTM_IPG, 0);
+  std::vector<int> order(n_items);
+  for (int b = 0; b < n_items; b++) {
+    if (len[b] < 1) return fail(KK_ERR_INVALID_ARG, "item length < 1");
+    order[b] = b;
+  }
+  std::vector<int> start(n_items);
+  for (int b = 0; b < n_items; b++) start[b] = rows, rows += len[b], Tmax = len[b] > Tmax ? len[b] : Tmax;
+  // longest first within the group, as the engine orders it
+  for (int i = 0; i < n_items; i++)
+    for (int j = i + 1; j < n_items; j++)
+      if (len[order[j]] > len[order[i]]) std::swap(order[i], order[j]);
+  for (int r = 0; r < n_items; r++) gstart[r] = start[order[r]], glen[r] = len[order[r]];
+  std::vector<int> gact(Tmax);
+  for (int s2 = 0; s2 < Tmax; s2++) {
+    int n = 0;
+    while (n < LSTM_IPG && glen[n] > s2) n++;
+    gact[s2] = n;
+  }
+  if (cudaSetDevice(cuda_ordinal) != cudaSuccess || (tc && !tc_available()))
+    return fail(KK_ERR_CUDA, "no suitable device");
+  DevBuf dgx, dw, db, dout, dgs, dgl, dga, derr;
+  auto put = [&](DevBuf& b, const void* h, size_t n) -> bool {
+    if (cudaMalloc(&b.p, n) != cudaSuccess) return false;
+    return cudaMemcpy(b.p, h, n, cudaMemcpyHostToDevice) == cudaSuccess;
+  };
+  bool ok = put(dgx, gx, sizeof(float) * rows * 2048) && put(dw, whh, sizeof(float) * 2 * 1024 * 256) &&
+            put(db, bhh, sizeof(float) * 2 * 1024) && put(dgs, gstart.data(), sizeof(int) * LSTM_IPG) &&
+            put(dgl, glen.data(), sizeof(int) * LSTM_IPG) && put(dga, gact.data(), sizeof(int) * Tmax) &&
+            cudaMalloc(&dout.p, sizeof(float) * rows * 512) == cudaSuccess &&
+            cudaMemset(dout.p, 0, sizeof(float) * rows * 512) == cudaSuccess &&
+            cudaMalloc(&derr.p, sizeof(int)) == cudaSuccess && cudaMemset(derr.p, 0, sizeof(int)) == cudaSuccess;
+  if (!ok) return fail(KK_ERR_OOM, "device allocation / copy failed");
+  LstmArgs a;
+  memset(&a, 0, sizeof(a));
+  a.gx = (const float*)dgx.p, a.ldgx = 2048, a.whh = (const float*)dw.p, a.bhh = (const float*)db.p;
+  a.out = (float*)dout.p, a.ldo = 512, a.gstart = (const int*)dgs.p, a.glen = (const int*)dgl.p;
+  a.gact = (const int*)dga.p, a.G = 1, a.IPG = LSTM_IPG, a.Tmax = Tmax, a.tc = tc, a.err = (int*)derr.p;
+  cudaError_t e = launch_lstm(a, nullptr);
+  if (e == cudaSuccess) e = cudaDeviceSynchronize();
+  if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
+  int errh = 0;
+  cudaMemcpy(&errh, derr.p, sizeof(int), cudaMemcpyDeviceToHost);
+  if (errh) return fail(KK_ERR_TIMEOUT, "an LSTM MMA wait timed out");
+  if (cudaMemcpy(out, dout.p, sizeof(float) * rows * 512, cudaMemcpyDeviceToHost) != cudaSuccess)
     return fail(KK_ERR_CUDA, "output copy failed");
   return KK_OK;
 }

@@ -55,6 +55,7 @@ _SIGS = {
     "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int, _P]),
     "kk_conv_selftest_error": (ctypes.c_char_p, []),
     "kk_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P]),
+    "kk_lstm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]),
 }
 
 
@@ -115,6 +116,22 @@ def attention_selftest(ordinal: int, tok_len, qkv):
     if st != KK_OK:
         raise KokoroError(st, lib.kk_conv_selftest_error().decode())
     return ctx
+
+
+def lstm_selftest(ordinal: int, tc: int, lens, gx, whh, bhh):
+    """One BiLSTM recurrence (kk_lstm_selftest): gx [sum len][2048], whh [2][1024][256],
+    bhh [2][1024]; returns h [sum len][512]."""
+    lib = load_library()
+    ln = np.ascontiguousarray(lens, np.int32)
+    gx = np.ascontiguousarray(gx, np.float32)
+    whh = np.ascontiguousarray(whh, np.float32)
+    bhh = np.ascontiguousarray(bhh, np.float32)
+    out = np.zeros((gx.shape[0], 512), np.float32)
+    st = lib.kk_lstm_selftest(ordinal, tc, len(ln), ln.ctypes.data, gx.ctypes.data, whh.ctypes.data, bhh.ctypes.data,
+                              out.ctypes.data)
+    if st != KK_OK:
+        raise KokoroError(st, lib.kk_conv_selftest_error().decode())
+    return out
 
 
 _lib = None
