@@ -336,8 +336,9 @@ struct Engine {
                   float slope, const float* alpha);
   void resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, const Dom& dout, float* y, int ldy,
               const float* gb, int ldgb, const ItemTab* items, int B, int max_n);
+  // in_mean / in_rstd: statistics of xin when the caller already has them (shared by parallel blocks)
   void snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d, const float* gb, int ldgb,
-             const ItemTab* items, int B, int max_n);
+             const ItemTab* items, int B, int max_n, const float* in_mean = nullptr, const float* in_rstd = nullptr);
   void lstm(const Lstm& L, const float* x, int ldx, int rows, const std::vector<int>& start,
             const std::vector<int>& len, float* out, int ldo);
   void linear(const Conv& c, const float* x, int ldx, int rows, float* y, int ldy, int out_mode = OUT_STORE,
@@ -913,14 +914,14 @@ void Engine::resblk(const ResBlk& R, const float* x, int ldx, const Dom& din, co
 
 // AdaINResBlock1 with Snake (src/gpu_batch.rs:137-154): out = x_in + sum_i conv2_i(snake(AdaIN(conv1_i(snake(AdaIN(.))))))
 void Engine::snake(const SnakeBlk& S, const float* xin, float* out, const Dom& d, const float* gb, int ldgb,
-                   const ItemTab* items, int B, int max_n) {
+                   const ItemTab* items, int B, int max_n, const float* in_mean, const float* in_rstd) {
   auto mk = ar.mark();
   const int C = S.c;
   float* h = ar.get<float>((size_t)d.L * C);
   const float* cur = xin;
   const int max_len = max_n * d.scale + d.plus1;
-  float *m1 = nullptr, *r1 = nullptr;
-  stats(xin, C, C, d, items, B, max_len, &m1, &r1);
+  float *m1 = const_cast<float*>(in_mean), *r1 = const_cast<float*>(in_rstd);
+  if (!m1) stats(xin, C, C, d, items, B, max_len, &m1, &r1);
   for (int i = 0; i < 3; i++) {
     float *m2, *r2;
     ConvArgs a = ca(S.c1[i]);
@@ -1074,9 +1075,11 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     dump("y0", y0, L20, 256, 256);
     ar.rewind(mk);
     float* r[3];
+    float *ym, *yr;  // statistics of y0, shared by the three parallel resblocks
+    stats(y0, 256, 256, d20, items, B, max_n * d20.scale + d20.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
       r[j] = ar.get<float>((size_t)L20 * 256);
-      snake(m.rb[j], y0, r[j], d20, gb_dec, ldgb, items, B, max_n);
+      snake(m.rb[j], y0, r[j], d20, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
     check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
     dump("r0_0", r[0], L20, 256, 256);
@@ -1106,9 +1109,11 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     dump("y1", y1, L120, 128, 128);
     ar.rewind(mk);
     float* r[3];
+    float *ym, *yr;  // statistics of y1, shared by the three parallel resblocks
+    stats(y1, 128, 128, d120, items, B, max_n * d120.scale + d120.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
       r[j] = ar.get<float>((size_t)L120 * 128);
-      snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n);
+      snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
     check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
     dump("x2", x2, L120, 128, 128);

@@ -257,37 +257,72 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
 
 // ------------------------------------------------------------------------------ AdaIN statistics
 
-__global__ void stats_partial_kernel(const float* x, int ldx, int C, const ItemTab* items, int scale, int plus1,
-                                     int rs, double* part) {
-  __shared__ double sh[8][32][2];
-  const int b = blockIdx.x, c = blockIdx.y * 32 + (threadIdx.x & 31), lr = threadIdx.x >> 5;
+// Block (item b, 128-channel group, row chunk): thread (float4 lane cl = 4 channels, row lane lr of
+// 8) accumulates shifted f32 sums of its 4 channels over rows r0 + lr, r0 + lr + 8, ... with 4 rows
+// in flight; the 8 row lanes are combined in shared memory and added to the item's f64 sums.
+__global__ void __launch_bounds__(256) stats_partial_kernel(const float* x, int ldx, int C, const ItemTab* items,
+                                                            int scale, int plus1, int chunk, double* part) {
+  __shared__ float sh[8][32][8];
+  const int b = blockIdx.x, cl = threadIdx.x & 31, lr = threadIdx.x >> 5;
+  const int c0 = blockIdx.y * 128 + 4 * cl;
   const ItemTab it = items[b];
   const long start = (long)it.a * scale;
   const int len = it.n * scale + plus1;
-  const int chunk = (len + rs - 1) / rs;
   const int r0 = blockIdx.z * chunk, r1 = min(len, r0 + chunk);
-  double S = 0.0, S2 = 0.0;
-  if (c < C && r0 < r1) {
-    const float shift = x[start * ldx + c];
-    float s = 0.0f, s2 = 0.0f;
-    for (int r = r0 + lr; r < r1; r += 8) {
-      float v = x[(start + r) * ldx + c] - shift;
-      s += v;
-      s2 += v * v;
+  float s[4] = {0, 0, 0, 0}, s2[4] = {0, 0, 0, 0};
+  const bool vec = (ldx % 4) == 0 && ((((uintptr_t)x) & 15) == 0) && c0 + 4 <= C;
+  if (c0 < C && r0 < r1) {
+    float sf[4];
+#pragma unroll
+    for (int e = 0; e < 4; e++) sf[e] = c0 + e < C ? x[start * ldx + c0 + e] : 0.0f;
+    int r = r0 + lr;
+    for (; r + 24 < r1; r += 32) {  // 4 rows in flight
+      float v[4][4];
+#pragma unroll
+      for (int u = 0; u < 4; u++) {
+        const float* p = x + (start + r + 8 * u) * ldx + c0;
+        if (vec) {
+          const float4 q = __ldg(reinterpret_cast<const float4*>(p));
+          v[u][0] = q.x, v[u][1] = q.y, v[u][2] = q.z, v[u][3] = q.w;
+        } else {
+#pragma unroll
+          for (int e = 0; e < 4; e++) v[u][e] = c0 + e < C ? __ldg(p + e) : 0.0f;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++)
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+          const float d = v[u][e] - sf[e];
+          s[e] += d;
+          s2[e] += d * d;
+        }
     }
-    S = s;
-    S2 = s2;
+    for (; r < r1; r += 8) {
+      const float* p = x + (start + r) * ldx + c0;
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        const float d = (c0 + e < C ? __ldg(p + e) : 0.0f) - sf[e];
+        s[e] += d;
+        s2[e] += d * d;
+      }
+    }
   }
-  sh[lr][threadIdx.x & 31][0] = S;
-  sh[lr][threadIdx.x & 31][1] = S2;
+#pragma unroll
+  for (int e = 0; e < 4; e++) sh[lr][cl][e] = s[e], sh[lr][cl][4 + e] = s2[e];
   __syncthreads();
-  if (lr == 0 && c < C && r0 < r1) {
-    for (int k = 1; k < 8; k++) {
-      S += sh[k][threadIdx.x][0];
-      S2 += sh[k][threadIdx.x][1];
+  if (threadIdx.x < 128) {
+    const int c = blockIdx.y * 128 + threadIdx.x;  // one channel per thread
+    const int l2 = threadIdx.x >> 2, e = threadIdx.x & 3;
+    if (c < C && r0 < r1) {
+      double S = 0.0, S2 = 0.0;
+      for (int k = 0; k < 8; k++) {
+        S += sh[k][l2][e];
+        S2 += sh[k][l2][4 + e];
+      }
+      atomicAdd(part + ((long)b * C + c) * 2, S);
+      atomicAdd(part + ((long)b * C + c) * 2 + 1, S2);
     }
-    atomicAdd(part + ((long)b * C + c) * 2, S);
-    atomicAdd(part + ((long)b * C + c) * 2 + 1, S2);
   }
 }
 
@@ -310,11 +345,10 @@ cudaError_t launch_stats(const float* x, int ldx, int C, const ItemTab* items, i
                          int max_len, double* part, float* mean, float* rstd, cudaStream_t st) {
   cudaError_t e = cudaMemsetAsync(part, 0, sizeof(double) * 2L * B * C, st);
   if (e != cudaSuccess) return e;
-  const int cg = (C + 31) / 32;
-  int rs = (4 * 148 + B * cg - 1) / (B * cg);
-  int rmax = (max_len + 511) / 512;
-  rs = max(1, min(rs, rmax));
-  stats_partial_kernel<<<dim3(B, cg, rs), 256, 0, st>>>(x, ldx, C, items, scale, plus1, rs, part);
+  const int cg = (C + 127) / 128;
+  const int chunk = 2048;  // rows per block: long frame-domain items are split over many blocks
+  const int rs = max(1, (max_len + chunk - 1) / chunk);
+  stats_partial_kernel<<<dim3(B, cg, rs), 256, 0, st>>>(x, ldx, C, items, scale, plus1, chunk, part);
   if ((e = cudaGetLastError()) != cudaSuccess) return e;
   stats_final_kernel<<<nblk((long)B * C, 256), 256, 0, st>>>(x, ldx, C, items, B, scale, plus1, part, mean, rstd);
   return cudaGetLastError();
@@ -691,35 +725,45 @@ cudaError_t launch_istft(const float* post, int ldp, const ItemTab* items, Dom d
 
 // ------------------------------------------------------------------------------ glue
 
-__global__ void sum3_kernel(const float* r0, const float* r1, const float* r2, float* y, long n) {
+__global__ void sum3_kernel(const float4* r0, const float4* r1, const float4* r2, float4* y, long n4) {
   long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-  if (i < n) y[i] = ((r0[i] + r1[i]) + r2[i]) / 3.0f;
+  if (i >= n4) return;
+  const float4 a = __ldg(r0 + i), b = __ldg(r1 + i), c = __ldg(r2 + i);
+  y[i] = make_float4(((a.x + b.x) + c.x) / 3.0f, ((a.y + b.y) + c.y) / 3.0f, ((a.z + b.z) + c.z) / 3.0f,
+                     ((a.w + b.w) + c.w) / 3.0f);
 }
 
 cudaError_t launch_sum3(const float* r0, const float* r1, const float* r2, float* y, long n, cudaStream_t st) {
-  sum3_kernel<<<nblk(n, 256), 256, 0, st>>>(r0, r1, r2, y, n);
+  if (n % 4 != 0) return cudaErrorInvalidValue;  // channel counts of the generator are multiples of 4
+  sum3_kernel<<<nblk(n / 4, 256), 256, 0, st>>>((const float4*)r0, (const float4*)r1, (const float4*)r2,
+                                                 (float4*)y, n / 4);
   return cudaGetLastError();
 }
 
 // Stage-1 ReflectionPad1d((1, 0)) per item (reflect_pad_left1_seg, kernels/kokoro.cu:452-467)
 // fused with the noise-branch add: x[o] = pad(y)[o] + xs[o]; y holds 120 N rows, x 120 N + 1.
+// Block of 256 threads = 8 rows x 32 float4 lanes (C = 128 channels per row; wider C loops).
 __global__ void reflect_add_kernel(const float* y, const float* xs, int C, const ItemTab* items, Dom d120, float* x) {
-  long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
-  if (i >= (long)d120.L * C) return;
-  int o = (int)(i / C), c = (int)(i % C);
-  int b = dom_item(d120, o);
-  float v = 0.0f;
+  const int o = blockIdx.x * 8 + (threadIdx.x >> 5);
+  if (o >= d120.L) return;
+  const int b = dom_item(d120, o);
+  long src = -1;
   if (b >= 0) {
-    int s = 120 * items[b].a;
-    v = (o == s) ? y[(long)(s + 1) * C + c] : y[(long)(o - 1) * C + c];
+    const int s = 120 * items[b].a;
+    src = (o == s) ? (long)(s + 1) : (long)(o - 1);
   }
-  x[i] = v + xs[i];
+  for (int c = 4 * (threadIdx.x & 31); c < C; c += 128) {
+    float4 v = src >= 0 ? __ldg(reinterpret_cast<const float4*>(y + src * C + c)) : make_float4(0, 0, 0, 0);
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xs + (long)o * C + c));
+    v.x += a.x, v.y += a.y, v.z += a.z, v.w += a.w;
+    *reinterpret_cast<float4*>(x + (long)o * C + c) = v;
+  }
 }
 
 cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const ItemTab* items, Dom d120, float* x,
                                cudaStream_t st) {
-  long n = (long)d120.L * C;
-  reflect_add_kernel<<<nblk(n, 256), 256, 0, st>>>(y, xs, C, items, d120, x);
+  if (C % 4 != 0) return cudaErrorInvalidValue;
+  reflect_add_kernel<<<(d120.L + 7) / 8, 256, 0, st>>>(y, xs, C, items, d120, x);
   return cudaGetLastError();
 }
 
