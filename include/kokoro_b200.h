@@ -99,6 +99,44 @@ KK_API kk_status kk_forward_batch(kk_engine* e, int n_items, const int64_t* ids,
 KK_API kk_status kk_fetch_audio(kk_engine* e, int item, float* dst, int64_t cap);
 
 /*
+ * Item `item`'s audio of the last forward run with KK_OPT_OUTPUT_PCM16, as PCM_16 samples
+ * (capacity `cap`), and how many of its samples were clipped. The conversion is the reference's WAV
+ * rule (src/wav.rs:76-84), done on the GPU so half the bytes cross PCIe. No counterpart in the
+ * reference (it converts on the CPU in wav::encode).
+ */
+KK_API kk_status kk_fetch_audio_pcm16(kk_engine* e, int item, int16_t* dst, int64_t cap, int64_t* clipped);
+
+/*
+ * WAV output (src/wav.rs): the canonical 44-byte RIFF/WAVE header, PCM_16 (sample * 0x7FFF rounded
+ * half to even, clamped, clipped samples counted; NaN is stored as 0 and counted) or float32 mono.
+ */
+typedef enum { KK_WAV_PCM16 = 0, KK_WAV_FLOAT32 = 1 } kk_wav_format;
+/* Header for data_bytes of audio (wav::header, src/wav.rs:44-61); KK_ERR_INVALID_ARG above the
+   4 GiB RIFF limit (data_bytes > 2^32 - 37), never a wrapped size field. */
+KK_API kk_status kk_wav_header(int fmt, uint32_t sample_rate, uint64_t data_bytes, uint8_t out[44]);
+/* Header + samples into out (capacity cap bytes); n_bytes receives 44 + data size (out may be NULL
+   to query it), clipped the clipped-sample count (wav::encode, src/wav.rs:63-87). */
+KK_API kk_status kk_wav_encode(const float* audio, int64_t n, uint32_t sample_rate, int fmt, uint8_t* out,
+                               int64_t cap, int64_t* n_bytes, int64_t* clipped);
+/* Data size of a WAV file written by kk_wav_encode after checking its header and file size
+   (wav::read_canonical, src/wav.rs:118-130). */
+KK_API kk_status kk_wav_read_canonical(const char* path, int fmt, uint32_t sample_rate, uint64_t* data_bytes);
+/*
+ * wav::assemble (src/wav.rs:132-187): concatenate the samples of WAV parts (each with the sha256
+ * it had when written) into one WAV at dest, in order: one header, then every part's samples. The
+ * result is written to a temporary file next to dest and renamed into place only when every part
+ * was readable, canonical and unchanged (sha256), so dest is the complete new file or untouched.
+ * sha256_out (65 bytes, may be NULL) receives the whole file's hex digest.
+ */
+KK_API kk_status kk_wav_assemble(int n_parts, const char* const* part_paths, const char* const* part_sha256, int fmt,
+                                 uint32_t sample_rate, const char* dest, int sync, char sha256_out[65],
+                                 uint64_t* data_bytes, uint64_t* samples);
+/* Lower-case hex SHA-256 of n bytes (65 bytes with the terminator). */
+KK_API kk_status kk_sha256_hex(const uint8_t* data, int64_t n, char out[65]);
+/* Message of the last WAV-function failure on this thread. */
+KK_API const char* kk_wav_error(void);
+
+/*
  * kk_decode_batch -- decoder + iSTFTNet generator only (the reference's
  * `decoder(asr, F0, N, ref_s[:, :128])`, src/gpu_batch.rs:299-420) on a ragged batch.
  *
@@ -143,8 +181,11 @@ KK_API kk_status kk_decode_batch_noalloc(kk_engine* e, int n_items, const int32_
 typedef enum {
   KK_OPT_KEEP_AUDIO_ON_DEVICE = 1, /* 1: forward leaves audio on the device (no D2H) */
   KK_OPT_SYNC_EACH_STAGE = 2,      /* 1: synchronise after each stage (error localisation) */
-  KK_OPT_PROFILE = 3               /* 1: time every convolution / LSTM / attention launch with
+  KK_OPT_PROFILE = 3,              /* 1: time every convolution / LSTM / attention launch with
                                       CUDA events on the engine stream (see kk_profile_entry) */
+  KK_OPT_OUTPUT_PCM16 = 4          /* 1: forward converts the audio to PCM_16 on the device (the WAV
+                                      rule of kk_wav_encode) and copies only int16 to the host; read
+                                      it with kk_fetch_audio_pcm16 (kk_fetch_audio then refuses) */
 } kk_option;
 KK_API kk_status kk_set_option(kk_engine* e, int option, int64_t value);
 

@@ -263,6 +263,10 @@ struct Engine {
   std::string err;
   std::string ident;
   bool keep_audio_dev = false, sync_each = false;
+  bool pcm16_out = false;                // KK_OPT_OUTPUT_PCM16
+  int16_t* audio_host16 = nullptr;       // pinned PCM_16 of the last forward
+  size_t audio_host16_cap = 0;
+  std::vector<long long> out_clipped;    // per item, with KK_OPT_OUTPUT_PCM16
   long long launches = 0;
   int* err_flag = nullptr;
   bool tc_ok = false;
@@ -349,7 +353,8 @@ struct Engine {
   float* decode_core(int B, int max_n, const ItemTab* items, const int* col_item_n, int LN, float* xcat0, float* f0,
                      float* nc, const float* gb_dec, int ldgb, const uint64_t* seeds_d, const float* noise_d,
                      const long long* noise_off_d);
-  void finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h);
+  // pcm16: honour KK_OPT_OUTPUT_PCM16 (the forward); the vocoder entry returns f32 to its caller
+  void finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h, const int* col_item_n, bool pcm16);
   void forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
                const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
                int64_t* nsamp_out);
@@ -365,6 +370,7 @@ Engine::~Engine() {
   for (void* p : wallocs) cudaFree(p);
   ar.release();
   if (audio_host) cudaFreeHost(audio_host);
+  if (audio_host16) cudaFreeHost(audio_host16);
   for (auto e : ev)
     if (e) cudaEventDestroy(e);
   for (auto e : ev_pool) cudaEventDestroy(e);
@@ -1137,7 +1143,8 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   return audio;
 }
 
-void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h) {
+void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h, const int* col_item_n,
+                          bool pcm16) {
   const size_t n = (size_t)600 * LN;
   out_off.clear();
   out_len.clear();
@@ -1146,7 +1153,30 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
     out_len.push_back(600LL * it.n);
   }
   int errh = 0;
-  if (!keep_audio_dev) {
+  unsigned long long* clip_h = nullptr;
+  if (!keep_audio_dev && pcm16 && pcm16_out) {
+    // PCM_16 on the device: half the bytes cross PCIe
+    if (audio_host16_cap < n) {
+      if (audio_host16) cudaFreeHost(audio_host16);
+      audio_host16 = nullptr;
+      audio_host16_cap = 0;
+      if (cudaHostAlloc(&audio_host16, n * sizeof(int16_t), cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        audio_host16 = nullptr;
+        throw KKError(KK_ERR_OOM, "pinned audio buffer");
+      }
+      audio_host16_cap = n;
+    }
+    const int B = (int)items_h.size();
+    int16_t* q = ar.get<int16_t>(n);
+    unsigned long long* clip = ar.get<unsigned long long>((size_t)std::max(B, 1));
+    KK_CUDA(cudaMemsetAsync(clip, 0, sizeof(unsigned long long) * std::max(B, 1), st));
+    check(launch_pcm16(audio_d, (long)n, col_item_n, q, clip, st), "pcm16");
+    KK_CUDA(cudaMemcpyAsync(audio_host16, q, n * sizeof(int16_t), cudaMemcpyDeviceToHost, st));
+    clip_h = (unsigned long long*)pin.alloc(sizeof(unsigned long long) * std::max(B, 1));
+    KK_CUDA(cudaMemcpyAsync(clip_h, clip, sizeof(unsigned long long) * std::max(B, 1), cudaMemcpyDeviceToHost, st));
+    d2h_bytes += (double)(n * sizeof(int16_t));
+  } else if (!keep_audio_dev) {
     if (audio_host_cap < n) {
       if (audio_host) cudaFreeHost(audio_host);
       audio_host = nullptr;
@@ -1166,6 +1196,9 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
   KK_CUDA(cudaEventRecord(ev[3], st));
   KK_CUDA(cudaStreamSynchronize(st));
   errh = *eh;
+  out_clipped.assign(items_h.size(), 0);
+  if (clip_h)
+    for (size_t b = 0; b < items_h.size(); b++) out_clipped[b] = (long long)clip_h[b];
   if (errh) throw KKError(KK_ERR_TIMEOUT, errh == 1 ? "an LSTM step barrier timed out"
                                                     : "a tcgen05 convolution pipeline wait timed out");
   float t_all = 0, t_comp = 0;
@@ -1451,7 +1484,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   }
   float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
                              noise_off_d);
-  finish_audio(audio, LN, items_h);
+  finish_audio(audio, LN, items_h, col_item_d, true);
 }
 
 void Engine::decode(int B, const int32_t* n_frames, const float* asr, const float* f0_in, const float* n_in,
@@ -1515,7 +1548,7 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
   linear(m.fc_dec, sdec_d, 128, B, gb_dec, wdec);
   float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
                              noise_off_d);
-  finish_audio(audio, LN, items_h);
+  finish_audio(audio, LN, items_h, col_item_d, false);
   if (audio_out && !keep_audio_dev) {
     long long o = 0;
     for (int b = 0; b < B; b++) {
@@ -1726,8 +1759,22 @@ kk_status kk_fetch_audio(kk_engine* h, int item, float* dst, int64_t cap) {
     kk::Engine& e = *h->e;
     KK_REQUIRE(item >= 0 && item < (int)e.out_off.size(), "item index out of range (no forward result)");
     KK_REQUIRE(!e.keep_audio_dev, "audio was kept on the device (KK_OPT_KEEP_AUDIO_ON_DEVICE)");
+    KK_REQUIRE(!e.pcm16_out, "the last forward produced PCM_16 (KK_OPT_OUTPUT_PCM16): use kk_fetch_audio_pcm16");
     KK_REQUIRE(dst && cap >= e.out_len[item], "destination too small");
     memcpy(dst, e.audio_host + e.out_off[item], sizeof(float) * e.out_len[item]);
+  });
+}
+
+kk_status kk_fetch_audio_pcm16(kk_engine* h, int item, int16_t* dst, int64_t cap, int64_t* clipped) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    kk::Engine& e = *h->e;
+    KK_REQUIRE(item >= 0 && item < (int)e.out_off.size(), "item index out of range (no forward result)");
+    KK_REQUIRE(!e.keep_audio_dev, "audio was kept on the device (KK_OPT_KEEP_AUDIO_ON_DEVICE)");
+    KK_REQUIRE(e.pcm16_out && e.audio_host16, "the last forward produced f32 audio: use kk_fetch_audio");
+    KK_REQUIRE(dst && cap >= e.out_len[item], "destination too small");
+    memcpy(dst, e.audio_host16 + e.out_off[item], sizeof(int16_t) * e.out_len[item]);
+    if (clipped) *clipped = e.out_clipped[item];
   });
 }
 
@@ -1751,6 +1798,7 @@ kk_status kk_set_option(kk_engine* h, int option, int64_t value) {
     if (option == KK_OPT_KEEP_AUDIO_ON_DEVICE) h->e->keep_audio_dev = value != 0;
     else if (option == KK_OPT_SYNC_EACH_STAGE) h->e->sync_each = value != 0;
     else if (option == KK_OPT_PROFILE) h->e->profile = value != 0;
+    else if (option == KK_OPT_OUTPUT_PCM16) h->e->pcm16_out = value != 0;
     else throw kk::KKError(KK_ERR_INVALID_ARG, "unknown option");
   });
 }

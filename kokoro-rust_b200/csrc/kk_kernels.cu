@@ -767,6 +767,31 @@ cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const Ite
   return cudaGetLastError();
 }
 
+// PCM_16 of every sample of the batch (src/wav.rs:76-84: s * 32767 rounded half to even, values
+// outside [-32768, 32767] (and NaN, stored as 0) clamped and counted per item).
+__global__ void pcm16_kernel(const float* audio, long n, const int* col_item_n, int16_t* out,
+                             unsigned long long* clipped) {
+  const long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float v = rintf(audio[i] * 32767.0f);
+  int16_t q;
+  if (!(v >= -32768.0f && v <= 32767.0f)) {
+    q = v != v ? 0 : (v < 0.0f ? -32768 : 32767);
+    const int b = col_item_n[i / 600];
+    if (b >= 0) atomicAdd(clipped + b, 1ull);
+  } else {
+    q = (int16_t)v;
+  }
+  out[i] = q;
+}
+
+cudaError_t launch_pcm16(const float* audio, long n, const int* col_item_n, int16_t* out, unsigned long long* clipped,
+                         cudaStream_t st) {
+  if (n == 0) return cudaSuccess;
+  pcm16_kernel<<<nblk(n, 256), 256, 0, st>>>(audio, n, col_item_n, out, clipped);
+  return cudaGetLastError();
+}
+
 __global__ void copy_cols_kernel(const float* src, int lds, int c0s, float* dst, int ldd, int c0d, int rows, int ncol) {
   long i = blockIdx.x * (long)blockDim.x + threadIdx.x;
   if (i >= (long)rows * ncol) return;

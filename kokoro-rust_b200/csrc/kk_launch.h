@@ -128,6 +128,9 @@ cudaError_t launch_sum3(const float* r0, const float* r1, const float* r2, float
 // stage-1 reflection pad (1, 0) per item plus the noise branch: x[o] = pad(y)[o] + xs[o]
 cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const ItemTab* items, Dom d120,
                                float* x, cudaStream_t st);
+// PCM_16 conversion of n samples (600 per N-domain column) with per-item clip counts (pre-zeroed)
+cudaError_t launch_pcm16(const float* audio, long n, const int* col_item_n, int16_t* out, unsigned long long* clipped,
+                         cudaStream_t st);
 // dst[r, c0d + j] = src[r, c0s + j] for j < ncol
 cudaError_t launch_copy_cols(const float* src, int lds, int c0s, float* dst, int ldd, int c0d, int rows,
                              int ncol, cudaStream_t st);

@@ -26,7 +26,7 @@ LIB_PATH = os.path.join(HERE, "libkokoro_b200.so")
 
 KK_OK, KK_ERR_INVALID_ARG, KK_ERR_OOM, KK_ERR_CUDA, KK_ERR_TIMEOUT, KK_ERR_IO = range(6)
 KK_PRECISION_FP32, KK_PRECISION_BF16 = 0, 1
-KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE, KK_OPT_PROFILE = 1, 2, 3
+KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE, KK_OPT_PROFILE, KK_OPT_OUTPUT_PCM16 = 1, 2, 3, 4
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "TIMEOUT", 5: "IO"}
 
 MAX_PHONEMES = 510  # src/engine.rs:12
@@ -56,6 +56,14 @@ _SIGS = {
     "kk_conv_selftest_error": (ctypes.c_char_p, []),
     "kk_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P]),
     "kk_lstm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]),
+    "kk_fetch_audio_pcm16": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64, _P]),
+    "kk_wav_header": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, _P]),
+    "kk_wav_encode": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_uint32, ctypes.c_int, _P, ctypes.c_int64, _P, _P]),
+    "kk_wav_read_canonical": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.c_uint32, _P]),
+    "kk_wav_assemble": (ctypes.c_int, [ctypes.c_int, _P, _P, ctypes.c_int, ctypes.c_uint32, ctypes.c_char_p,
+                                       ctypes.c_int, ctypes.c_char_p, _P, _P]),
+    "kk_sha256_hex": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_char_p]),
+    "kk_wav_error": (ctypes.c_char_p, []),
 }
 
 
@@ -186,8 +194,9 @@ class BatchItem:
 
 @dataclass
 class Output:
-    audio: np.ndarray
+    audio: np.ndarray           # f32 samples, or int16 PCM_16 samples with pcm16=True
     pred_dur: np.ndarray
+    clipped: int = 0            # PCM_16 samples clipped on the device (pcm16=True)
 
 
 class GpuKokoro:
@@ -261,8 +270,11 @@ class GpuKokoro:
         self.lib.kk_profile_reset(self.h)
 
     def forward_batch(self, items: Sequence[BatchItem], forced_dur: Optional[Sequence[np.ndarray]] = None,
-                      fetch: bool = True) -> List[Output]:
-        """Batched ragged forward; results in input order (src/gpu_batch.rs:179-421)."""
+                      fetch: bool = True, pcm16: bool = False) -> List[Output]:
+        """Batched ragged forward; results in input order (src/gpu_batch.rs:179-421). pcm16=True
+        converts the audio to PCM_16 on the device (the WAV rule of src/wav.rs:76-84) and returns
+        int16 samples with per-item clip counts."""
+        self._check(self.lib.kk_set_option(self.h, KK_OPT_OUTPUT_PCM16, 1 if pcm16 else 0))
         n = len(items)
         ids = np.ascontiguousarray(np.concatenate([np.asarray(it.ids, np.int64) for it in items]) if n else
                                    np.zeros(0, np.int64))
@@ -284,10 +296,16 @@ class GpuKokoro:
         outs = []
         o = 0
         for i in range(n):
-            a = np.empty(int(ns[i]), np.float32)
-            if fetch:
-                self._check(self.lib.kk_fetch_audio(self.h, i, _ptr(a), a.shape[0]))
-            outs.append(Output(a, dur[o:o + lens[i]].copy()))
+            clipped = ctypes.c_int64(0)
+            if pcm16:
+                a = np.empty(int(ns[i]), np.int16)
+                if fetch:
+                    self._check(self.lib.kk_fetch_audio_pcm16(self.h, i, _ptr(a), a.shape[0], ctypes.byref(clipped)))
+            else:
+                a = np.empty(int(ns[i]), np.float32)
+                if fetch:
+                    self._check(self.lib.kk_fetch_audio(self.h, i, _ptr(a), a.shape[0]))
+            outs.append(Output(a, dur[o:o + lens[i]].copy(), int(clipped.value)))
             o += lens[i]
         return outs
 

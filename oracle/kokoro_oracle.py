@@ -308,6 +308,35 @@ def lstm_dir(gx: torch.Tensor, whh: torch.Tensor, bhh: torch.Tensor, reverse: bo
     return out
 
 
+# ----------------------------------------------------------------------------- WAV output
+
+WAV_PCM16, WAV_FLOAT32 = 0, 1
+WAV_MAX_DATA_BYTES = 0xFFFFFFFF - 36  # src/wav.rs:23-24
+
+
+def wav_header(fmt: int, sample_rate: int, data_bytes: int) -> bytes:
+    """Canonical 44-byte RIFF/WAVE header (src/wav.rs:44-61); ValueError above the RIFF limit."""
+    if data_bytes > WAV_MAX_DATA_BYTES:
+        raise ValueError("the audio exceeds the 4 GiB limit of a WAV file")
+    bits, tag = (32, 3) if fmt == WAV_FLOAT32 else (16, 1)
+    le = lambda v, n: int(v).to_bytes(n, "little")  # noqa: E731
+    return (b"RIFF" + le(36 + data_bytes, 4) + b"WAVEfmt " + le(16, 4) + le(tag, 2) + le(1, 2) + le(sample_rate, 4) +
+            le(sample_rate * bits // 8, 4) + le(bits // 8, 2) + le(bits, 2) + b"data" + le(data_bytes, 4))
+
+
+def wav_encode(audio: np.ndarray, sample_rate: int, fmt: int):
+    """(bytes, clipped) as src/wav.rs:63-87: PCM_16 = f32 (s * 32767) rounded half to even; values
+    outside [-32768, 32767] are counted and clamped; NaN counts and becomes 0 (Rust's saturating
+    cast)."""
+    a = np.asarray(audio, np.float32)
+    if fmt == WAV_FLOAT32:
+        return wav_header(fmt, sample_rate, a.size * 4) + a.astype("<f4").tobytes(), 0
+    v = np.rint(a * np.float32(32767.0))  # numpy rint: round half to even
+    bad = ~((v >= -32768.0) & (v <= 32767.0))
+    q = np.where(np.isnan(v), 0.0, np.clip(v, -32768.0, 32767.0)).astype(np.int16)
+    return wav_header(fmt, sample_rate, a.size * 2) + q.astype("<i2").tobytes(), int(bad.sum())
+
+
 # ----------------------------------------------------------------------------- model
 
 class KokoroOracle:
