@@ -54,7 +54,6 @@ __device__ __forceinline__ void st_cluster_v4(uint32_t local_addr, uint32_t rank
                : "memory");
 }
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + expf(-x)); }
-
 __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_cluster_kernel(const LstmArgs a) {
   extern __shared__ __align__(16) float sm[];
   float* Hs = sm;                                    // [2][LC_IPG][LC_HROW] staged hidden states
@@ -203,21 +202,27 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
 // BF16 precision mode. Same clusters, groups and cell arithmetic; the recurrent product of a step,
 // G[128 gate rows][32 items] = W_hh[rows of this CTA's 32 units][256] x H[256][32 items], runs on
 // the tensor cores with both operands split into bf16 pairs (x = hi + lo, hi = bf16(x),
-// lo = bf16(x - hi)): G = Wh Hh + Wh Hl + Wl Hh accumulated in fp32 in TMEM (48 MMAs of
-// M 128 x N 32 x K 16; the dropped Wl Hl term is below 2^-16 relative). A rows are ordered
-// unit * 4 + gate, so the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane
-// transpose through shared memory hands each thread one unit's four gates for 4 items. The new h
-// is split into bf16 hi / lo and pushed straight into every CTA's B operand of the next step.
+// lo = bf16(x - hi)): G = Wh Hh + Wh Hl + Wl Hh accumulated in fp32 in TMEM (the dropped Wl Hl term
+// is below 2^-16 relative). The H image of a step holds Hh in its rows 0..31 and Hl in rows 32..63,
+// so each K step is two MMAs: Wh x [Hh | Hl] (N 64, columns 0..63) and Wl x Hh (N 32, accumulated
+// into columns 0..31); G = columns 0..31 + columns 32..63. A rows are ordered unit * 4 + gate, so
+// the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane transpose through shared
+// memory hands each thread one unit's four gates for 4 items. The new h is split into bf16 hi / lo
+// and pushed straight into every CTA's next H image with st.async, which completes bytes of the
+// receiver's own mbarrier: each CTA waits (bounded) for exactly the bytes of the next step's
+// active items, so steps need no cluster barrier.
 
-constexpr int LT_ROWS = 128;                   // gate rows per CTA (32 units x 4 gates)
-constexpr int LT_KC = LC_H / 8;                // 8-element K chunks of the recurrent product
+constexpr int LT_ROWS = 128;                     // gate rows per CTA (32 units x 4 gates)
+constexpr int LT_KC = LC_H / 8;                  // 8-element K chunks of the recurrent product
 constexpr int LT_ABYTES = LT_KC * LT_ROWS * 16;  // one bf16 W image (64 KB)
-constexpr int LT_BBYTES = LT_KC * LC_IPG * 16;   // one bf16 H image (16 KB)
-constexpr int LT_GXLD = 17;                    // transpose staging row (floats)
-constexpr uint32_t LT_IDESC = idesc_bf16(LT_ROWS, LC_IPG);
+constexpr int LT_HROWS = 2 * LC_IPG;             // H image rows: 32 items hi, then 32 items lo
+constexpr int LT_BBYTES = LT_KC * LT_HROWS * 16; // one H image (32 KB)
+constexpr int LT_GXLD = 17;                      // transpose staging row (floats)
+constexpr uint32_t LT_IDESC_HL = idesc_bf16(LT_ROWS, LT_HROWS);  // Wh x [Hh | Hl]
+constexpr uint32_t LT_IDESC_H = idesc_bf16(LT_ROWS, LC_IPG);     // Wl x Hh
 
 __host__ __device__ constexpr size_t lt_smem() {
-  return 2 * (size_t)LT_ABYTES + 4 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
+  return 2 * (size_t)LT_ABYTES + 2 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
 }
 
 __device__ __forceinline__ uint32_t bf16_bits(float x) {
@@ -226,15 +231,17 @@ __device__ __forceinline__ uint32_t bf16_bits(float x) {
   memcpy(&u, &h, 2);
   return u;
 }
+__device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
 
 __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_kernel(const LstmArgs a) {
   extern __shared__ __align__(1024) uint8_t sm8[];
   uint8_t* Ahi = sm8;
   uint8_t* Alo = Ahi + LT_ABYTES;
-  uint8_t* Bb = Alo + LT_ABYTES;                                  // [2 stages][hi, lo] H images
-  float* Tile = reinterpret_cast<float*>(Bb + 4 * LT_BBYTES);     // [32 items][LC_TLD] new h (f32)
+  uint8_t* Bb = Alo + LT_ABYTES;                                  // [2 stages] H images
+  float* Tile = reinterpret_cast<float*>(Bb + 2 * LT_BBYTES);     // [32 items][LC_TLD] new h (f32)
   float* Gx = Tile + LC_IPG * LC_TLD;                             // [8 warps][32 lanes][LT_GXLD]
   __shared__ uint64_t bar;
+  __shared__ uint64_t hbar[2];  // H image j complete: the 8 CTAs' slices of the next step have landed
   __shared__ uint32_t tslot;
   __shared__ int bad;
   const int rank = (int)cl_rank();
@@ -256,7 +263,7 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       *reinterpret_cast<unsigned short*>(Ahi + off) = (unsigned short)hi;
       *reinterpret_cast<unsigned short*>(Alo + off) = (unsigned short)lo;
     }
-    for (int i = tid; i < 2 * LT_BBYTES / 16; i += 256) reinterpret_cast<uint4*>(Bb)[i] = make_uint4(0, 0, 0, 0);
+    for (int i = tid; i < LT_BBYTES / 16; i += 256) reinterpret_cast<uint4*>(Bb)[i] = make_uint4(0, 0, 0, 0);
   }
   // this thread's cells: unit ul (lane quarter q = warp % 4 holds units 8q .. 8q + 7), items i0 .. i0 + 3
   const int q = warp & 3, hf = warp >> 2;
@@ -275,14 +282,35 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   // push role: item pi, part (0 hi, 1 lo), 8-unit chunk kc4 of this CTA's 32 units
   const int pi = tid >> 3, part = (tid >> 2) & 1, kc4 = tid & 3;
   const int pst = gs[pi], pln = gl[pi];
+  const int* act = a.gact + (long)g * a.Tmax;
+  // bytes of the 8 CTAs' pushes made during step s (into H image (s + 1) & 1)
+  auto push_bytes = [&](int s) -> uint32_t {
+    const int n = s + 1 < a.Tmax ? act[s + 1] : 0;
+    return (uint32_t)(LC_CL * n * 2 * 4 * 16);
+  };
+  // cluster addresses of this thread's push slot in each CTA's H images and of their barriers
+  uint32_t rslot[LC_CL], rbar0[LC_CL];
+  {
+    const uint32_t slot = smem_u32(Bb + (4 * rank + kc4) * (LT_HROWS * 16) + (part * LC_IPG + pi) * 16);
+    const uint32_t b0 = smem_u32(&hbar[0]);
+#pragma unroll
+    for (int r = 0; r < LC_CL; r++) {
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rslot[r]) : "r"(slot), "r"(r));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar0[r]) : "r"(b0), "r"(r));
+    }
+  }
 
   if (tid == 0) {
     mbar_init(&bar, 1);
+    mbar_init(&hbar[0], 1);
+    mbar_init(&hbar[1], 1);
     bad = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    // armed before any CTA can push step 0's results (the cluster barrier below)
+    if (push_bytes(0)) mbar_arrive_expect_tx(&hbar[1], push_bytes(0));
   }
   if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 32;" ::"r"(smem_u32(&tslot))
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], 64;" ::"r"(smem_u32(&tslot))
                  : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
@@ -291,14 +319,18 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tslot;
-  const int* act = a.gact + (long)g * a.Tmax;
   volatile int abort_flag = 0;
+  uint32_t hph[2] = {0, 0};  // phase parity of each H-image barrier
   cluster_sync();  // every CTA of the cluster is running and initialised before remote stores
 
   for (int s = 0; s < a.Tmax; s++) {
     const int na = act[s];
     if (na == 0) break;  // same for the whole group, so for every CTA of the cluster
     const int cur = s & 1;
+    if (s > 0) {  // this step's H image: all 8 CTAs' slices of step s - 1 have landed
+      if (!bad && !mbar_wait(&hbar[cur], hph[cur], &abort_flag, a.err)) bad = 1;
+      hph[cur] ^= 1;
+    }
     // gate inputs of this thread's cells, loaded ahead of the product
     float gxv[4][4];
 #pragma unroll
@@ -313,18 +345,18 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       }
     }
     if (tid == 0 && !bad) {
-      fence_proxy_async();  // H images arrived through generic-proxy stores
+      fence_proxy_async();  // the H image arrived through generic-proxy stores
       tc_fence_after();
-      const uint32_t bh0 = smem_u32(Bb + (cur * 2 + 0) * LT_BBYTES), bl0 = smem_u32(Bb + (cur * 2 + 1) * LT_BBYTES);
+      // descriptors advance by constant steps of the 14-bit start-address field (16-byte units)
+      uint64_t ah = sdesc(smem_u32(Ahi), LT_ROWS * 16, 128);
+      uint64_t al = sdesc(smem_u32(Alo), LT_ROWS * 16, 128);
+      uint64_t bd = sdesc(smem_u32(Bb + cur * LT_BBYTES), LT_HROWS * 16, 128);
+      constexpr uint64_t dA = (2 * LT_ROWS * 16) >> 4, dB = (2 * LT_HROWS * 16) >> 4;
 #pragma unroll
       for (int kk = 0; kk < LT_KC / 2; kk++) {
-        const uint64_t ah = sdesc(smem_u32(Ahi) + kk * 2 * (LT_ROWS * 16), LT_ROWS * 16, 128);
-        const uint64_t al = sdesc(smem_u32(Alo) + kk * 2 * (LT_ROWS * 16), LT_ROWS * 16, 128);
-        const uint64_t bhd = sdesc(bh0 + kk * 2 * (LC_IPG * 16), LC_IPG * 16, 128);
-        const uint64_t bld = sdesc(bl0 + kk * 2 * (LC_IPG * 16), LC_IPG * 16, 128);
-        mma_bf16(tmem, ah, bhd, LT_IDESC, kk > 0);
-        mma_bf16(tmem, ah, bld, LT_IDESC, 1);
-        mma_bf16(tmem, al, bhd, LT_IDESC, 1);
+        mma_bf16(tmem, ah, bd, LT_IDESC_HL, kk > 0);
+        mma_bf16(tmem, al, bd, LT_IDESC_H, 1);
+        ah += dA, al += dA, bd += dB;
       }
       mma_commit(&bar);
     }
@@ -332,13 +364,14 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
     tc_fence_after();
     __syncthreads();  // bad is uniform from here on
     if (!bad) {
-      // lane (unit 8q + lane / 4, gate lane % 4) reads its 16 items of this half, then a 4-lane
-      // transpose gives each lane one unit's 4 gates for items i0 .. i0 + 3
-      float v[16];
+      // lane (unit 8q + lane / 4, gate lane % 4) reads its 16 items of this half (hi columns and
+      // lo columns), then a 4-lane transpose gives each lane one unit's 4 gates for items i0 .. i0 + 3
+      float v[16], w[16];
       tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + hf * 16, v);
+      tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + LC_IPG + hf * 16, w);
       float* gw = Gx + warp * 32 * LT_GXLD;
 #pragma unroll
-      for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = v[j];
+      for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = v[j] + w[j];
       __syncwarp();
 #pragma unroll
       for (int m = 0; m < 4; m++) {
@@ -346,17 +379,21 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
           float d[4];
 #pragma unroll
           for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
-          const float ig = sigm(gxv[m][0] + (d[0] + bh[0]));
-          const float fg = sigm(gxv[m][1] + (d[1] + bh[1]));
+          const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
+          const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
           const float cg = tanhf(gxv[m][2] + (d[2] + bh[2]));
-          const float og = sigm(gxv[m][3] + (d[3] + bh[3]));
+          const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
           c[m] = fg * c[m] + ig * cg;
           Tile[(i0 + m) * LC_TLD + ul] = og * tanhf(c[m]);
         }
       }
     }
+    // re-arm image `cur` (consumed this step) for the pushes of step s + 1, before the barrier that
+    // releases this CTA's own step-s pushes: no CTA can push step s + 1 before it has received them
+    if (tid == 0 && !bad && push_bytes(s + 1)) mbar_arrive_expect_tx(&hbar[cur], push_bytes(s + 1));
     tc_fence_before();
     __syncthreads();  // Tile complete; TMEM and staging reads done
+    const int na_next = s + 1 < a.Tmax ? act[s + 1] : 0;
     if (!bad && pi < na) {
       const float* hp = Tile + pi * LC_TLD + 8 * kc4;
       uint32_t w4[4];
@@ -371,12 +408,15 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
         }
         w4[e >> 1] = b0 | (b1 << 16);
       }
-      const float4 pk = make_float4(__uint_as_float(w4[0]), __uint_as_float(w4[1]), __uint_as_float(w4[2]),
-                                    __uint_as_float(w4[3]));
-      const int kc = 4 * rank + kc4;  // 8-unit chunk of the 256 hidden units
-      const uint32_t la = smem_u32(Bb + ((cur ^ 1) * 2 + part) * LT_BBYTES + kc * (LC_IPG * 16) + pi * 16);
+      if (pi < na_next) {  // only items still running at step s + 1 are needed there
+        const uint32_t off = (uint32_t)((cur ^ 1) * LT_BBYTES), boff = (uint32_t)((cur ^ 1) * 8);
 #pragma unroll
-      for (int r = 0; r < LC_CL; r++) st_cluster_v4(la, (uint32_t)r, pk);
+        for (int r = 0; r < LC_CL; r++)
+          asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::
+                           "r"(rslot[r] + off),
+                       "r"(w4[0]), "r"(w4[1]), "r"(w4[2]), "r"(w4[3]), "r"(rbar0[r] + boff)
+                       : "memory");
+      }
       if (part == 0) {
         const int t = dir == 0 ? s : pln - 1 - s;
         float* o = a.out + (long)(pst + t) * a.ldo + dir * LC_H + rank * 32 + 8 * kc4;
@@ -384,15 +424,16 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
         *reinterpret_cast<float4*>(o + 4) = make_float4(hp[4], hp[5], hp[6], hp[7]);
       }
     }
-    fence_proxy_async();
-    cluster_sync();  // step s + 1 multiplies the H images every CTA just received
   }
+  // every push was awaited by its receiver inside the loop; the barrier keeps each CTA (and its
+  // shared memory) alive until the whole cluster has left the loop
+  cluster_sync();
   if (bad && tid == 0) atomicExch(a.err, 4);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 32;" ::"r"(tmem) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, 64;" ::"r"(tmem) : "memory");
   }
 }
 
