@@ -278,6 +278,9 @@ def main():
         dist.all_reduce(tm[1:2], op=dist.ReduceOp.SUM)
         t = tm
     max_ms, total_audio = float(t[0]), float(t[1])
+    ms_ = eng.memory_stats()
+    mem = dict(ms_, bytes_per_frame=ms_["peak_bytes"] / max(ms_["frames"], 1),
+               frames_per_token=ms_["frames"] / max(ms_["tokens"], 1))
     value = total_audio / (max_ms / 1000.0)
 
     # ---- end to end through the public API with host buffers (e2e)
@@ -364,6 +367,7 @@ def main():
             "kernel_profile": {k: {"launches": v[0], "ms": v[1], "tflops": v[2] / max(v[1], 1e-9) / 1e9}
                                for k, v in prof.items()},
             "clocks": clk.summary(),
+            "device_memory": mem,
         }
         print(json.dumps(res))
     eng.close()

@@ -278,6 +278,18 @@ KK_API const char* kk_conv_selftest_error(void);
 /* Bytes of device memory the engine currently holds (weights + arena). */
 KK_API int64_t kk_device_bytes(const kk_engine* e);
 
+/*
+ * Device memory of the engine and of its last call, for the free-VRAM batch budget the reference
+ * describes for its scheduler (docs/design/BATCHING.md:44-47; its code uses a fixed phoneme budget,
+ * src/engine.rs:148-161): out[0] = weight bytes, out[1] = arena bytes held (reused by the next
+ * call), out[2] = peak arena bytes in use during the last call, out[3] = phoneme tokens of the
+ * last kk_forward_batch (0 after a decode), out[4] = frames of the last call.
+ */
+KK_API kk_status kk_memory_stats(const kk_engine* e, int64_t out[5]);
+
+/* Free and total device memory of a CUDA device (cudaMemGetInfo). */
+KK_API kk_status kk_device_memory(int cuda_ordinal, int64_t* free_bytes, int64_t* total_bytes);
+
 /* Number of kernel launches issued by the engine since creation (counted on the host). */
 KK_API int64_t kk_launch_count(const kk_engine* e);
 

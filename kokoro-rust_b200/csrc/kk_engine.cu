@@ -64,6 +64,7 @@ class Arena {
         throw KKError(KK_ERR_INVALID_ARG, "static scratch exhausted (batch above the no-allocation limit)");
       void* p = ext_base_ + ext_used_;
       ext_used_ += bytes;
+      if (ext_used_ > peak_) peak_ = ext_used_;
       return p;
     }
     while (cur_ < blocks_.size()) {
@@ -71,6 +72,7 @@ class Arena {
       if (b.used + bytes <= b.cap) {
         void* p = b.p + b.used;
         b.used += bytes;
+        note_peak();
         return p;
       }
       cur_++;
@@ -90,6 +92,7 @@ class Arena {
     }
     blocks_.push_back({p, cap, bytes});
     cur_ = blocks_.size() - 1;
+    note_peak();
     return p;
   }
   template <class T>
@@ -115,14 +118,23 @@ class Arena {
   void reset() {
     for (auto& b : blocks_) b.used = 0;
     cur_ = 0;
+    peak_ = 0;
   }
   size_t bytes() const {
     size_t s = 0;
     for (auto& b : blocks_) s += b.cap;
     return s;
   }
+  // Largest number of bytes in use at once since the last reset (the device memory a call needs
+  // beyond the weights; the free-VRAM batch budget is derived from it).
+  size_t peak() const { return peak_; }
 
  private:
+  void note_peak() {
+    size_t u = 0;
+    for (size_t i = 0; i <= cur_ && i < blocks_.size(); i++) u += blocks_[i].used;
+    if (u > peak_) peak_ = u;
+  }
   struct Block {
     char* p;
     size_t cap, used;
@@ -131,6 +143,7 @@ class Arena {
   size_t cur_ = 0;
   char* ext_base_ = nullptr;
   size_t ext_cap_ = 0, ext_used_ = 0;
+  size_t peak_ = 0;
 };
 
 // Pinned host staging for the uploads and downloads of one call (reset per call).
@@ -274,6 +287,7 @@ struct Engine {
   const char* tc_trace_dir = getenv("KK_TC_TRACE_DIR");  // diagnostics: per-launch pipeline cycle accounting
   const bool prof_shapes = getenv("KK_PROFILE_SHAPES") != nullptr;  // diagnostics: conv shape in the class name
   int cur_B = 0;  // items of the batch being run
+  long long last_tokens = 0, last_frames = 0;  // sizes of the last call (memory statistics)
   // timing: events on the engine stream (begin, compute begin, compute end, end)
   cudaEvent_t ev[4] = {nullptr, nullptr, nullptr, nullptr};
   double last_times[4] = {0, 0, 0, 0};
@@ -1243,9 +1257,11 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   // ---- token layout (src/gpu_batch.rs:189-213)
   std::vector<ItemTab> items_h(B);
   int LT = 0;
+  last_tokens = 0;
   for (int b = 0; b < B; b++) {
     items_h[b] = {LT, ids_len[b], 0, 0};
     LT += ids_len[b] + GAP_T;
+    last_tokens += ids_len[b];
   }
   std::vector<int> row_item_h(LT, -1), ids_h(LT, 0);
   {
@@ -1397,6 +1413,8 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     items_h[b].n = (int)n;
     LN += (int)n + GAP_N;
   }
+  last_frames = 0;
+  for (int b = 0; b < B; b++) last_frames += items_h[b].n;
   if (nsamp_out)
     for (int b = 0; b < B; b++) nsamp_out[b] = 600LL * items_h[b].n;
   std::vector<int> col_item_h(LN, -1), src_row_h(LN, -1);
@@ -1500,6 +1518,8 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
     LN += n_frames[b] + GAP_N;
     tot += n_frames[b];
   }
+  last_tokens = 0;
+  last_frames = tot;
   KK_CUDA(cudaSetDevice(dev));
   ar.reset();
   pin.reset();
@@ -1598,6 +1618,8 @@ void Engine::decode_noalloc(int B, const int32_t* n_frames, const float* asr, co
     tot += n_frames[b];
     max_n = std::max(max_n, n_frames[b]);
   }
+  last_tokens = 0;
+  last_frames = tot;
   KK_CUDA(cudaSetDevice(dev));
   struct Guard {  // leave the engine's normal (allocating) mode however the call ends
     Engine* e;
@@ -1852,6 +1874,35 @@ void kk_profile_reset(kk_engine* h) {
 }
 
 int64_t kk_device_bytes(const kk_engine* h) { return h ? (int64_t)(h->e->wbytes + h->e->ar.bytes()) : 0; }
+
+kk_status kk_memory_stats(const kk_engine* h, int64_t out[5]) {
+  if (!h || !out) return KK_ERR_INVALID_ARG;
+  out[0] = (int64_t)h->e->wbytes;
+  out[1] = (int64_t)h->e->ar.bytes();
+  out[2] = (int64_t)h->e->ar.peak();
+  out[3] = h->e->last_tokens;
+  out[4] = h->e->last_frames;
+  return KK_OK;
+}
+
+kk_status kk_device_memory(int cuda_ordinal, int64_t* free_bytes, int64_t* total_bytes) {
+  if (!free_bytes || !total_bytes) return KK_ERR_INVALID_ARG;
+  int prev = 0;
+  if (cudaGetDevice(&prev) != cudaSuccess || cudaSetDevice(cuda_ordinal) != cudaSuccess) {
+    cudaGetLastError();
+    return KK_ERR_CUDA;
+  }
+  size_t f = 0, t = 0;
+  const cudaError_t e = cudaMemGetInfo(&f, &t);
+  cudaSetDevice(prev);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    return KK_ERR_CUDA;
+  }
+  *free_bytes = (int64_t)f;
+  *total_bytes = (int64_t)t;
+  return KK_OK;
+}
 
 int64_t kk_launch_count(const kk_engine* h) { return h ? h->e->launches : 0; }
 

@@ -64,6 +64,8 @@ _SIGS = {
                                        ctypes.c_int, ctypes.c_char_p, _P, _P]),
     "kk_sha256_hex": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_char_p]),
     "kk_wav_error": (ctypes.c_char_p, []),
+    "kk_memory_stats": (ctypes.c_int, [_P, _P]),
+    "kk_device_memory": (ctypes.c_int, [ctypes.c_int, _P, _P]),
 }
 
 
@@ -211,6 +213,7 @@ class GpuKokoro:
             raise KokoroError(st, self.lib.kk_last_error(None).decode())
         self.h = h
         self.precision = precision
+        self.ordinal = cuda_ordinal
 
     def close(self):
         if getattr(self, "h", None):
@@ -236,6 +239,17 @@ class GpuKokoro:
 
     def device_bytes(self) -> int:
         return int(self.lib.kk_device_bytes(self.h))
+
+    def memory_stats(self) -> dict:
+        """Device memory of the engine and of its last call (kk_memory_stats)."""
+        out = (ctypes.c_int64 * 5)()
+        self._check(self.lib.kk_memory_stats(self.h, out))
+        return {"weight_bytes": out[0], "arena_bytes": out[1], "peak_bytes": out[2], "tokens": out[3],
+                "frames": out[4]}
+
+    def device_memory(self) -> tuple:
+        """(free, total) bytes of this engine's device."""
+        return device_memory(self.ordinal)
 
     def last_times(self) -> dict:
         """Device-side timings of the last call (CUDA events on the engine stream)."""
@@ -371,12 +385,58 @@ def mix_seed(seed: int, index: int) -> int:
     return z ^ (z >> 31)
 
 
+def device_memory(cuda_ordinal: int) -> tuple:
+    """(free, total) bytes of a CUDA device (kk_device_memory)."""
+    lib = load_library()
+    f, t = ctypes.c_int64(), ctypes.c_int64()
+    st = lib.kk_device_memory(cuda_ordinal, ctypes.byref(f), ctypes.byref(t))
+    if st != KK_OK:
+        raise KokoroError(st, "cudaMemGetInfo failed")
+    return int(f.value), int(t.value)
+
+
+# Working set of one forward per output frame (peak arena bytes / frames) and predicted frames per
+# phoneme token at speed 1, measured on a B200 over config 4's 251-line batch (BF16 mode); used
+# until the engine has run a forward of its own.
+# (measured: 30.8 GB peak for 69,319 frames = 444 KB per frame; 2.03 frames per token)
+DEFAULT_BYTES_PER_FRAME = 450_000
+DEFAULT_FRAMES_PER_PHONEME = 2.5
+
+
 @dataclass
 class BatchPolicy:
     """Batching budget (src/engine.rs:148-161): total phoneme characters and items per batch."""
 
     max_phonemes: int = 4000
     max_items: int = 64
+
+    @classmethod
+    def from_free_vram(cls, gpu: "GpuKokoro", speed: float = 1.0, max_items: int = 1024, headroom: float = 0.85,
+                       bytes_per_frame: Optional[float] = None,
+                       frames_per_phoneme: Optional[float] = None) -> "BatchPolicy":
+        """A phoneme budget derived from the device's free memory, the scheduler rule of
+        docs/design/BATCHING.md:44-47 (the reference's code keeps a fixed budget).
+
+        Memory available to a batch = (free device memory + the engine's arena, which the next call
+        reuses) x ``headroom``. Frames that fit = that / bytes per frame (the engine's own last
+        forward when it has run one, else ``DEFAULT_BYTES_PER_FRAME``); phonemes = frames /
+        (frames per phoneme / speed), frames per phoneme again from the last forward (never below
+        the default, so a short calibration batch cannot inflate the budget). A batch that still
+        does not fit fails with KK_ERR_OOM and ``synth_batch`` splits it in half."""
+        st = gpu.memory_stats()
+        free, _total = gpu.device_memory()
+        avail = (free + st["arena_bytes"]) * headroom
+        bpf = bytes_per_frame
+        if bpf is None:
+            bpf = st["peak_bytes"] / st["frames"] if st["frames"] > 0 and st["tokens"] > 0 else DEFAULT_BYTES_PER_FRAME
+            bpf = max(bpf, DEFAULT_BYTES_PER_FRAME * 0.5)
+        fpp = frames_per_phoneme
+        if fpp is None:
+            fpp = DEFAULT_FRAMES_PER_PHONEME
+            if st["tokens"] > 0:
+                fpp = max(fpp, st["frames"] / st["tokens"] * speed)
+        frames = avail / bpf
+        return cls(max_phonemes=max(MAX_PHONEMES + 2, int(frames / (fpp / speed))), max_items=max_items)
 
 
 def plan_batches(lens: Sequence[int], p: BatchPolicy) -> List[List[int]]:

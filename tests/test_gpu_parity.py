@@ -103,3 +103,23 @@ def test_predicted_durations_bit_exact(kk, eng32, oracle):
         margin = np.abs(r["dur_q"] - np.floor(r["dur_q"]) - 0.5)
         tie = margin < 1e-4
         assert np.array_equal(o.pred_dur[~tie], r["dur"][~tie]), (o.pred_dur, r["dur"])
+
+
+def test_memory_stats_and_free_vram_budget(kk, eng32):
+    """kk_memory_stats after a forward: the call's token and frame totals, a peak working set
+    within the arena, and a free-VRAM policy built from them."""
+    rng = np.random.default_rng(5)
+    items, durs = [], []
+    for n in (7, 20):
+        ids, ref_s = synth_item(rng, n)
+        items.append(kk.BatchItem(ids, ref_s, 1.0, kk.ItemNoise(seed=n)))
+        durs.append(np.concatenate([[0], np.full(n, 2), [0]]))
+    eng32.forward_batch(items, forced_dur=durs)
+    st = eng32.memory_stats()
+    assert st["tokens"] == sum(len(it.ids) for it in items)
+    assert st["frames"] == sum(int(d.sum()) for d in durs)
+    assert 0 < st["peak_bytes"] <= st["arena_bytes"]
+    free, total = eng32.device_memory()
+    assert 0 < free <= total
+    p = kk.BatchPolicy.from_free_vram(eng32)
+    assert p.max_phonemes >= kk.engine.MAX_PHONEMES + 2

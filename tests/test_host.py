@@ -94,3 +94,43 @@ def test_voice_rules(kk):
         v.ref_s(511)
     e.add_voice("w", np.zeros((510, 256), np.float32))
     assert np.allclose(e.voice("v,w").pack, v.pack / 2)
+
+
+class FakeMem:
+    """memory_stats / device_memory of a GpuKokoro, for the free-VRAM budget arithmetic."""
+
+    def __init__(self, free, arena=0, peak=0, tokens=0, frames=0):
+        self.free, self.st = free, {"weight_bytes": 330 << 20, "arena_bytes": arena, "peak_bytes": peak,
+                                    "tokens": tokens, "frames": frames}
+
+    def memory_stats(self):
+        return dict(self.st)
+
+    def device_memory(self):
+        return self.free, 180 << 30
+
+
+def test_free_vram_budget(kk):
+    E = kk.engine
+    # before any forward: the built-in per-frame and per-phoneme figures
+    p = kk.BatchPolicy.from_free_vram(FakeMem(free=100 << 30), headroom=0.5)
+    frames = (100 << 30) * 0.5 / E.DEFAULT_BYTES_PER_FRAME
+    assert p.max_phonemes == int(frames / E.DEFAULT_FRAMES_PER_PHONEME)
+    # the arena the engine already holds is reusable; a faster speed means fewer frames per phoneme
+    p2 = kk.BatchPolicy.from_free_vram(FakeMem(free=60 << 30, arena=40 << 30), headroom=0.5, speed=2.0)
+    assert p2.max_phonemes == int(frames / (E.DEFAULT_FRAMES_PER_PHONEME / 2.0))
+    # after a forward: that call's bytes per frame and frames per phoneme (never below the default)
+    m = FakeMem(free=50 << 30, arena=10 << 30, peak=16 << 30, tokens=10_000, frames=40_000)
+    p3 = kk.BatchPolicy.from_free_vram(m, headroom=1.0)
+    assert p3.max_phonemes == int((60 << 30) / ((16 << 30) / 40_000) / 4.0)
+    m = FakeMem(free=50 << 30, arena=10 << 30, peak=16 << 30, tokens=40_000, frames=40_000)
+    assert kk.BatchPolicy.from_free_vram(m, headroom=1.0).max_phonemes == int(
+        (60 << 30) / ((16 << 30) / 40_000) / E.DEFAULT_FRAMES_PER_PHONEME)
+    # a calibration call with an implausibly small working set cannot inflate the budget
+    m = FakeMem(free=50 << 30, arena=10 << 30, peak=1 << 20, tokens=40_000, frames=40_000)
+    assert kk.BatchPolicy.from_free_vram(m, headroom=1.0).max_phonemes == int(
+        (60 << 30) / (E.DEFAULT_BYTES_PER_FRAME * 0.5) / E.DEFAULT_FRAMES_PER_PHONEME)
+    # a nearly full device still admits one maximal item (the OOM split handles the rest)
+    assert kk.BatchPolicy.from_free_vram(FakeMem(free=1 << 20)).max_phonemes == kk.engine.MAX_PHONEMES + 2
+    plan = kk.plan_batches([100] * 50, kk.BatchPolicy(max_phonemes=p.max_phonemes, max_items=p.max_items))
+    assert sum(len(b) for b in plan) == 50
