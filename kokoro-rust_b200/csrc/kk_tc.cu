@@ -60,8 +60,12 @@ constexpr int TC_NEPI = 8;                       // epilogue warps
 constexpr int TC_NPROD = 8;                      // producer warps
 constexpr int TC_PROWS = TC_NPROD * 32 / 8;      // box rows converted at once (8 lanes per row)
 constexpr int TC_EROWS = TC_N / 2;               // time rows per epilogue warp
-// per epilogue warp: 2 staging chunks, TC_RES_DEPTH residual chunks, the item of each output row
-constexpr int TC_EPI_WARP_BYTES = 2 * TC_EBOX + TC_RES_DEPTH * TC_EBOX + TC_EROWS * 4;
+// per epilogue warp: 2 staging chunks, TC_RES_DEPTH residual chunks (only for residual / shortcut
+// epilogues), the item of each output row
+__host__ __device__ constexpr int tc_epi_warp_bytes(bool need_res) {
+  return (2 + (need_res ? TC_RES_DEPTH : 0)) * TC_EBOX + TC_EROWS * 4;
+}
+constexpr int TC_TAB = 256;                      // channels of the shared-memory coefficient tables
 constexpr int TC_THREADS = (4 + TC_NEPI + TC_NPROD) * 32;
 constexpr int TC_WBLOCK = TC_M * TC_KB * 2;      // 16 KB weight block
 constexpr int TC_SMEM_MAX = 227 * 1024;
@@ -83,6 +87,8 @@ struct TcArgs {
   int win_pad;    // window rows rounded to 8, + 1 (bank-conflict-free producer stores)
   int rst;        // input-box ring stages (0 on the pre-transform route)
   int xst;        // activation-window stages
+  int epb;        // shared-memory bytes per epilogue warp
+  int tab;        // AdaIN coefficients and Snake alphas come from shared-memory tables (cin <= TC_TAB)
   int* err;
   unsigned long long* trace;  // optional cycle accounting of CTA 0 (diagnostics), 16 counters
 };
@@ -126,8 +132,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   const int XST = p.xst;
   uint8_t* xbuf = wbuf + TC_WST * TC_WBLOCK;                  // XST x xbytes
   uint8_t* inring = xbuf + XST * xbytes;                      // RST x 8 KB
-  uint8_t* epi = inring + RST * TC_INBOX;                     // TC_NEPI x TC_EPI_WARP_BYTES
-  uint64_t* bars = (uint64_t*)(epi + TC_NEPI * TC_EPI_WARP_BYTES);
+  uint8_t* epi = inring + RST * TC_INBOX;                     // TC_NEPI x p.epb
+  uint64_t* bars = (uint64_t*)(epi + TC_NEPI * p.epb);
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + TC_WST;
   uint64_t* in_full = w_empty + TC_WST;
@@ -137,9 +143,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   uint64_t* acc_full = x_empty + TC_XST_MAX;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* res_full = acc_empty + 2;                         // [TC_NEPI][TC_RES_DEPTH]
-  uint32_t* tmem_slot = (uint32_t*)(res_full + TC_NEPI * TC_RES_DEPTH);
+  uint64_t* meta_full = res_full + TC_NEPI * TC_RES_DEPTH;    // [2] a tile's row items / coefficients written
+  uint64_t* meta_empty = meta_full + 2;                       // [2] the producers are done with them
+  uint32_t* tmem_slot = (uint32_t*)(meta_empty + 2);
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
-  int* ritem = (int*)(tmem_slot + 4);                         // item of each window row (producers)
+  int* mitem = (int*)(tmem_slot + 2);                         // [2] item whose coefficients ctab holds
+  int* ritem = (int*)(tmem_slot + 4);                         // [2][TC_MAX_WIN] item of each window row
+  float2* ctab = (float2*)(ritem + 2 * TC_MAX_WIN);           // [2][TC_TAB] AdaIN (scale, shift) of mitem
+  float2* atab = ctab + 2 * TC_TAB;                           // [TC_TAB] Snake (alpha, 1 / alpha)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.n_cot * p.n_tt;
@@ -163,6 +174,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       mbar_init(&acc_empty[i], TC_NEPI);
     }
     for (int i = 0; i < TC_NEPI * TC_RES_DEPTH; i++) mbar_init(&res_full[i], 1);
+    for (int i = 0; i < 2; i++) {
+      mbar_init(&meta_full[i], 1);
+      mbar_init(&meta_empty[i], TC_NPROD);
+    }
     *abort_flag = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
@@ -327,6 +342,60 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         }
       }
     }
+  } else if (warp == 3 && IM != IN_PRE) {
+    // ---------------------------------------------------------------- row items and coefficients
+    // One tile ahead of the producers, this warp writes into the tile's half of the double-buffered
+    // tables the item of every window row and, when the prologue is affine and cin <= TC_TAB, the
+    // AdaIN (scale, shift) of one item of the window (that of its middle row; items span
+    // thousands of rows, so it is nearly always every row's) for all channels; the Snake
+    // (alpha, 1 / alpha) table is written once, before the first tile. The producers then read
+    // shared memory where they would otherwise wait on global loads at every tile and channel
+    // block. All loads of a table are issued before any is stored.
+    const int cin = a.cin, win_rows = p.win_rows;
+    const bool tab = p.tab != 0;
+    if (tab && in_mode == IN_ADAIN_SNAKE) {
+      float av[TC_TAB / 32];
+#pragma unroll
+      for (int k = 0; k < TC_TAB / 32; k++) {
+        const int c = lane + 32 * k;
+        av[k] = c < cin ? a.alpha[c] : 1.0f;
+      }
+#pragma unroll
+      for (int k = 0; k < TC_TAB / 32; k++) atab[lane + 32 * k] = make_float2(av[k], 1.0f / av[k]);
+    }
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
+      const int bf = lt & 1;
+      if (!mbar_wait(&meta_empty[bf], ((lt >> 1) & 1) ^ 1, abort_flag, p.err)) break;
+      const InSpan sp = in_span(p, tile, in_up2);
+      int* ri = ritem + bf * TC_MAX_WIN;
+      int iv[TC_MAX_WIN / 32];
+#pragma unroll
+      for (int k = 0; k < TC_MAX_WIN / 32; k++) {
+        const int r = lane + 32 * k, g = sp.base + r;
+        iv[k] = (r >= win_rows || g < 0 || g >= a.L_in) ? -1 : (in_mode == IN_NOMASK ? 0 : dom_item(a.din, g));
+      }
+#pragma unroll
+      for (int k = 0; k < TC_MAX_WIN / 32; k++)
+        if (lane + 32 * k < win_rows) ri[lane + 32 * k] = iv[k];
+      __syncwarp();
+      if (tab) {
+        int item = ri[win_rows / 2];
+        if (item < 0) item = ri[0] >= 0 ? ri[0] : ri[win_rows - 1];
+        float2 cv[TC_TAB / 32];
+#pragma unroll
+        for (int k = 0; k < TC_TAB / 32; k++) {
+          const int c = lane + 32 * k;
+          cv[k] = (item >= 0 && c < cin) ? a.coef[(long)item * cin + c] : make_float2(0.0f, 0.0f);
+        }
+        float2* ct = ctab + bf * TC_TAB;
+#pragma unroll
+        for (int k = 0; k < TC_TAB / 32; k++) ct[lane + 32 * k] = cv[k];
+        if (lane == 0) mitem[bf] = item;
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&meta_full[bf]);  // release: the tables are visible to the waiters
+    }
   } else if (warp >= 4 && warp < 4 + TC_NEPI) {
     // ---------------------------------------------------------------- epilogue
     // Warp ew owns the 32 channels of TMEM lane quarter q = warp % 4 for time rows
@@ -337,9 +406,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     const int ew = warp - 4;
     const int q = warp & 3;
     const int hrow = (ew >> 2) * TC_EROWS;
-    float* stg = (float*)(epi + ew * TC_EPI_WARP_BYTES);         // [2][16][32]
-    float* rsb = stg + 2 * TC_EC * 32;                            // [TC_RES_DEPTH][16][32]
-    int* eit = (int*)(rsb + TC_RES_DEPTH * TC_EC * 32);           // [128]
+    const bool need_res = out_mode_k == OUT_ADD || out_mode_k == OUT_PLUS;
+    float* stg = (float*)(epi + ew * p.epb);                      // [2][16][32]
+    float* rsb = stg + 2 * TC_EC * 32;                            // [TC_RES_DEPTH][16][32] (need_res)
+    int* eit = (int*)(rsb + (need_res ? TC_RES_DEPTH : 0) * TC_EC * 32);  // [128]
     uint64_t* rbar = res_full + ew * TC_RES_DEPTH;
     constexpr int NCH = TC_EROWS / TC_EC;
     const bool trc = p.trace && blockIdx.x == 0 && ew == 0 && lane == 0;
@@ -349,7 +419,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     uint32_t rcons = 0, riss = 0;  // residual chunks consumed / issued by this warp
     const int out_mode = out_mode_k, L_out = a.L_out;
     const float oscale = a.oscale;
-    const bool need_res = out_mode == OUT_ADD || out_mode == OUT_PLUS;
     double* const stat = a.stat;
     uint32_t lt = 0;
     bool bad = false;
@@ -489,14 +558,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     }
   } else if (warp >= 4 + TC_NEPI && IM != IN_PRE) {
     // ---------------------------------------------------------------- activation producers
-    // At each tile the producers first resolve the item of every window row into shared memory
-    // (one lookup per row, shared by all channel blocks). Then, box by box, thread (box row
-    // prow = ptid / 8, chunk j = ptid % 8) converts 8 channels of one input row;
-    // with the x2 upsample each input row feeds two window rows. The item's AdaIN coefficients stay
-    // in registers until the item changes.
+    // Box by box, thread (box row prow = ptid / 8, chunk j = ptid % 8) converts 8 channels of one
+    // input row, with the row's item from the tile's row-item table (written by warp 3); with the
+    // x2 upsample each input row feeds two window rows. The item's AdaIN coefficients stay in
+    // registers until the item changes; they and the Snake alphas come from the shared-memory
+    // tables when the layer has them (else from global memory).
     const int ptid = threadIdx.x - (4 + TC_NEPI) * 32;  // 0 .. TC_NPROD * 32 - 1
     const int j = ptid & 7, prow = ptid >> 3;
-    const int cin = a.cin, L_in = a.L_in, up2 = in_up2, win_rows = p.win_rows;
+    const int cin = a.cin, up2 = in_up2, win_rows = p.win_rows;
     const float2* __restrict__ coef = a.coef;
     const float slope = a.slope;
     const bool affine = in_mode == IN_ADAIN_LEAKY || in_mode == IN_ADAIN_SNAKE;
@@ -506,17 +575,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     int in_sl = 0;
     uint32_t in_ph = 0;  // input ring slot and phase parity of the next box
     const bool trc = p.trace && blockIdx.x == 0 && ptid == 0;
+    const bool tab = p.tab != 0;
     unsigned long long tpw = 0, tpi = 0;
     const long long t_start = clock64();
     bool ok = true;
-    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
+    uint32_t lt = 0;
+    for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, lt++) {
       const InSpan sp = in_span(p, tile, in_up2);
-      asm volatile("bar.sync 1, %0;" ::"n"(TC_NPROD * 32) : "memory");  // previous tile's windows are all written
-      for (int r = ptid; r < win_rows; r += TC_NPROD * 32) {
-        const int g = sp.base + r;
-        ritem[r] = (g < 0 || g >= L_in) ? -1 : (in_mode == IN_NOMASK ? 0 : dom_item(a.din, g));
-      }
-      asm volatile("bar.sync 1, %0;" ::"n"(TC_NPROD * 32) : "memory");
+      const int bf = lt & 1;
+      if (!mbar_wait_t(&meta_full[bf], (lt >> 1) & 1, abort_flag, p.err, trc ? &tpw : nullptr)) break;
+      const int* ri = ritem + bf * TC_MAX_WIN;
+      const float2* ct = ctab + bf * TC_TAB;
+      const int titem = tab ? mitem[bf] : -1;
       for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
         const int xs = xit % XST;
         if (!mbar_wait_t(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err, trc ? &tpw : nullptr)) {
@@ -532,15 +602,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         float al[8], ial[8], ca[8], cbb[8];
         int cached = -1;
         if (snake) {
+          if (tab) {  // (alpha, 1 / alpha) of chA .. chA + 3 and chA + 32 .. chA + 35: 4 x 16 bytes
 #pragma unroll
-          for (int e = 0; e < 8; e++) {
-            al[e] = chs[e] < cin ? a.alpha[chs[e]] : 1.0f;
-            ial[e] = 1.0f / al[e];
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+              for (int e2 = 0; e2 < 4; e2 += 2) {
+                const float4 q4 = *reinterpret_cast<const float4*>(atab + chA + 32 * h + e2);
+                al[4 * h + e2] = q4.x, ial[4 * h + e2] = q4.y, al[4 * h + e2 + 1] = q4.z, ial[4 * h + e2 + 1] = q4.w;
+              }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              al[e] = chs[e] < cin ? a.alpha[chs[e]] : 1.0f;
+              ial[e] = 1.0f / al[e];
+            }
           }
+        }
+        // (scale, shift) of this thread's channels for item b: from the tile's table when b is its item
+        auto load_coef = [&](int b) {
+          if (tab && b == titem) {
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+#pragma unroll
+              for (int e2 = 0; e2 < 4; e2 += 2) {
+                const float4 q4 = *reinterpret_cast<const float4*>(ct + chA + 32 * h + e2);
+                ca[4 * h + e2] = q4.x, cbb[4 * h + e2] = q4.y, ca[4 * h + e2 + 1] = q4.z, cbb[4 * h + e2 + 1] = q4.w;
+              }
+          } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+              const float2 q2 = chs[e] < cin ? coef[(long)b * cin + chs[e]] : make_float2(0.0f, 0.0f);
+              ca[e] = q2.x, cbb[e] = q2.y;
+            }
+          }
+        };
+        if (affine && tab && titem >= 0) {
+          cached = titem;
+          load_coef(titem);
         }
         // prologue of one window row r from the 8 input values v, stored as bf16
         auto emit = [&](int r, const float (&v)[8]) {
-          const int b = ritem[r];
+          const int b = ri[r];
           float o[8];
           if (b < 0) {
 #pragma unroll
@@ -548,11 +650,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           } else if (affine) {
             if (b != cached) {
               cached = b;
-#pragma unroll
-              for (int e = 0; e < 8; e++) {
-                const float2 q2 = chs[e] < cin ? coef[(long)b * cin + chs[e]] : make_float2(0.0f, 0.0f);
-                ca[e] = q2.x, cbb[e] = q2.y;
-              }
+              load_coef(b);
             }
             // packed f32x2 arithmetic (each lane rounds exactly like the scalar fmaf / multiply)
 #pragma unroll
@@ -619,6 +717,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         __syncwarp();
         if (lane == 0) mbar_arrive(&x_full[xs]);
       }
+      __syncwarp();
+      if (ok && lane == 0) mbar_arrive(&meta_empty[bf]);  // this warp is done with the tile's tables
     }
     if (trc) {
       p.trace[TR_PR_WAIT_X] = tpw;
@@ -803,19 +903,29 @@ cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights*
   return cudaSuccess;
 }
 
-static size_t tc_smem(int win_pad, int rst, int xst = 2) {
+// Shared memory of one CTA: weight ring, activation windows, input-box ring, epilogue buffers
+// (epb bytes per warp), mbarriers (+ TMEM slot, abort flag, table items), the double-buffered
+// row-item table and, with tab, the coefficient and alpha tables.
+static size_t tc_smem(int win_pad, int rst, int xst, int epb, bool tab) {
   return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + (size_t)rst * TC_INBOX +
-         (size_t)TC_NEPI * TC_EPI_WARP_BYTES +
-         (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST_MAX + 4 + TC_NEPI * TC_RES_DEPTH) * 8 + 16 + TC_MAX_WIN * 4;
+         (size_t)TC_NEPI * epb + (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST_MAX + 4 + TC_NEPI * TC_RES_DEPTH + 4) * 8 +
+         16 + 2 * TC_MAX_WIN * 4 + (tab ? 3 * TC_TAB * 8 : 0);
 }
 
 static inline int win_pad_of(int K, int dil) { return ((TC_N + (K - 1) * dil + 7) / 8) * 8 + 1; }
 
 // Input-box ring depth that fits next to the other buffers (0 when even 2 stages do not fit).
-static int ring_stages(int win_pad) {
+static int ring_stages(int win_pad, int epb, bool tab) {
   for (int r = TC_RST_MAX; r >= 2; r--)
-    if (tc_smem(win_pad, r) <= (size_t)TC_SMEM_MAX) return r;
+    if (tc_smem(win_pad, r, 2, epb, tab) <= (size_t)TC_SMEM_MAX) return r;
   return 0;
+}
+
+static int epb_of(const ConvArgs& a) { return tc_epi_warp_bytes(a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS); }
+
+// The shared-memory coefficient tables serve affine prologues of up to TC_TAB input channels.
+static bool tab_of(const ConvArgs& a, int cin_pad) {
+  return (a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && cin_pad <= TC_TAB;
 }
 
 static bool rows_ok(const void* base, long ld) { return base && ld % 4 == 0 && (((uintptr_t)base) & 15) == 0; }
@@ -825,7 +935,7 @@ bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (a.L_out < 64) return false;  // tiny row counts (per-item style projections) stay on SIMT
   if ((a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && !a.coef) return false;
   if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
-  if (ring_stages(win_pad_of(a.K, a.dil)) == 0) return false;
+  if (ring_stages(win_pad_of(a.K, a.dil), epb_of(a), tab_of(a, t.cin_pad)) == 0) return false;
   // every global operand moves by TMA: 16-byte aligned bases and row strides
   if ((a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) || !rows_ok(a.y, a.ldy)) return false;
   if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
@@ -926,11 +1036,13 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   p.win_rows = TC_N + (a.K - 1) * a.dil;
   p.win_pad = win_pad_of(a.K, a.dil);
   p.err = err;
-  p.rst = pre ? 0 : ring_stages(p.win_pad);
+  p.epb = epb_of(a);
+  p.tab = !pre && tab_of(a, t.cin_pad);
+  p.rst = pre ? 0 : ring_stages(p.win_pad, p.epb, p.tab);
   p.xst = 2;
   if (pre)  // no input ring: spend its shared memory on deeper window staging
-    while (p.xst < TC_XST_MAX && tc_smem(p.win_pad, 0, p.xst + 1) <= (size_t)TC_SMEM_MAX) p.xst++;
-  const size_t smem = tc_smem(p.win_pad, p.rst, p.xst);
+    while (p.xst < TC_XST_MAX && tc_smem(p.win_pad, 0, p.xst + 1, p.epb, false) <= (size_t)TC_SMEM_MAX) p.xst++;
+  const size_t smem = tc_smem(p.win_pad, p.rst, p.xst, p.epb, p.tab);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && g_num_sms[dev] == 0) {
