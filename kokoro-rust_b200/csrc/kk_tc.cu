@@ -28,8 +28,10 @@
 //    by TMA tensor loads two boxes ahead.
 //
 // Warp roles (20 warps): 0 weight loader + TMEM owner, 1 MMA issuer (one elected lane), 2 input
-// loader, 3 idle, 4-11 epilogue, 12-19 activation producers. Persistent CTAs walk the tiles in
-// time-fastest order so the CTAs running together share one co tile's weights in L2.
+// loader, 3 row items and coefficient tables (fused route), 4-11 epilogue, 12-19 activation
+// producers. Persistent CTAs walk the tiles in output-channel-fastest order: the CTAs running
+// together cover every co tile of a few time tiles, so each input window leaves HBM once and the
+// other co tiles read it from L2 (a layer's weights, at most a few MB, stay in L2 throughout).
 //
 // Every mbarrier wait is bounded (1 s of %globaltimer): on expiry the CTA records the failure in
 // the engine's error flag, drains its own bulk copies (bounded), releases its TMEM and returns.
@@ -108,7 +110,7 @@ struct InSpan {
 };
 __device__ __forceinline__ InSpan in_span(const TcArgs& p, int tile, int up2) {
   InSpan s;
-  s.base = (tile % p.n_tt) * TC_N - p.a.pad;
+  s.base = (tile / p.n_cot) * TC_N - p.a.pad;
   const int last = s.base + p.win_rows - 1;
   s.xr0 = up2 ? (s.base >> 1) : s.base;
   const int xr1 = up2 ? (last >> 1) : last;
@@ -199,7 +201,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       const long long t_start = clock64();
       uint32_t it = 0;
       for (int tile = blockIdx.x; tile < ntiles && !*abort_flag; tile += gridDim.x) {
-        const int cot = tile / p.n_tt;
+        const int cot = tile % p.n_cot;
         const uint8_t* src = (const uint8_t*)p.wimg + (size_t)cot * p.ncb * K * TC_WBLOCK;
         for (int s = 0; s < p.ncb * K; s++, it++) {
           const int st = it % TC_WST;
@@ -282,7 +284,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       uint32_t xit = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const long row0 = (long)(tile % p.n_tt) * TC_N - a.pad + PRE_PAD_FRONT;
+        const long row0 = (long)(tile / p.n_cot) * TC_N - a.pad + PRE_PAD_FRONT;
         for (int cb = 0; cb < p.ncb; cb++, xit++) {
           const int xs = xit % XST;
           if (!mbar_wait(&x_empty[xs], ((xit / XST) & 1) ^ 1, abort_flag, p.err)) {
@@ -424,7 +426,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     bool bad = false;
     for (int tile = blockIdx.x; tile < ntiles && !bad; tile += gridDim.x, lt++) {
       const int ab = lt & 1;
-      const int cot = tile / p.n_tt, tt = tile % p.n_tt;
+      const int cot = tile % p.n_cot, tt = tile / p.n_cot;
       const int co0 = cot * TC_M + q * 32;
       const int co = co0 + lane;
       const int t0 = tt * TC_N + hrow;
