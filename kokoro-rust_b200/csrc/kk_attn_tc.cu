@@ -84,41 +84,53 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
 
-  // ---- operands: Q tile, K, V^T as bf16 (a warp stores 32 consecutive rows of one chunk: no
-  // shared-memory bank conflicts)
-  for (int c = 0; c < 8; c++) {
-    const int r = tid;
-    float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (q0 + r < T) {
-      const float* p = base + (long)(q0 + r) * ld + c * 8;
-      const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-      const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
-      v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-    }
-    *reinterpret_cast<uint4*>(Qs + c * (ATT_QT * 16) + r * 16) = pack8_bf16(v);
-  }
-  for (int c = 0; c < 8; c++)
-    for (int j = tid; j < Tp; j += 128) {
-      float v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      if (j < T) {
-        const float* p = base + (long)j * ld + 768 + c * 8;
-        const float4 a = __ldg(reinterpret_cast<const float4*>(p));
-        const float4 b = __ldg(reinterpret_cast<const float4*>(p + 4));
-        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
-      }
-      *reinterpret_cast<uint4*>(Ks + c * (TMAX * 16) + j * 16) = pack8_bf16(v);
-    }
-  // V^T: task (key chunk kc, dim d): 8 keys of one dim -> one 16-byte store (a warp covers 32
-  // consecutive dims of one key chunk: coalesced loads, conflict-free stores)
-  for (int t = tid; t < (Tp / 8) * ATT_D; t += 128) {
-    const int kc = t / ATT_D, d = t % ATT_D;
-    float v[8];
+  // ---- operands: Q tile, K, V^T as bf16. Every row's (or task's) loads are issued before any of
+  // its stores, so each thread has 16-32 loads in flight instead of waiting on them one chunk at a
+  // time (the pass is bound by memory latency). A warp stores 32 consecutive rows of one chunk: no
+  // shared-memory bank conflicts.
+  auto load_row = [&](int row, int off, float4 (&rv)[16]) {
+    const float4* p = reinterpret_cast<const float4*>(base + (long)row * ld + off);
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const int j = kc * 8 + e;
-      v[e] = j < T ? __ldg(base + (long)j * ld + 1536 + d) : 0.0f;
+    for (int c = 0; c < 16; c++) rv[c] = row < T ? __ldg(p + c) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  };
+  auto store_row = [&](uint8_t* dst, int stride, int row, const float4 (&rv)[16]) {
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      const float v[8] = {rv[2 * c].x, rv[2 * c].y, rv[2 * c].z, rv[2 * c].w,
+                          rv[2 * c + 1].x, rv[2 * c + 1].y, rv[2 * c + 1].z, rv[2 * c + 1].w};
+      *reinterpret_cast<uint4*>(dst + c * stride + row * 16) = pack8_bf16(v);
     }
-    *reinterpret_cast<uint4*>(Vt + kc * (ATT_D * 16) + d * 16) = pack8_bf16(v);
+  };
+  {
+    float4 rv[16];
+    load_row(q0 + tid, 0, rv);
+    store_row(Qs, ATT_QT * 16, tid, rv);
+  }
+  for (int j = tid; j < Tp; j += 128) {
+    float4 rv[16];
+    load_row(j, 768, rv);
+    store_row(Ks, TMAX * 16, j, rv);
+  }
+  // V^T: task (key chunk kc, dim d): 8 keys of one dim -> one 16-byte store (a warp covers 32
+  // consecutive dims of one key chunk: coalesced loads, conflict-free stores); 4 tasks per thread
+  // in flight
+  const int ntask = (Tp / 8) * ATT_D;
+  for (int t0 = 0; t0 < ntask; t0 += 4 * 128) {
+    float v[4][8];
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int t = t0 + u * 128 + tid, kc = t / ATT_D, d = t % ATT_D;
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int j = kc * 8 + e;
+        v[u][e] = (t < ntask && j < T) ? __ldg(base + (long)j * ld + 1536 + d) : 0.0f;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; u++) {
+      const int t = t0 + u * 128 + tid, kc = t / ATT_D, d = t % ATT_D;
+      if (t < ntask) *reinterpret_cast<uint4*>(Vt + kc * (ATT_D * 16) + d * 16) = pack8_bf16(v[u]);
+    }
   }
   fence_proxy_async();
   tc_fence_before();
