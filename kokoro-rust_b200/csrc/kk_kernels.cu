@@ -137,10 +137,85 @@ __global__ void ln_rows_kernel(const float* x, int ldx, int d, const float* g, c
   }
 }
 
+// The same normalisation with one warp per row (d = 128 * NV, rows held in registers as float4):
+// no block barriers, 8 rows per 256-thread block. Sums in double as above (the float mean and
+// variance do not depend on the summation order).
+__device__ __forceinline__ double warp_sum_d(double v) {
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+template <int NV>
+__global__ void __launch_bounds__(256) ln_rows_warp_kernel(const float* x, int ldx, int rows, const float* g,
+                                                           const float* bb, float eps, int mode, float slope,
+                                                           const int* row_item, const float* gb, int ldgb,
+                                                           const float* style, int sdim, float* y, int ldy) {
+  constexpr int d = 128 * NV;
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= rows) return;
+  const float4* row = reinterpret_cast<const float4*>(x + (long)r * ldx);
+  float* yr = y + (long)r * ldy;
+  int item = 0;
+  if (mode == 2) {
+    item = row_item[r];
+    if (item < 0) {
+      for (int j = lane; j < d + sdim; j += 32) yr[j] = 0.0f;
+      return;
+    }
+  }
+  float4 v[NV];
+#pragma unroll
+  for (int k = 0; k < NV; k++) v[k] = row[lane + 32 * k];
+  double s = 0.0;
+#pragma unroll
+  for (int k = 0; k < NV; k++) s += ((double)v[k].x + (double)v[k].y) + ((double)v[k].z + (double)v[k].w);
+  const float mean = (float)(warp_sum_d(s) / (double)d);
+  double q = 0.0;
+#pragma unroll
+  for (int k = 0; k < NV; k++) {
+    const double c0 = (double)(v[k].x - mean), c1 = (double)(v[k].y - mean);
+    const double c2 = (double)(v[k].z - mean), c3 = (double)(v[k].w - mean);
+    q += (c0 * c0 + c1 * c1) + (c2 * c2 + c3 * c3);
+  }
+  const float inv = 1.0f / sqrtf((float)(warp_sum_d(q) / (double)d) + eps);
+  float4* yo = reinterpret_cast<float4*>(yr);
+#pragma unroll
+  for (int k = 0; k < NV; k++) {
+    const int j = 4 * (lane + 32 * k);
+    float o[4] = {(v[k].x - mean) * inv, (v[k].y - mean) * inv, (v[k].z - mean) * inv, (v[k].w - mean) * inv};
+    if (mode == 2) {
+      const float* gg = gb + (long)item * ldgb;
+#pragma unroll
+      for (int e = 0; e < 4; e++) o[e] = (1.0f + gg[j + e]) * o[e] + gg[d + j + e];
+    } else {
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        if (g) o[e] = o[e] * g[j + e];
+        if (bb) o[e] = o[e] + bb[j + e];
+        if (mode == 1) o[e] = leaky(o[e], slope);
+      }
+    }
+    yo[lane + 32 * k] = make_float4(o[0], o[1], o[2], o[3]);
+  }
+  if (mode == 2)
+    for (int j = lane; j < sdim; j += 32) yr[d + j] = style[(long)item * sdim + j];
+}
+
 cudaError_t launch_ln_rows(const float* x, int ldx, int rows, int d, const float* g, const float* b, float eps,
                            int mode, float slope, const int* row_item, const float* gb, int ldgb,
                            const float* style, int sdim, float* y, int ldy, cudaStream_t st) {
   if (rows == 0) return cudaSuccess;
+  const bool vec = ldx % 4 == 0 && ldy % 4 == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  if (vec && (d == 512 || d == 768)) {
+    const int grid = (rows + 7) / 8;
+    if (d == 512)
+      ln_rows_warp_kernel<4><<<grid, 256, 0, st>>>(x, ldx, rows, g, b, eps, mode, slope, row_item, gb, ldgb, style,
+                                                   sdim, y, ldy);
+    else
+      ln_rows_warp_kernel<6><<<grid, 256, 0, st>>>(x, ldx, rows, g, b, eps, mode, slope, row_item, gb, ldgb, style,
+                                                   sdim, y, ldy);
+    return cudaGetLastError();
+  }
   ln_rows_kernel<<<rows, 256, 0, st>>>(x, ldx, d, g, b, eps, mode, slope, row_item, gb, ldgb, style, sdim, y, ldy);
   return cudaGetLastError();
 }
