@@ -25,6 +25,7 @@ SHAPES = [
     ("k7_128_snake_add", 128, 128, 7, 1, 3, 1, False, 1 << 20, (20000, 40000)),
     ("k7_256_snake_store_st", 256, 256, 7, 1, 3, 0, True, 300000, (4000, 8000)),
     ("k3_256_snake_store_st", 256, 256, 3, 1, 3, 0, True, 300000, (4000, 8000)),
+    ("k11_256_snake_plus_st", 256, 256, 11, 1, 3, 2, True, 300000, (4000, 8000)),
     ("k1_768_2304", 768, 2304, 1, 1, 0, 0, False, 34676, (60, 260)),
     ("k1_2048_768_plus", 2048, 768, 1, 1, 0, 2, False, 34676, (60, 260)),
     ("k3_1090_1024_mask_st", 1090, 1024, 3, 1, 1, 0, True, 69805, (100, 500)),
