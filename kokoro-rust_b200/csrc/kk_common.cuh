@@ -63,7 +63,9 @@ enum OutMode : int {
   OUT_STORE = 0,     // y = acc + bias
   OUT_ADD = 1,       // y += acc + bias
   OUT_PLUS = 2,      // y = ((acc + bias) + sc) * oscale
-  OUT_GELU = 3       // y = gelu_new(acc + bias)
+  OUT_GELU = 3,      // y = gelu_new(acc + bias)
+  OUT_GELU_PRE = 4   // gelu_new(acc + bias) written as bf16 window planes (ypre), the IN_PRE input of a
+                     // following layer, instead of f32 rows (tensor-core path, cout a multiple of 64)
 };
 
 struct ConvArgs {
@@ -101,6 +103,9 @@ struct ConvArgs {
   // at plane row PRE_PAD_FRONT + r (chunk j holds channels 4j..4j+3 and 32+4j..32+4j+3)
   const void* xpre;
   long pre_rows;
+  // OUT_GELU_PRE: output planes in the same layout, ypre_rows rows per plane
+  void* ypre;
+  long ypre_rows;
 };
 
 __device__ __forceinline__ float leaky(float v, float s) { return v < 0.0f ? v * s : v; }

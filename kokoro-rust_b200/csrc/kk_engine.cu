@@ -784,7 +784,9 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   const bool res = a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS;
   const bool tc_path = precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc);
   const double in_rows = a.in_up2 ? (double)((a.L_in + 1) / 2) : (double)a.L_in;
-  const double bytes = 4.0 * (in_rows * a.cin + (double)a.L_out * a.cout * (res ? 2 : 1)) +
+  // bf16 window planes in or out: 2 bytes per element
+  const double in_b = a.in_mode == IN_PRE ? 2.0 : 4.0, out_b = a.out_mode == OUT_GELU_PRE ? 2.0 : 4.0;
+  const double bytes = in_b * in_rows * a.cin + out_b * (double)a.L_out * a.cout + (res ? 4.0 * a.L_out * a.cout : 0.0) +
                        (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
   if (tc_path) {
     unsigned long long* tr = nullptr;
@@ -792,7 +794,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       tr = ar.get<unsigned long long>(16);
       KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
     }
-    if (c.cout > TC_PRE_MIN_COUT) {
+    if (c.cout > TC_PRE_MIN_COUT && a.in_mode != IN_PRE) {
       // several 128-channel output tiles share each input window: transform the input once into
       // bf16 window planes instead of once per output tile
       auto mk = ar.mark();
@@ -1307,7 +1309,23 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     float* qkv = ar.get<float>((size_t)LT * 2304);
     float* ctx = ar.get<float>((size_t)LT * 768);
     float* a = ar.get<float>((size_t)LT * 768);
-    float* f = ar.get<float>((size_t)LT * 2048);
+    // BF16 mode on the tensor cores: the FFN hands its GELU output to the down projection as bf16
+    // window planes (no f32 round trip through HBM, no separate input transform of 2048 channels)
+    float* f = nullptr;
+    const long fpre_rows = PRE_PAD_FRONT + (long)LT + PRE_PAD_BACK;
+    void* fpre = nullptr;
+    bool ffn_planes = false;
+    if (precision == KK_PRECISION_BF16 && tc_ok) {
+      fpre = ar.get<uint8_t>((size_t)(2048 / 64) * 8 * fpre_rows * 16);
+      ConvArgs t1 = ca(m.ffn);
+      t1.x = h, t1.ldx = 768, t1.L_in = LT, t1.L_out = LT, t1.out_mode = OUT_GELU_PRE;
+      t1.ypre = fpre, t1.ypre_rows = fpre_rows;
+      ConvArgs t2 = ca(m.ffn_out);
+      t2.in_mode = IN_PRE, t2.xpre = fpre, t2.pre_rows = fpre_rows, t2.L_in = LT;
+      t2.y = h, t2.ldy = 768, t2.L_out = LT, t2.out_mode = OUT_PLUS, t2.sc = h, t2.ldsc = 768;
+      ffn_planes = tc_route(m.ffn, t1) && tc_route(m.ffn_out, t2);
+    }
+    if (!ffn_planes) f = ar.get<float>((size_t)LT * 2048);
     linear(m.map_in, emb, 128, LT, h, 768);
     int max_t = 0;
     for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
@@ -1344,8 +1362,20 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       check(launch_ln_rows(a, 768, LT, 768, m.attn_g, m.attn_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, a,
                            768, st),
             "ln");
-      linear(m.ffn, a, 768, LT, f, 2048, OUT_GELU);
-      linear(m.ffn_out, f, 2048, LT, h, 768, OUT_PLUS, a, 768);
+      if (ffn_planes) {
+        // the FFN's GELU output goes straight into the bf16 window planes its down projection reads
+        ConvArgs a1 = ca(m.ffn);
+        a1.x = a, a1.ldx = 768, a1.L_in = LT, a1.L_out = LT, a1.out_mode = OUT_GELU_PRE;
+        a1.ypre = fpre, a1.ypre_rows = fpre_rows;
+        run_conv(m.ffn, a1);
+        ConvArgs a2 = ca(m.ffn_out);
+        a2.in_mode = IN_PRE, a2.xpre = fpre, a2.pre_rows = fpre_rows, a2.L_in = LT;
+        a2.y = h, a2.ldy = 768, a2.L_out = LT, a2.out_mode = OUT_PLUS, a2.sc = a, a2.ldsc = 768;
+        run_conv(m.ffn_out, a2);
+      } else {
+        linear(m.ffn, a, 768, LT, f, 2048, OUT_GELU);
+        linear(m.ffn_out, f, 2048, LT, h, 768, OUT_PLUS, a, 768);
+      }
       check(launch_ln_rows(h, 768, LT, 768, m.full_g, m.full_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, h,
                            768, st),
             "ln");

@@ -500,6 +500,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             rr = rsb + sl * TC_EC * 32;
           }
           if (trc) t_res += clock64() - tq, tq = clock64();
+          if (out_mode == OUT_GELU_PRE) {
+            // bf16 window planes for the next layer: lane l holds channel co0 + l, which is element
+            // 4 * h + l % 4 of chunk l / 4 of 64-channel block co0 / 64 (h = 32-channel half); four
+            // lanes make one 8-byte store per row
+            const int h = (co0 >> 5) & 1;
+            uint8_t* pl = (uint8_t*)a.ypre + ((size_t)((co0 >> 6) * 8 + (lane >> 2)) * a.ypre_rows + PRE_PAD_FRONT) * 16 +
+                          h * 8;
+#pragma unroll
+            for (int jj = 0; jj < TC_EC; jj++) {
+              const float r = gelu_new(v[sub * TC_EC + jj] + bias);
+              const float r1 = __shfl_down_sync(0xffffffffu, r, 1);
+              const float r2 = __shfl_down_sync(0xffffffffu, r, 2);
+              const float r3 = __shfl_down_sync(0xffffffffu, r, 3);
+              const int t = t0 + c * TC_EC + jj;
+              if ((lane & 3) == 0 && t < L_out && co0 < a.cout) {
+                __nv_bfloat162 p0 = __floats2bfloat162_rn(r, r1), p1 = __floats2bfloat162_rn(r2, r3);
+                uint2 u;
+                memcpy(&u.x, &p0, 4);
+                memcpy(&u.y, &p1, 4);
+                *reinterpret_cast<uint2*>(pl + (size_t)t * 16) = u;
+              }
+            }
+            continue;
+          }
           float* sb = stg + (c & 1) * TC_EC * 32;
           if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
           __syncwarp();
@@ -939,7 +963,12 @@ bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
   if (ring_stages(win_pad_of(a.K, a.dil), epb_of(a), tab_of(a, t.cin_pad)) == 0) return false;
   // every global operand moves by TMA: 16-byte aligned bases and row strides
-  if ((a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) || !rows_ok(a.y, a.ldy)) return false;
+  if (a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) return false;
+  if (a.out_mode == OUT_GELU_PRE) {
+    if (!a.ypre || (((uintptr_t)a.ypre) & 15) != 0 || a.cout % TC_KB != 0 || a.stat) return false;
+  } else if (!rows_ok(a.y, a.ldy)) {
+    return false;
+  }
   if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
   return true;
 }
@@ -971,6 +1000,7 @@ static TcKernelFn pick_kernel(int im, int up, int om, int* idx) {
       {IN_PRE, 0, OUT_ADD, tc_conv_kernel<IN_PRE, 0, OUT_ADD>},
       {IN_PRE, 0, OUT_PLUS, tc_conv_kernel<IN_PRE, 0, OUT_PLUS>},
       {IN_PRE, 0, OUT_GELU, tc_conv_kernel<IN_PRE, 0, OUT_GELU>},
+      {IN_PRE, 0, OUT_GELU_PRE, tc_conv_kernel<IN_PRE, 0, OUT_GELU_PRE>},
   };
   const int n = (int)(sizeof(table) / sizeof(table[0]));
   for (int i = 0; i < n; i++)
@@ -1026,7 +1056,7 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   const bool pre = a.in_mode == IN_PRE;
   if (pre && (!a.xpre || (((uintptr_t)a.xpre) & 15) != 0)) return cudaErrorInvalidValue;
   bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, TC_BOX_ROWS)) &&
-              make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
+              (a.out_mode == OUT_GELU_PRE || make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC));
   if (maps && a.out_mode == OUT_ADD) maps = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
   if (maps && a.out_mode == OUT_PLUS) maps = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc, 32, TC_EC);
   if (!maps) return cudaErrorInvalidValue;
