@@ -208,9 +208,9 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
 // into columns 0..31); G = columns 0..31 + columns 32..63. A rows are ordered unit * 4 + gate, so
 // the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane transpose through shared
 // memory hands each thread one unit's four gates for 4 items. The new h is split into bf16 hi / lo
-// and pushed straight into every CTA's next H image with st.async, which completes bytes of the
-// receiver's own mbarrier: each CTA waits (bounded) for exactly the bytes of the next step's
-// active items, so steps need no cluster barrier.
+// and written into this CTA's 4 KB slice of its own next H image; one bulk copy per other CTA
+// then sends the slice, completing bytes of the receiver's own mbarrier: each CTA waits (bounded)
+// for the 7 slices of the next step, so steps need no cluster barrier.
 
 constexpr int LT_ROWS = 128;                     // gate rows per CTA (32 units x 4 gates)
 constexpr int LT_KC = LC_H / 8;                  // 8-element K chunks of the recurrent product
@@ -218,6 +218,7 @@ constexpr int LT_ABYTES = LT_KC * LT_ROWS * 16;  // one bf16 W image (64 KB)
 constexpr int LT_HROWS = 2 * LC_IPG;             // H image rows: 32 items hi, then 32 items lo
 constexpr int LT_BBYTES = LT_KC * LT_HROWS * 16; // one H image (32 KB)
 constexpr int LT_GXLD = 17;                      // transpose staging row (floats)
+constexpr int LT_SLICE = 4 * LT_HROWS * 16;      // one CTA's 32 units of an H image (4 KB)
 constexpr uint32_t LT_IDESC_HL = idesc_bf16(LT_ROWS, LT_HROWS);  // Wh x [Hh | Hl]
 constexpr uint32_t LT_IDESC_H = idesc_bf16(LT_ROWS, LC_IPG);     // Wl x Hh
 
@@ -232,6 +233,8 @@ __device__ __forceinline__ uint32_t bf16_bits(float x) {
   return u;
 }
 __device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+// tanh x = 2 sigma(2x) - 1 (absolute error about 1e-7, below the split-operand product error)
+__device__ __forceinline__ float tanh_fast(float x) { return fmaf(2.0f, sigm_fast(2.0f * x), -1.0f); }
 
 __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_kernel(const LstmArgs a) {
   extern __shared__ __align__(1024) uint8_t sm8[];
@@ -283,19 +286,22 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   const int pi = tid >> 3, part = (tid >> 2) & 1, kc4 = tid & 3;
   const int pst = gs[pi], pln = gl[pi];
   const int* act = a.gact + (long)g * a.Tmax;
-  // bytes of the 8 CTAs' pushes made during step s (into H image (s + 1) & 1)
+  // bytes the other 7 CTAs send during step s (into H image (s + 1) & 1): each copies its whole
+  // 4 KB slice (rows of finished items are stale and ignored)
   auto push_bytes = [&](int s) -> uint32_t {
     const int n = s + 1 < a.Tmax ? act[s + 1] : 0;
-    return (uint32_t)(LC_CL * n * 2 * 4 * 16);
+    return n > 0 ? (uint32_t)((LC_CL - 1) * LT_SLICE) : 0u;
   };
-  // cluster addresses of this thread's push slot in each CTA's H images and of their barriers
-  uint32_t rslot[LC_CL], rbar0[LC_CL];
+  // this thread's row of this CTA's slice (in image 0), and the cluster addresses of the slice and
+  // of the H-image barriers in each CTA
+  uint8_t* lslot = Bb + (4 * rank + kc4) * (LT_HROWS * 16) + (part * LC_IPG + pi) * 16;
+  uint32_t rblk[LC_CL], rbar0[LC_CL];
   {
-    const uint32_t slot = smem_u32(Bb + (4 * rank + kc4) * (LT_HROWS * 16) + (part * LC_IPG + pi) * 16);
+    const uint32_t blk = smem_u32(Bb + 4 * rank * (LT_HROWS * 16));
     const uint32_t b0 = smem_u32(&hbar[0]);
 #pragma unroll
     for (int r = 0; r < LC_CL; r++) {
-      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rslot[r]) : "r"(slot), "r"(r));
+      asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rblk[r]) : "r"(blk), "r"(r));
       asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar0[r]) : "r"(b0), "r"(r));
     }
   }
@@ -381,10 +387,10 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
           for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
           const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
           const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
-          const float cg = tanhf(gxv[m][2] + (d[2] + bh[2]));
+          const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
           const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
           c[m] = fg * c[m] + ig * cg;
-          Tile[(i0 + m) * LC_TLD + ul] = og * tanhf(c[m]);
+          Tile[(i0 + m) * LC_TLD + ul] = og * tanh_fast(c[m]);
         }
       }
     }
@@ -408,21 +414,29 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
         }
         w4[e >> 1] = b0 | (b1 << 16);
       }
-      if (pi < na_next) {  // only items still running at step s + 1 are needed there
-        const uint32_t off = (uint32_t)((cur ^ 1) * LT_BBYTES), boff = (uint32_t)((cur ^ 1) * 8);
-#pragma unroll
-        for (int r = 0; r < LC_CL; r++)
-          asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.b32 [%0], {%1, %2, %3, %4}, [%5];" ::
-                           "r"(rslot[r] + off),
-                       "r"(w4[0]), "r"(w4[1]), "r"(w4[2]), "r"(w4[3]), "r"(rbar0[r] + boff)
-                       : "memory");
-      }
+      if (pi < na_next)  // only items still running at step s + 1 are needed there
+        *reinterpret_cast<uint4*>(lslot + (cur ^ 1) * LT_BBYTES) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
       if (part == 0) {
         const int t = dir == 0 ? s : pln - 1 - s;
         float* o = a.out + (long)(pst + t) * a.ldo + dir * LC_H + rank * 32 + 8 * kc4;
         *reinterpret_cast<float4*>(o) = make_float4(hp[0], hp[1], hp[2], hp[3]);
         *reinterpret_cast<float4*>(o + 4) = make_float4(hp[4], hp[5], hp[6], hp[7]);
       }
+    }
+    // this CTA's slice of the next H image is complete: one bulk copy sends it to each other CTA
+    // of the cluster, completing bytes of that CTA's barrier for the image
+    fence_proxy_async();
+    __syncthreads();
+    if (tid == 0 && !bad && na_next > 0) {
+      const uint32_t src = smem_u32(Bb + (cur ^ 1) * LT_BBYTES + 4 * rank * (LT_HROWS * 16));
+      const uint32_t off = (uint32_t)((cur ^ 1) * LT_BBYTES), boff = (uint32_t)((cur ^ 1) * 8);
+#pragma unroll
+      for (int r = 0; r < LC_CL; r++)
+        if (r != rank)
+          asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+                           "r"(rblk[r] + off),
+                       "r"(src), "n"(LT_SLICE), "r"(rbar0[r] + boff)
+                       : "memory");
     }
   }
   // every push was awaited by its receiver inside the loop; the barrier keeps each CTA (and its
