@@ -54,7 +54,8 @@ __host__ __device__ constexpr int att_smem() {
 
 template <int TMAX>
 __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict__ qkv, int ld, const ItemTab* items,
-                                                         const int2* work, float* ctx, int ldc, int* err) {
+                                                         const int2* work, float* ctx, int ldc, int* err,
+                                                         uint8_t* ctx_pre, long ctx_pre_rows) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* Qs = smem;                          // [8 dim chunks][128 rows][8] bf16
   uint8_t* Ks = smem + 16384;                  // [8 dim chunks][TMAX keys][8]
@@ -208,12 +209,26 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
   if (!bad) {
     const float inv = 1.0f / l;
     const bool row_ok = q0 + tid < T;
-    float* out = ctx + (long)(it.tok_start + q0 + tid) * ldc + h * ATT_D;
+    const long row = it.tok_start + q0 + tid;
+    float* out = ctx + row * ldc + h * ATT_D;
 #pragma unroll
     for (int c0 = 0; c0 < ATT_D; c0 += 32) {
       float o[32];
       tmem_ld32(trow + c0, o);
-      if (row_ok) {
+      if (row_ok && ctx_pre) {
+        // head h is 64-channel block h of the planes: channels c0 + 4j .. + 3 are half c0 / 32 of
+        // chunk j
+#pragma unroll
+        for (int jc = 0; jc < 8; jc++) {
+          __nv_bfloat162 p0 = __floats2bfloat162_rn(o[4 * jc] * inv, o[4 * jc + 1] * inv);
+          __nv_bfloat162 p1 = __floats2bfloat162_rn(o[4 * jc + 2] * inv, o[4 * jc + 3] * inv);
+          uint2 u;
+          memcpy(&u.x, &p0, 4);
+          memcpy(&u.y, &p1, 4);
+          *reinterpret_cast<uint2*>(ctx_pre + ((size_t)(h * 8 + jc) * ctx_pre_rows + PRE_PAD_FRONT + row) * 16 +
+                                    (c0 >> 5) * 8) = u;
+        }
+      } else if (row_ok) {
 #pragma unroll
         for (int e = 0; e < 32; e += 4)
           *reinterpret_cast<float4*>(out + c0 + e) =
@@ -232,7 +247,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
 
 template <int TMAX>
 cudaError_t launch_bucket(const float* qkv, int ld, const ItemTab* items, const int2* work, int n, float* ctx, int ldc,
-                          int* err, cudaStream_t st) {
+                          int* err, cudaStream_t st, void* ctx_pre, long ctx_pre_rows) {
   if (n == 0) return cudaSuccess;
   static bool attr[64] = {false};
   int dev = 0;
@@ -243,18 +258,23 @@ cudaError_t launch_bucket(const float* qkv, int ld, const ItemTab* items, const 
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  attn_tc_kernel<TMAX><<<dim3(n, ATT_HEADS), 128, att_smem<TMAX>(), st>>>(qkv, ld, items, work, ctx, ldc, err);
+  attn_tc_kernel<TMAX><<<dim3(n, ATT_HEADS), 128, att_smem<TMAX>(), st>>>(qkv, ld, items, work, ctx, ldc, err,
+                                                                           (uint8_t*)ctx_pre, ctx_pre_rows);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
-                                const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st) {
-  cudaError_t e = launch_bucket<128>(qkv, ldqkv, items, work, n_work[0], ctx, ldc, err, st);
-  if (e == cudaSuccess) e = launch_bucket<256>(qkv, ldqkv, items, work + n_work[0], n_work[1], ctx, ldc, err, st);
+                                const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st, void* ctx_pre,
+                                long ctx_pre_rows) {
+  if (ctx_pre && (((uintptr_t)ctx_pre) & 15) != 0) return cudaErrorInvalidValue;
+  cudaError_t e = launch_bucket<128>(qkv, ldqkv, items, work, n_work[0], ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
   if (e == cudaSuccess)
-    e = launch_bucket<512>(qkv, ldqkv, items, work + n_work[0] + n_work[1], n_work[2], ctx, ldc, err, st);
+    e = launch_bucket<256>(qkv, ldqkv, items, work + n_work[0], n_work[1], ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
+  if (e == cudaSuccess)
+    e = launch_bucket<512>(qkv, ldqkv, items, work + n_work[0] + n_work[1], n_work[2], ctx, ldc, err, st, ctx_pre,
+                           ctx_pre_rows);
   return e;
 }
 

@@ -1309,23 +1309,34 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     float* qkv = ar.get<float>((size_t)LT * 2304);
     float* ctx = ar.get<float>((size_t)LT * 768);
     float* a = ar.get<float>((size_t)LT * 768);
-    // BF16 mode on the tensor cores: the FFN hands its GELU output to the down projection as bf16
-    // window planes (no f32 round trip through HBM, no separate input transform of 2048 channels)
+    // BF16 mode on the tensor cores: every ALBERT linear reads its input as bf16 window planes
+    // written by the stage before it (the attention for the output projection, the LayerNorms for
+    // the QKV and FFN projections, the FFN's GELU epilogue for the down projection), so no f32
+    // activation makes a round trip through HBM only to be transformed again
     float* f = nullptr;
-    const long fpre_rows = PRE_PAD_FRONT + (long)LT + PRE_PAD_BACK;
-    void* fpre = nullptr;
-    bool ffn_planes = false;
+    const long pre_rows = PRE_PAD_FRONT + (long)LT + PRE_PAD_BACK;
+    const size_t planes768 = (size_t)(768 / 64) * 8 * pre_rows * 16;
+    void *hpre = nullptr, *ctxpre = nullptr, *apre = nullptr, *fpre = nullptr;
+    bool planes = false;
+    auto pre_args = [&](const Conv& c, const void* xp, float* y, int ldy, int out_mode, const float* sc, void* yp) {
+      ConvArgs t = ca(c);
+      t.in_mode = IN_PRE, t.xpre = xp, t.pre_rows = pre_rows, t.L_in = LT;
+      t.y = y, t.ldy = ldy, t.L_out = LT, t.out_mode = out_mode, t.sc = sc, t.ldsc = 768;
+      t.ypre = yp, t.ypre_rows = pre_rows;
+      return t;
+    };
     if (precision == KK_PRECISION_BF16 && tc_ok) {
-      fpre = ar.get<uint8_t>((size_t)(2048 / 64) * 8 * fpre_rows * 16);
-      ConvArgs t1 = ca(m.ffn);
-      t1.x = h, t1.ldx = 768, t1.L_in = LT, t1.L_out = LT, t1.out_mode = OUT_GELU_PRE;
-      t1.ypre = fpre, t1.ypre_rows = fpre_rows;
-      ConvArgs t2 = ca(m.ffn_out);
-      t2.in_mode = IN_PRE, t2.xpre = fpre, t2.pre_rows = fpre_rows, t2.L_in = LT;
-      t2.y = h, t2.ldy = 768, t2.L_out = LT, t2.out_mode = OUT_PLUS, t2.sc = h, t2.ldsc = 768;
-      ffn_planes = tc_route(m.ffn, t1) && tc_route(m.ffn_out, t2);
+      hpre = ar.get<uint8_t>(planes768);
+      ctxpre = ar.get<uint8_t>(planes768);
+      apre = ar.get<uint8_t>(planes768);
+      fpre = ar.get<uint8_t>((size_t)(2048 / 64) * 8 * pre_rows * 16);
+      ConvArgs t0 = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE, nullptr, nullptr);
+      ConvArgs t1 = pre_args(m.dense, ctxpre, a, 768, OUT_PLUS, h, nullptr);
+      ConvArgs t2 = pre_args(m.ffn, apre, nullptr, 0, OUT_GELU_PRE, nullptr, fpre);
+      ConvArgs t3 = pre_args(m.ffn_out, fpre, h, 768, OUT_PLUS, a, nullptr);
+      planes = tc_route(m.qkv, t0) && tc_route(m.dense, t1) && tc_route(m.ffn, t2) && tc_route(m.ffn_out, t3);
     }
-    if (!ffn_planes) f = ar.get<float>((size_t)LT * 2048);
+    if (!planes) f = ar.get<float>((size_t)LT * 2048);
     linear(m.map_in, emb, 128, LT, h, 768);
     int max_t = 0;
     for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
@@ -1348,36 +1359,43 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       work_d = upload(all.data(), all.size());
     }
     for (int layer = 0; layer < 12; layer++) {
-      linear(m.qkv, h, 768, LT, qkv, 2304);
+      if (planes && layer > 0) {
+        ConvArgs t = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE, nullptr, nullptr);
+        run_conv(m.qkv, t);
+      } else {
+        linear(m.qkv, h, 768, LT, qkv, 2304);  // the first layer's input comes from map_in
+      }
       cudaEvent_t e0;
       prof_begin(&e0);
       if (attn_tc)
-        check(launch_attention_tc(qkv, 2304, items_d, work_d, n_work, ctx, 768, err_flag, st), "attention(tcgen05)");
+        check(launch_attention_tc(qkv, 2304, items_d, work_d, n_work, ctx, 768, err_flag, st, planes ? ctxpre : nullptr,
+                                  pre_rows),
+              "attention(tcgen05)");
       else
         check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
       double af = 0;
       for (int b = 0; b < B; b++) af += 4.0 * 12 * 64 * (double)ids_len[b] * ids_len[b];
       prof_end(e0, "attention", af);
-      linear(m.dense, ctx, 768, LT, a, 768, OUT_PLUS, h, 768);
+      if (planes) {
+        ConvArgs t1 = pre_args(m.dense, ctxpre, a, 768, OUT_PLUS, h, nullptr);
+        run_conv(m.dense, t1);
+      } else {
+        linear(m.dense, ctx, 768, LT, a, 768, OUT_PLUS, h, 768);
+      }
       check(launch_ln_rows(a, 768, LT, 768, m.attn_g, m.attn_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, a,
-                           768, st),
+                           768, st, planes ? apre : nullptr, pre_rows),
             "ln");
-      if (ffn_planes) {
-        // the FFN's GELU output goes straight into the bf16 window planes its down projection reads
-        ConvArgs a1 = ca(m.ffn);
-        a1.x = a, a1.ldx = 768, a1.L_in = LT, a1.L_out = LT, a1.out_mode = OUT_GELU_PRE;
-        a1.ypre = fpre, a1.ypre_rows = fpre_rows;
-        run_conv(m.ffn, a1);
-        ConvArgs a2 = ca(m.ffn_out);
-        a2.in_mode = IN_PRE, a2.xpre = fpre, a2.pre_rows = fpre_rows, a2.L_in = LT;
-        a2.y = h, a2.ldy = 768, a2.L_out = LT, a2.out_mode = OUT_PLUS, a2.sc = a, a2.ldsc = 768;
-        run_conv(m.ffn_out, a2);
+      if (planes) {
+        ConvArgs t2 = pre_args(m.ffn, apre, nullptr, 0, OUT_GELU_PRE, nullptr, fpre);
+        run_conv(m.ffn, t2);
+        ConvArgs t3 = pre_args(m.ffn_out, fpre, h, 768, OUT_PLUS, a, nullptr);
+        run_conv(m.ffn_out, t3);
       } else {
         linear(m.ffn, a, 768, LT, f, 2048, OUT_GELU);
         linear(m.ffn_out, f, 2048, LT, h, 768, OUT_PLUS, a, 768);
       }
       check(launch_ln_rows(h, 768, LT, 768, m.full_g, m.full_b, 1e-12f, 0, 0.0f, nullptr, nullptr, 0, nullptr, 0, h,
-                           768, st),
+                           768, st, planes && layer < 11 ? hpre : nullptr, pre_rows),
             "ln");
     }
     // bert_encoder -> d_en, then [d_en | s_pro] (src/gpu_batch.rs:223-231)

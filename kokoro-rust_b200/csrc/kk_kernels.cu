@@ -7,7 +7,9 @@
 // the SineGen phase path uses the reference's FMA placement and f64 accumulation
 // (kernels/kokoro.cu:188-254), durations use a sequential f32 sigmoid sum with
 // round-half-to-even (src/model.rs:90-99), STFT / iSTFT run their DFTs in f64 (:470-508).
+#include <cuda_bf16.h>
 #include <math.h>
+#include <string.h>
 #include "kk_common.cuh"
 #include "kk_launch.h"
 
@@ -149,7 +151,8 @@ template <int NV>
 __global__ void __launch_bounds__(256) ln_rows_warp_kernel(const float* x, int ldx, int rows, const float* g,
                                                            const float* bb, float eps, int mode, float slope,
                                                            const int* row_item, const float* gb, int ldgb,
-                                                           const float* style, int sdim, float* y, int ldy) {
+                                                           const float* style, int sdim, float* y, int ldy,
+                                                           uint8_t* ypre, long ypre_rows) {
   constexpr int d = 128 * NV;
   const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
   if (r >= rows) return;
@@ -196,6 +199,14 @@ __global__ void __launch_bounds__(256) ln_rows_warp_kernel(const float* x, int l
       }
     }
     yo[lane + 32 * k] = make_float4(o[0], o[1], o[2], o[3]);
+    if (ypre) {  // channels j .. j + 3: half (j / 32) % 2 of chunk (j % 32) / 4 of block j / 64
+      __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
+      uint2 u;
+      memcpy(&u.x, &p0, 4);
+      memcpy(&u.y, &p1, 4);
+      const int plane = (j >> 6) * 8 + ((j & 31) >> 2);
+      *reinterpret_cast<uint2*>(ypre + ((size_t)plane * ypre_rows + PRE_PAD_FRONT + r) * 16 + ((j >> 5) & 1) * 8) = u;
+    }
   }
   if (mode == 2)
     for (int j = lane; j < sdim; j += 32) yr[d + j] = style[(long)item * sdim + j];
@@ -203,17 +214,20 @@ __global__ void __launch_bounds__(256) ln_rows_warp_kernel(const float* x, int l
 
 cudaError_t launch_ln_rows(const float* x, int ldx, int rows, int d, const float* g, const float* b, float eps,
                            int mode, float slope, const int* row_item, const float* gb, int ldgb,
-                           const float* style, int sdim, float* y, int ldy, cudaStream_t st) {
+                           const float* style, int sdim, float* y, int ldy, cudaStream_t st, void* ypre,
+                           long ypre_rows) {
   if (rows == 0) return cudaSuccess;
   const bool vec = ldx % 4 == 0 && ldy % 4 == 0 && (((uintptr_t)x | (uintptr_t)y) & 15) == 0;
+  if (ypre && (!vec || mode == 2 || (d != 512 && d != 768) || (((uintptr_t)ypre) & 15) != 0))
+    return cudaErrorInvalidValue;
   if (vec && (d == 512 || d == 768)) {
     const int grid = (rows + 7) / 8;
     if (d == 512)
       ln_rows_warp_kernel<4><<<grid, 256, 0, st>>>(x, ldx, rows, g, b, eps, mode, slope, row_item, gb, ldgb, style,
-                                                   sdim, y, ldy);
+                                                   sdim, y, ldy, (uint8_t*)ypre, ypre_rows);
     else
       ln_rows_warp_kernel<6><<<grid, 256, 0, st>>>(x, ldx, rows, g, b, eps, mode, slope, row_item, gb, ldgb, style,
-                                                   sdim, y, ldy);
+                                                   sdim, y, ldy, (uint8_t*)ypre, ypre_rows);
     return cudaGetLastError();
   }
   ln_rows_kernel<<<rows, 256, 0, st>>>(x, ldx, d, g, b, eps, mode, slope, row_item, gb, ldgb, style, sdim, y, ldy);

@@ -33,9 +33,12 @@ cudaError_t launch_embed_rows(const int* ids, const int* row_item, int rows, con
 //  mode 2: AdaLayerNorm (no affine, (1 + g) * x + b with gb rows per item, kernels/kokoro.cu:337-372),
 //          written to y[:, 0:d], followed by the item's style in y[:, d:d+sdim] (cat_style_rows_seg,
 //          :375-383); gap rows of y -> 0.
+// ypre (optional, d = 512 / 768, modes 0 / 1): the output rows also as bf16 window planes (the
+// IN_PRE operand layout of kk_common.cuh, ypre_rows rows per plane) for a following tensor-core layer.
 cudaError_t launch_ln_rows(const float* x, int ldx, int rows, int d, const float* g, const float* b,
                            float eps, int mode, float slope, const int* row_item, const float* gb,
-                           int ldgb, const float* style, int sdim, float* y, int ldy, cudaStream_t st);
+                           int ldgb, const float* style, int sdim, float* y, int ldy, cudaStream_t st,
+                           void* ypre = nullptr, long ypre_rows = 0);
 // cat_style_rows_seg: y[:, d:d+sdim] = style[item]; gap rows of y[:, 0:d+sdim] -> 0
 cudaError_t launch_cat_style(const int* row_item, int rows, int d, const float* style, int sdim, float* y,
                              int ldy, cudaStream_t st);
@@ -45,8 +48,11 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
 // The same attention on tcgen05 tensor cores (bf16 Q, K, V and P, fp32 accumulation and softmax).
 // work: (item, first query row) per 128-query tile, grouped by item length into the buckets
 // T <= 128, T <= 256 and T <= 512 of n_work[0..2] entries. err receives 3 if an MMA wait expires.
+// With ctx_pre set, ctx is written only as bf16 window planes (IN_PRE layout, ctx_pre_rows rows per
+// plane; head h = 64-channel block h) for the output projection, and ctx is not touched.
 cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
-                                const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st);
+                                const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st,
+                                void* ctx_pre = nullptr, long ctx_pre_rows = 0);
 
 // ---- LSTM recurrence (one launch per BiLSTM, thread-block clusters; kk_lstm.cu)
 // Items sorted longest-first form G groups of LSTM_IPG; one cluster of 8 CTAs runs each
