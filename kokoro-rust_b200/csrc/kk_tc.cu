@@ -763,111 +763,104 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
 
 // ------------------------------------------------------------------------------ IN_PRE prologue
 
-// Block (256 plane rows, 64-channel block cb); warp j converts plane cb * 8 + j (channels 4j..4j+3
-// and 32+4j..32+4j+3) of those rows, lane = row within each of 8 groups of 32. The 8 warps together
-// read each input row's 256 bytes once, at the same time (shared sectors hit L1), and each warp
-// writes 512 contiguous bytes of its plane per group. All 8 rows' item lookups and loads are issued
-// before any is used (8 rows in flight per thread: the pass is bound by memory latency otherwise);
-// the transform uses the producer warps' arithmetic, with the item's coefficients cached.
-__global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, uint4* __restrict__ out, long pre_rows) {
-  constexpr int R = 8;
-  const int pl = blockIdx.y * 8 + (threadIdx.x >> 5);
-  const long r0 = blockIdx.x * 256L + (threadIdx.x & 31);
-  const int cin = a.cin;
-  const int cA = (pl >> 3) * TC_KB + 4 * (pl & 7);  // channels cA .. cA + 3 and cA + 32 .. cA + 35
-  const bool vec = cA + 36 <= cin && (a.ldx % 4) == 0 && ((((uintptr_t)a.x) & 15) == 0);
+// Block = 32 plane rows x 128 input channels (two 64-channel blocks), 8 warps. Warp w reads rows
+// 4w .. 4w + 3 of the tile as whole 512-byte row segments (lane l: channels 4l .. 4l + 3; all four
+// rows' loads issued before any is used), applies the layer's prologue with the item's
+// coefficients cached across rows, and leaves bf16 values in a plane-major shared-memory tile
+// (plane stride padded to 33 rows: conflict-free 8-byte stores). Warp w then writes planes 2w and
+// 2w + 1: 32 consecutive 16-byte plane rows, 512 contiguous bytes each. Reads and writes of HBM
+// are both fully coalesced.
+__global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, uint4* __restrict__ out, long pre_rows,
+                                                            int n_planes) {
+  __shared__ uint4 tile[16][33];
+  constexpr int RW = 4;  // rows per warp
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long r0 = blockIdx.x * 32L;
+  const int cin = a.cin, c0 = blockIdx.y * 128 + 4 * lane;
   const bool affine = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE;
   const bool snake = a.in_mode == IN_ADAIN_SNAKE;
   const bool leaky_on = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_LEAKY_MASK;
-  int bm[R];
+  const bool full = c0 + 3 < cin;
+  int bm[RW];
+  float4 v[RW];
 #pragma unroll
-  for (int m = 0; m < R; m++) {
-    const long g = r0 + 32 * m - PRE_PAD_FRONT;
-    bm[m] = (g >= 0 && g < a.L_in && r0 + 32 * m < pre_rows) ? (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)g))
-                                                             : -1;
-  }
-  float v[R][8];
-#pragma unroll
-  for (int m = 0; m < R; m++) {
-    const long g = r0 + 32 * m - PRE_PAD_FRONT;
-#pragma unroll
-    for (int e = 0; e < 8; e++) v[m][e] = 0.0f;
-    if (g >= 0 && g < a.L_in) {
-      const float* src = a.x + (long)(a.in_up2 ? (g >> 1) : g) * a.ldx;
-      if (vec) {
-        const float4 lo = __ldg(reinterpret_cast<const float4*>(src + cA));
-        const float4 hi = __ldg(reinterpret_cast<const float4*>(src + cA + 32));
-        v[m][0] = lo.x, v[m][1] = lo.y, v[m][2] = lo.z, v[m][3] = lo.w;
-        v[m][4] = hi.x, v[m][5] = hi.y, v[m][6] = hi.z, v[m][7] = hi.w;
+  for (int m = 0; m < RW; m++) {
+    const long r = r0 + warp * RW + m, g = r - PRE_PAD_FRONT;
+    const bool in = g >= 0 && g < a.L_in && r < pre_rows;
+    bm[m] = in ? (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)g)) : -1;
+    v[m] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (in && c0 < cin) {
+      const float* src = a.x + (long)(a.in_up2 ? (g >> 1) : g) * a.ldx + c0;
+      if (full) {
+        v[m] = __ldg(reinterpret_cast<const float4*>(src));
       } else {
-#pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const int c = cA + (e < 4 ? e : 28 + e);
-          if (c < cin) v[m][e] = __ldg(src + c);
-        }
+        v[m].x = __ldg(src);
+        if (c0 + 1 < cin) v[m].y = __ldg(src + 1);
+        if (c0 + 2 < cin) v[m].z = __ldg(src + 2);
       }
     }
   }
-  float al[8], ial[8];
+  float al[4], ial[4];
   if (snake) {
 #pragma unroll
-    for (int e = 0; e < 8; e++) {
-      const int c = cA + (e < 4 ? e : 28 + e);
-      al[e] = c < cin ? __ldg(a.alpha + c) : 1.0f;
+    for (int e = 0; e < 4; e++) {
+      al[e] = c0 + e < cin ? __ldg(a.alpha + c0 + e) : 1.0f;
       ial[e] = 1.0f / al[e];
     }
   }
-  float2 q[8];
+  // plane of lane l's channels within the tile: block l / 16, chunk l % 8, half (l / 8) % 2
+  const int tp = (lane >> 4) * 8 + (lane & 7), th = (lane >> 3) & 1;
+  float2 q[4];
   int cached = -1;
 #pragma unroll
-  for (int m = 0; m < R; m++) {
-    const long rr = r0 + 32 * m;
-    if (rr >= pre_rows) break;
+  for (int m = 0; m < RW; m++) {
     const int b = bm[m];
-    float o8[8];
+    float o[4] = {v[m].x, v[m].y, v[m].z, v[m].w};
     if (b < 0) {
 #pragma unroll
-      for (int e = 0; e < 8; e++) o8[e] = 0.0f;
+      for (int e = 0; e < 4; e++) o[e] = 0.0f;
     } else if (affine) {
       if (b != cached) {
         cached = b;
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-          const int c = cA + (e < 4 ? e : 28 + e);
-          q[e] = c < cin ? __ldg(a.coef + (long)b * cin + c) : make_float2(0.0f, 0.0f);
-        }
+        for (int e = 0; e < 4; e++)
+          q[e] = c0 + e < cin ? __ldg(a.coef + (long)b * cin + c0 + e) : make_float2(0.0f, 0.0f);
       }
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        float t = fmaf(v[m][e], q[e].x, q[e].y);
+      for (int e = 0; e < 4; e++) {
+        float t = fmaf(o[e], q[e].x, q[e].y);
         if (snake) {
           const float sn = __sinf(al[e] * t);
           t = fmaf(ial[e], sn * sn, t);
         } else {
           t = leaky(t, a.slope);
         }
-        o8[e] = t;
+        o[e] = t;
       }
-    } else {
+    } else if (leaky_on) {
 #pragma unroll
-      for (int e = 0; e < 8; e++) o8[e] = leaky_on ? leaky(v[m][e], a.slope) : v[m][e];
+      for (int e = 0; e < 4; e++) o[e] = leaky(o[e], a.slope);
     }
-    uint4 pk;
-    __nv_bfloat162 h0 = __floats2bfloat162_rn(o8[0], o8[1]);
-    __nv_bfloat162 h1 = __floats2bfloat162_rn(o8[2], o8[3]);
-    __nv_bfloat162 h2 = __floats2bfloat162_rn(o8[4], o8[5]);
-    __nv_bfloat162 h3 = __floats2bfloat162_rn(o8[6], o8[7]);
-    memcpy(&pk.x, &h0, 4);
-    memcpy(&pk.y, &h1, 4);
-    memcpy(&pk.z, &h2, 4);
-    memcpy(&pk.w, &h3, 4);
-    out[(long)pl * pre_rows + rr] = pk;
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
+    uint2 u;
+    memcpy(&u.x, &p0, 4);
+    memcpy(&u.y, &p1, 4);
+    reinterpret_cast<uint2*>(&tile[tp][warp * RW + m])[th] = u;
+  }
+  __syncthreads();
+#pragma unroll
+  for (int k = 0; k < 2; k++) {
+    const int p = 2 * warp + k, plane = blockIdx.y * 16 + p;
+    const long r = r0 + lane;
+    if (plane < n_planes && r < pre_rows) out[(long)plane * pre_rows + r] = tile[p][lane];
   }
 }
 
 cudaError_t launch_prologue_bf16(const ConvArgs& a, void* xpre, long pre_rows, cudaStream_t st) {
   const int ncb = (a.cin + TC_KB - 1) / TC_KB;
-  prologue_bf16_kernel<<<dim3((unsigned)((pre_rows + 255) / 256), ncb), 256, 0, st>>>(a, (uint4*)xpre, pre_rows);
+  if (a.ldx % 4 != 0 || (((uintptr_t)a.x) & 15) != 0) return cudaErrorInvalidValue;
+  prologue_bf16_kernel<<<dim3((unsigned)((pre_rows + 31) / 32), (ncb + 1) / 2), 256, 0, st>>>(a, (uint4*)xpre,
+                                                                                             pre_rows, ncb * 8);
   return cudaGetLastError();
 }
 
