@@ -10,8 +10,9 @@
 //    its shared-memory operand (LBO 2048 B between 8-channel chunks, SBO 128 B between 8-row
 //    groups), streamed with one cp.async.bulk per block into a 3-stage ring;
 //  * input rows: a loader warp streams the f32 rows of each tile's window
-//    [t0 - pad, t0 + 256 + (K-1)*dil - pad) with TMA tensor loads (boxes of 32 rows x 64 channels,
-//    8 KB; rows and channels outside the tensor read as zero) into a ring of up to 6 stages, so
+//    [t0 - pad, t0 + 256 + (K-1)*dil - pad) with TMA tensor loads (boxes of 64 channels x 32 rows,
+//    8 KB, or 64 rows, 16 KB, for layers without a residual read; rows and channels outside the
+//    tensor read as zero) into a ring of up to 6 stages, so
 //    HBM latency is covered by the ring depth rather than by registers;
 //  * activations: 4 producer warps read the boxes from shared memory, apply the layer's prologue
 //    (gap masking, AdaIN + leaky ReLU, AdaIN + Snake, leaky ReLU, nearest x2 upsample) and store
@@ -52,8 +53,13 @@ constexpr int TC_KB = 64;
 constexpr int TC_WST = 3;                        // weight ring stages
 constexpr int TC_XST_MAX = 4;                    // activation-window stages (2 on the fused route)
 constexpr int TC_RST_MAX = 6;                    // input-box ring stages (fewer when shared memory is short)
-constexpr int TC_BOX_ROWS = 32;
-constexpr int TC_INBOX = TC_BOX_ROWS * TC_KB * 4;  // 8 KB f32 input box
+constexpr int TC_BOX_ROWS = 32;                  // input box rows (64 for stores without a residual read)
+// Input box rows of an instance: 64 (16 KB boxes, each producer thread converts two rows per box
+// wait) when the epilogue reads no residual; 32 otherwise, where the residual buffers leave room
+// for a deeper ring of smaller boxes only.
+__host__ __device__ constexpr int tc_box_rows(int im, int om) {
+  return (im >= 0 && im != IN_PRE && (om == OUT_STORE || om == OUT_GELU)) ? 64 : TC_BOX_ROWS;
+}
 constexpr int TC_MAX_WIN = 512;
 constexpr int TC_EC = 16;                        // epilogue chunk: 16 time rows x 32 channels per warp
 constexpr int TC_RES_DEPTH = 2;                  // residual chunks in flight per epilogue warp
@@ -108,13 +114,13 @@ enum TcTrace : int {
 struct InSpan {
   int base, xr0, nbox;
 };
-__device__ __forceinline__ InSpan in_span(const TcArgs& p, int tile, int up2) {
+__device__ __forceinline__ InSpan in_span(const TcArgs& p, int tile, int up2, int box_rows) {
   InSpan s;
   s.base = (tile / p.n_cot) * TC_N - p.a.pad;
   const int last = s.base + p.win_rows - 1;
   s.xr0 = up2 ? (s.base >> 1) : s.base;
   const int xr1 = up2 ? (last >> 1) : last;
-  s.nbox = (xr1 - s.xr0) / TC_BOX_ROWS + 1;
+  s.nbox = (xr1 - s.xr0) / box_rows + 1;
   return s;
 }
 
@@ -130,11 +136,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   const int out_mode_k = IM >= 0 ? OM : a.out_mode;
   const uint32_t xbytes = 8u * p.win_pad * 16u;
   const int RST = p.rst;
+  constexpr int BOXR = tc_box_rows(IM, OM);
+  constexpr uint32_t INBOX = BOXR * TC_KB * 4;
   uint8_t* wbuf = smem;                                       // TC_WST x 16 KB
   const int XST = p.xst;
   uint8_t* xbuf = wbuf + TC_WST * TC_WBLOCK;                  // XST x xbytes
   uint8_t* inring = xbuf + XST * xbytes;                      // RST x 8 KB
-  uint8_t* epi = inring + RST * TC_INBOX;                     // TC_NEPI x p.epb
+  uint8_t* epi = inring + RST * INBOX;                        // TC_NEPI x p.epb
   uint64_t* bars = (uint64_t*)(epi + TC_NEPI * p.epb);
   uint64_t* w_full = bars;
   uint64_t* w_empty = w_full + TC_WST;
@@ -319,15 +327,15 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       uint32_t ph = 0;  // ring slot and phase parity of box `it`
       bool ok = true;
       for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x) {
-        const InSpan sp = in_span(p, tile, in_up2);
+        const InSpan sp = in_span(p, tile, in_up2, BOXR);
         for (int cb = 0; cb < p.ncb && ok; cb++)
           for (int i = 0; i < sp.nbox; i++, it++) {
             if (!mbar_wait_t(&in_empty[sl], ph ^ 1, abort_flag, p.err, tr)) {
               ok = false;
               break;
             }
-            mbar_arrive_expect_tx(&in_full[sl], TC_INBOX);
-            tma_load_2d(inring + sl * TC_INBOX, &p.xmap, cb * TC_KB, sp.xr0 + i * TC_BOX_ROWS, &in_full[sl]);
+            mbar_arrive_expect_tx(&in_full[sl], INBOX);
+            tma_load_2d(inring + sl * INBOX, &p.xmap, cb * TC_KB, sp.xr0 + i * BOXR, &in_full[sl]);
             if (++sl == RST) sl = 0, ph ^= 1;
           }
       }
@@ -369,7 +377,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
       const int bf = lt & 1;
       if (!mbar_wait(&meta_empty[bf], ((lt >> 1) & 1) ^ 1, abort_flag, p.err)) break;
-      const InSpan sp = in_span(p, tile, in_up2);
+      const InSpan sp = in_span(p, tile, in_up2, BOXR);
       int* ri = ritem + bf * TC_MAX_WIN;
       int iv[TC_MAX_WIN / 32];
 #pragma unroll
@@ -607,7 +615,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     bool ok = true;
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < ntiles && ok; tile += gridDim.x, lt++) {
-      const InSpan sp = in_span(p, tile, in_up2);
+      const InSpan sp = in_span(p, tile, in_up2, BOXR);
       const int bf = lt & 1;
       if (!mbar_wait_t(&meta_full[bf], (lt >> 1) & 1, abort_flag, p.err, trc ? &tpw : nullptr)) break;
       const int* ri = ritem + bf * TC_MAX_WIN;
@@ -719,18 +727,18 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             break;
           }
           if (++in_sl == RST) in_sl = 0, in_ph ^= 1;
-          const float* box = (const float*)(inring + sl * TC_INBOX);
+          const float* box = (const float*)(inring + sl * INBOX);
 #pragma unroll
-          for (int hh = 0; hh < TC_BOX_ROWS / TC_PROWS; hh++) {
+          for (int hh = 0; hh < BOXR / TC_PROWS; hh++) {
             const int br = prow + TC_PROWS * hh;
             const float4 lo = *reinterpret_cast<const float4*>(box + br * TC_KB + 4 * j);
             const float4 hi = *reinterpret_cast<const float4*>(box + br * TC_KB + 32 + 4 * j);
             const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
             if (!up2) {
-              const int r = i * TC_BOX_ROWS + br;
+              const int r = i * BOXR + br;
               if (r < win_rows) emit(r, v);
             } else {
-              const int r0 = 2 * (sp.xr0 + i * TC_BOX_ROWS + br) - sp.base;
+              const int r0 = 2 * (sp.xr0 + i * BOXR + br) - sp.base;
               if (r0 >= 0 && r0 < win_rows) emit(r0, v);
               if (r0 + 1 >= 0 && r0 + 1 < win_rows) emit(r0 + 1, v);
             }
@@ -922,53 +930,6 @@ cudaError_t tc_make_weights(const float* w, int cin, int cout, int K, TcWeights*
   return cudaSuccess;
 }
 
-// Shared memory of one CTA: weight ring, activation windows, input-box ring, epilogue buffers
-// (epb bytes per warp), mbarriers (+ TMEM slot, abort flag, table items), the double-buffered
-// row-item table and, with tab, the coefficient and alpha tables.
-static size_t tc_smem(int win_pad, int rst, int xst, int epb, bool tab) {
-  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + (size_t)rst * TC_INBOX +
-         (size_t)TC_NEPI * epb + (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST_MAX + 4 + TC_NEPI * TC_RES_DEPTH + 4) * 8 +
-         16 + 2 * TC_MAX_WIN * 4 + (tab ? 3 * TC_TAB * 8 : 0);
-}
-
-static inline int win_pad_of(int K, int dil) { return ((TC_N + (K - 1) * dil + 7) / 8) * 8 + 1; }
-
-// Input-box ring depth that fits next to the other buffers (0 when even 2 stages do not fit).
-static int ring_stages(int win_pad, int epb, bool tab) {
-  for (int r = TC_RST_MAX; r >= 2; r--)
-    if (tc_smem(win_pad, r, 2, epb, tab) <= (size_t)TC_SMEM_MAX) return r;
-  return 0;
-}
-
-static int epb_of(const ConvArgs& a) { return tc_epi_warp_bytes(a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS); }
-
-// The shared-memory coefficient tables serve affine prologues of up to TC_TAB input channels.
-static bool tab_of(const ConvArgs& a, int cin_pad) {
-  return (a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && cin_pad <= TC_TAB;
-}
-
-static bool rows_ok(const void* base, long ld) { return base && ld % 4 == 0 && (((uintptr_t)base) & 15) == 0; }
-
-bool tc_supported(const ConvArgs& a, const TcWeights& t) {
-  if (a.stride != 1 || a.K != t.K || a.cin != t.cin || a.cout != t.cout) return false;
-  if (a.L_out < 64) return false;  // tiny row counts (per-item style projections) stay on SIMT
-  if ((a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && !a.coef) return false;
-  if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
-  if (ring_stages(win_pad_of(a.K, a.dil), epb_of(a), tab_of(a, t.cin_pad)) == 0) return false;
-  // every global operand moves by TMA: 16-byte aligned bases and row strides
-  if (a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) return false;
-  if (a.out_mode == OUT_GELU_PRE) {
-    if (!a.ypre || (((uintptr_t)a.ypre) & 15) != 0 || a.cout % TC_KB != 0 || a.stat) return false;
-  } else if (!rows_ok(a.y, a.ldy)) {
-    return false;
-  }
-  if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
-  return true;
-}
-
-static int g_num_sms[64] = {0};
-static unsigned g_attr_set[64] = {0};  // per device: instances whose shared-memory limit is raised
-
 typedef void (*TcKernelFn)(const TcArgs);
 // Instances for the (input mode, x2 upsample, output mode) combinations the model uses; any other
 // combination runs the generic instance.
@@ -1004,6 +965,61 @@ static TcKernelFn pick_kernel(int im, int up, int om, int* idx) {
   *idx = n;
   return tc_conv_kernel<-1, 0, -1>;
 }
+
+// Input box rows of the instance that runs a layer (the generic instance uses 32).
+static int box_rows_of(const ConvArgs& a) {
+  const bool pre = a.in_mode == IN_PRE;
+  int idx = 0;
+  const TcKernelFn fn = pick_kernel(a.in_mode, pre ? 0 : a.in_up2, a.out_mode, &idx);
+  return fn == tc_conv_kernel<-1, 0, -1> ? TC_BOX_ROWS : tc_box_rows(a.in_mode, a.out_mode);
+}
+
+// Shared memory of one CTA: weight ring, activation windows, input-box ring, epilogue buffers
+// (epb bytes per warp), mbarriers (+ TMEM slot, abort flag, table items), the double-buffered
+// row-item table and, with tab, the coefficient and alpha tables.
+static size_t tc_smem(int win_pad, int rst, int box_rows, int xst, int epb, bool tab) {
+  return (size_t)TC_WST * TC_WBLOCK + (size_t)xst * 8 * win_pad * 16 + (size_t)rst * box_rows * TC_KB * 4 +
+         (size_t)TC_NEPI * epb + (2 * TC_WST + 2 * TC_RST_MAX + 2 * TC_XST_MAX + 4 + TC_NEPI * TC_RES_DEPTH + 4) * 8 +
+         16 + 2 * TC_MAX_WIN * 4 + (tab ? 3 * TC_TAB * 8 : 0);
+}
+
+static inline int win_pad_of(int K, int dil) { return ((TC_N + (K - 1) * dil + 7) / 8) * 8 + 1; }
+
+// Input-box ring depth that fits next to the other buffers (0 when even 2 stages do not fit).
+static int ring_stages(int win_pad, int box_rows, int epb, bool tab) {
+  for (int r = TC_RST_MAX; r >= 2; r--)
+    if (tc_smem(win_pad, r, box_rows, 2, epb, tab) <= (size_t)TC_SMEM_MAX) return r;
+  return 0;
+}
+
+static int epb_of(const ConvArgs& a) { return tc_epi_warp_bytes(a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS); }
+
+// The shared-memory coefficient tables serve affine prologues of up to TC_TAB input channels.
+static bool tab_of(const ConvArgs& a, int cin_pad) {
+  return (a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && cin_pad <= TC_TAB;
+}
+
+static bool rows_ok(const void* base, long ld) { return base && ld % 4 == 0 && (((uintptr_t)base) & 15) == 0; }
+
+bool tc_supported(const ConvArgs& a, const TcWeights& t) {
+  if (a.stride != 1 || a.K != t.K || a.cin != t.cin || a.cout != t.cout) return false;
+  if (a.L_out < 64) return false;  // tiny row counts (per-item style projections) stay on SIMT
+  if ((a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && !a.coef) return false;
+  if (TC_N + (a.K - 1) * a.dil > TC_MAX_WIN) return false;
+  if (ring_stages(win_pad_of(a.K, a.dil), box_rows_of(a), epb_of(a), tab_of(a, t.cin_pad)) == 0) return false;
+  // every global operand moves by TMA: 16-byte aligned bases and row strides
+  if (a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) return false;
+  if (a.out_mode == OUT_GELU_PRE) {
+    if (!a.ypre || (((uintptr_t)a.ypre) & 15) != 0 || a.cout % TC_KB != 0 || a.stat) return false;
+  } else if (!rows_ok(a.y, a.ldy)) {
+    return false;
+  }
+  if (a.out_mode == OUT_PLUS && !rows_ok(a.sc, a.ldsc)) return false;
+  return true;
+}
+
+static int g_num_sms[64] = {0};
+static unsigned g_attr_set[64] = {0};  // per device: instances whose shared-memory limit is raised
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -1048,7 +1064,8 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   const long x_rows = a.in_up2 ? (a.L_in + 1) / 2 : a.L_in;
   const bool pre = a.in_mode == IN_PRE;
   if (pre && (!a.xpre || (((uintptr_t)a.xpre) & 15) != 0)) return cudaErrorInvalidValue;
-  bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, TC_BOX_ROWS)) &&
+  const int box_rows = box_rows_of(a);
+  bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, box_rows)) &&
               (a.out_mode == OUT_GELU_PRE || make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC));
   if (maps && a.out_mode == OUT_ADD) maps = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
   if (maps && a.out_mode == OUT_PLUS) maps = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc, 32, TC_EC);
@@ -1063,11 +1080,12 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   p.err = err;
   p.epb = epb_of(a);
   p.tab = !pre && tab_of(a, t.cin_pad);
-  p.rst = pre ? 0 : ring_stages(p.win_pad, p.epb, p.tab);
+  p.rst = pre ? 0 : ring_stages(p.win_pad, box_rows, p.epb, p.tab);
   p.xst = 2;
   if (pre)  // no input ring: spend its shared memory on deeper window staging
-    while (p.xst < TC_XST_MAX && tc_smem(p.win_pad, 0, p.xst + 1, p.epb, false) <= (size_t)TC_SMEM_MAX) p.xst++;
-  const size_t smem = tc_smem(p.win_pad, p.rst, p.xst, p.epb, p.tab);
+    while (p.xst < TC_XST_MAX && tc_smem(p.win_pad, 0, box_rows, p.xst + 1, p.epb, false) <= (size_t)TC_SMEM_MAX)
+      p.xst++;
+  const size_t smem = tc_smem(p.win_pad, p.rst, box_rows, p.xst, p.epb, p.tab);
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && g_num_sms[dev] == 0) {
