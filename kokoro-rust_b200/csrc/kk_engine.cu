@@ -877,6 +877,7 @@ void Engine::stats(const float* x, int ldx, int C, const Dom& d, const ItemTab* 
   double* part = ar.get<double>((size_t)2 * B * C);
   check(launch_stats(x, ldx, C, items, B, d.scale == 0 ? 1 : d.scale, d.plus1, max_len, part, *mean, *rstd, st),
         "stats");
+  launches++;  // partial sums + finalisation: two kernels
 }
 
 void Engine::adain_args(ConvArgs& a, const AdaIN& n, const float* mean, const float* rstd, const float* gb, int ldgb,
@@ -1367,11 +1368,12 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       }
       cudaEvent_t e0;
       prof_begin(&e0);
-      if (attn_tc)
+      if (attn_tc) {
         check(launch_attention_tc(qkv, 2304, items_d, work_d, n_work, ctx, 768, err_flag, st, planes ? ctxpre : nullptr,
                                   pre_rows),
               "attention(tcgen05)");
-      else
+        launches += (n_work[0] > 0) + (n_work[1] > 0) + (n_work[2] > 0) - 1;  // one kernel per non-empty bucket
+      } else
         check(launch_attention_f32(qkv, 2304, items_d, B, max_t, ctx, 768, st), "attention");
       double af = 0;
       for (int b = 0; b < B; b++) af += 4.0 * 12 * 64 * (double)ids_len[b] * ids_len[b];
