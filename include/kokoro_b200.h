@@ -58,7 +58,8 @@ typedef struct kk_engine kk_engine;
 
 /*
  * kk_create -- load a safetensors checkpoint (the reference's layout: raw state-dict names,
- * weight_norm as weight_v/weight_g, AdaIN affine optional) onto CUDA device `cuda_ordinal`.
+ * weight_norm as weight_v/weight_g, AdaIN affine optional), or the PyTorch checkpoint itself when
+ * the path ends in .pth (see kk_pth_open), onto CUDA device `cuda_ordinal`.
  * Replaces Gpu::new (src/gpu.rs:81) + Weights::load (src/weights.rs:14) +
  * Kokoro::from_weights (src/model.rs:122) + GpuKokoro::with_gpu (src/gpu.rs:685).
  */
@@ -135,6 +136,30 @@ KK_API kk_status kk_wav_assemble(int n_parts, const char* const* part_paths, con
 KK_API kk_status kk_sha256_hex(const uint8_t* data, int64_t n, char out[65]);
 /* Message of the last WAV-function failure on this thread. */
 KK_API const char* kk_wav_error(void);
+
+/*
+ * PyTorch zip checkpoints (src/torchpt.rs): kokoro-v1_0.pth, a dict of state dicts, read as flat
+ * "submodule.param" f32 tensors (a leading "module." dropped), and voice packs voices/<name>.pt, one
+ * [rows, 1, 256] tensor. Deliberately restricted like the reference: STORED zip entries only, a small
+ * pickle opcode set that is interpreted and never executed, and only the globals
+ * collections.OrderedDict, torch._utils._rebuild_tensor_v2 and torch.FloatStorage; anything else
+ * fails with KK_ERR_IO and a message naming it. kk_create also accepts a .pth checkpoint directly.
+ */
+typedef struct kk_pth kk_pth;
+typedef enum { KK_PTH_CHECKPOINT = 0, KK_PTH_VOICE = 1 } kk_pth_kind;
+/* Load a checkpoint (load_kmodel_checkpoint, src/torchpt.rs:302-319) or a voice pack
+   (load_voice_pack, :322-335) into host memory. */
+KK_API kk_status kk_pth_open(const char* path, int kind, kk_pth** out);
+/* Tensors held (1 for a voice pack), in name order. */
+KK_API int kk_pth_count(const kk_pth* p);
+KK_API const char* kk_pth_name(const kk_pth* p, int i);
+/* Rank of tensor i (-1 if out of range); its first min(rank, cap) extents go to dims. */
+KK_API int kk_pth_shape(const kk_pth* p, int i, int64_t* dims, int cap);
+/* Contiguous row-major f32 data of tensor i, valid until kk_pth_close. */
+KK_API const float* kk_pth_data(const kk_pth* p, int i);
+KK_API void kk_pth_close(kk_pth* p);
+/* Message of the last kk_pth_open failure on this thread. */
+KK_API const char* kk_pth_error(void);
 
 /*
  * kk_decode_batch -- decoder + iSTFTNet generator only (the reference's

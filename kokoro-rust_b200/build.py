@@ -8,7 +8,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libkokoro_b200.so")
-SOURCES = ["kk_engine.cu", "kk_conv_simt.cu", "kk_kernels.cu", "kk_lstm.cu", "kk_tc.cu", "kk_attn_tc.cu", "kk_selftest.cu", "kk_weights.cpp", "kk_wav.cpp"]
+SOURCES = ["kk_engine.cu", "kk_conv_simt.cu", "kk_kernels.cu", "kk_lstm.cu", "kk_tc.cu", "kk_attn_tc.cu", "kk_selftest.cu", "kk_weights.cpp", "kk_wav.cpp", "kk_pth.cpp"]
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 COMPILE = [
     "-gencode", "arch=compute_100a,code=sm_100a",

@@ -1,5 +1,6 @@
 // Minimal safetensors reader and weight-resolution rules (see kk_weights.h).
 #include "kk_weights.h"
+#include "kk_pth.h"
 
 #include <cmath>
 #include <cstdio>
@@ -124,6 +125,10 @@ std::string shape_str(const std::vector<int64_t>& s) {
 }  // namespace
 
 Checkpoint::Checkpoint(const std::string& path) {
+  if (path.size() >= 4 && path.compare(path.size() - 4, 4, ".pth") == 0) {  // torch.save zip (kk_pth.cpp)
+    for (auto& kv : load_pth_checkpoint(path)) map_[kv.first] = std::move(kv.second);
+    return;
+  }
   std::ifstream f(path, std::ios::binary);
   if (!f) throw KKError(5, "cannot open weights file " + path);
   f.seekg(0, std::ios::end);

@@ -65,6 +65,13 @@ _SIGS = {
     "kk_sha256_hex": (ctypes.c_int, [_P, ctypes.c_int64, ctypes.c_char_p]),
     "kk_wav_error": (ctypes.c_char_p, []),
     "kk_memory_stats": (ctypes.c_int, [_P, _P]),
+    "kk_pth_open": (ctypes.c_int, [ctypes.c_char_p, ctypes.c_int, ctypes.POINTER(_P)]),
+    "kk_pth_count": (ctypes.c_int, [_P]),
+    "kk_pth_name": (ctypes.c_char_p, [_P, ctypes.c_int]),
+    "kk_pth_shape": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int]),
+    "kk_pth_data": (ctypes.c_void_p, [_P, ctypes.c_int]),
+    "kk_pth_close": (None, [_P]),
+    "kk_pth_error": (ctypes.c_char_p, []),
     "kk_device_memory": (ctypes.c_int, [ctypes.c_int, _P, _P]),
 }
 
@@ -460,6 +467,7 @@ class Voice:
     """Voice pack [rows, 256]; ref_s = pack[n_phoneme_chars - 1] (src/engine.rs:46-60)."""
 
     pack: np.ndarray
+    sha256: str = ""  # of the .pt file(s) it came from, comma-joined (provenance)
 
     def ref_s(self, n_chars: int) -> np.ndarray:
         if n_chars < 1:
@@ -482,8 +490,12 @@ class Engine:
     The text frontend is out of scope: a request is a sequence of phoneme token ids (without the
     boundary pads, which ``synth_batch`` adds as the reference's ``phonemes_to_ids`` does)."""
 
-    def __init__(self, weights_path: str, cuda_ordinal: int = 0, precision: str = "fp32"):
+    def __init__(self, weights_path: str, cuda_ordinal: int = 0, precision: str = "fp32",
+                 model_dir: Optional[str] = None):
+        """weights_path: a safetensors file or the PyTorch checkpoint (.pth) itself; model_dir
+        holds voices/<name>.pt (src/engine.rs:80-112)."""
         self.gpu = GpuKokoro(weights_path, cuda_ordinal, precision)
+        self.model_dir = model_dir if model_dir is not None else os.path.dirname(os.path.abspath(weights_path))
         self.voices = {}
 
     def identity(self) -> str:
@@ -492,14 +504,25 @@ class Engine:
     def add_voice(self, name: str, pack: np.ndarray):
         self.voices[name] = Voice(np.asarray(pack, np.float32).reshape(-1, 256))
 
+    def _load_voice_part(self, part: str) -> Voice:
+        if part in self.voices:
+            return self.voices[part]
+        from . import pth, wav
+        path = part if part.endswith(".pt") else os.path.join(self.model_dir, "voices", part + ".pt")
+        pack = pth.load_voice_pack(path)
+        with open(path, "rb") as f:
+            digest = wav.sha256_hex(f.read())
+        return Voice(pack.reshape(pack.shape[0], 256), digest)
+
     def voice(self, spec: str) -> Voice:
-        """Voice by name, or comma-separated mean of several (src/engine.rs:115-137)."""
+        """Voice by name (an added pack, or voices/<name>.pt under model_dir), explicit .pt path, or
+        comma-separated element-wise mean of several (src/engine.rs:115-137)."""
         if spec not in self.voices:
-            parts = spec.split(",")
-            packs = [self.voices[p].pack for p in parts]
-            if any(p.shape != packs[0].shape for p in packs):
+            vs = [self._load_voice_part(p) for p in spec.split(",")]
+            if any(v.pack.shape != vs[0].pack.shape for v in vs):
                 raise ValueError("voice packs have different shapes")
-            self.voices[spec] = Voice(np.mean(np.stack(packs), axis=0).astype(np.float32))
+            pack = vs[0].pack if len(vs) == 1 else np.mean(np.stack([v.pack for v in vs]), axis=0).astype(np.float32)
+            self.voices[spec] = Voice(pack, ",".join(v.sha256 for v in vs))
         return self.voices[spec]
 
     def synth_batch(self, reqs: Sequence[tuple], voice: str, speed: float = 1.0,
