@@ -15,6 +15,7 @@ cannot be loaded, ``load_library`` raises.
 from __future__ import annotations
 
 import ctypes
+import json
 import os
 from dataclasses import dataclass, field
 from typing import List, Optional, Sequence
@@ -485,18 +486,41 @@ class Synth:
 
 
 class Engine:
-    """Resident synthesis engine (src/engine.rs:62-241) over token-id requests.
+    """Resident synthesis engine (src/engine.rs:62-241).
 
-    The text frontend is out of scope: a request is a sequence of phoneme token ids (without the
-    boundary pads, which ``synth_batch`` adds as the reference's ``phonemes_to_ids`` does)."""
+    The text frontend is out of scope: a request is a phoneme string (mapped to token ids with the
+    model's vocabulary, config.json, as the reference's ``phonemes_to_ids``) or a sequence of
+    phoneme token ids (without the boundary pads, which ``synth_batch`` adds)."""
 
     def __init__(self, weights_path: str, cuda_ordinal: int = 0, precision: str = "fp32",
                  model_dir: Optional[str] = None):
         """weights_path: a safetensors file or the PyTorch checkpoint (.pth) itself; model_dir
-        holds voices/<name>.pt (src/engine.rs:80-112)."""
+        holds config.json and voices/<name>.pt (src/engine.rs:80-112)."""
+        from . import wav
         self.gpu = GpuKokoro(weights_path, cuda_ordinal, precision)
         self.model_dir = model_dir if model_dir is not None else os.path.dirname(os.path.abspath(weights_path))
         self.voices = {}
+        with open(weights_path, "rb") as f:
+            self.model_sha256 = wav.sha256_hex(f.read())
+        self.vocab, self.config_sha256 = {}, ""
+        cfg = os.path.join(self.model_dir, "config.json")
+        if os.path.exists(cfg):
+            with open(cfg, "rb") as f:
+                raw = f.read()
+            self.config_sha256 = wav.sha256_hex(raw)
+            self.vocab = {k: int(v) for k, v in json.loads(raw.decode("utf-8")).get("vocab", {}).items()}
+
+    def phonemes_to_ids(self, ps: str) -> tuple:
+        """[0] + vocab ids of the characters + [0]; characters outside the vocabulary are dropped
+        and returned (src/model.rs:146-157)."""
+        ids, dropped = [0], []
+        for c in ps:
+            if c in self.vocab:
+                ids.append(self.vocab[c])
+            else:
+                dropped.append(c)
+        ids.append(0)
+        return np.asarray(ids, np.int64), dropped
 
     def identity(self) -> str:
         return self.gpu.identity
@@ -527,8 +551,9 @@ class Engine:
 
     def synth_batch(self, reqs: Sequence[tuple], voice: str, speed: float = 1.0,
                     policy: BatchPolicy = BatchPolicy()) -> list:
-        """reqs: [(token ids without pads, seed)]. Returns per request a Synth or an Exception,
-        in input order; a failing batch is split in half down to single items."""
+        """reqs: [(phoneme string or token ids without pads, seed)]. Returns per request a Synth
+        or an Exception, in input order; a failing batch is split in half down to single items.
+        The length rules count phoneme characters (dropped ones included), as the reference does."""
         results: list = [None] * len(reqs)
         prepared = []
         for i, (toks, _seed) in enumerate(reqs):
@@ -538,8 +563,11 @@ class Engine:
                     raise ValueError("empty phoneme string")
                 if n > MAX_PHONEMES:
                     raise ValueError(f"oversize: {n} phoneme chars > {MAX_PHONEMES}")
-                ids = np.concatenate([[0], np.asarray(toks, np.int64), [0]])
-                prepared.append((i, ids, self.voice(voice).ref_s(n)))
+                if isinstance(toks, str):
+                    ids, dropped = self.phonemes_to_ids(toks)
+                else:
+                    ids, dropped = np.concatenate([[0], np.asarray(toks, np.int64), [0]]), []
+                prepared.append((i, ids, self.voice(voice).ref_s(n), dropped))
             except Exception as e:  # per-chunk validation error (src/engine.rs:194-211)
                 results[i] = e
         lens = [len(p[1]) for p in prepared]
@@ -551,7 +579,7 @@ class Engine:
             try:
                 outs = self.gpu.forward_batch(items)
                 for k, o in zip(batch, outs):
-                    results[prepared[k][0]] = Synth(o.audio, o.pred_dur, [])
+                    results[prepared[k][0]] = Synth(o.audio, o.pred_dur, prepared[k][3])
             except KokoroError as e:
                 if len(batch) > 1:
                     mid = len(batch) // 2
