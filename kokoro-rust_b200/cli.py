@@ -482,7 +482,7 @@ def main(argv=None) -> int:
         return 2
     try:
         return synth(args)
-    except (JobError, OSError) as e:
+    except Exception as e:  # noqa: BLE001 - anything escaping the pipeline is a job-level error
         print(f"error: {e}", file=sys.stderr)
         return 2
 

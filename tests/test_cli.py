@@ -159,3 +159,13 @@ def test_cli_end_to_end_on_gpu(kk, ckpt_path, tmp_path):
     assert m["output"]["samples"] == total > 0
     assert cli.synth(args) == 0  # second run: everything resumed
     assert json.loads((out / "lines.manifest.json").read_text())["counts"]["resumed"] == 3
+
+
+def test_job_level_errors_exit_2(kk, tmp_path):
+    """Failures outside a line (unreadable input, a model directory without a checkpoint) end the
+    job with status 2."""
+    from kokoro_rust_b200 import cli
+    assert cli.main(["synth", str(tmp_path / "missing.txt"), "--model-dir", str(tmp_path)]) == 2
+    inp = tmp_path / "l.txt"
+    inp.write_text("abc\n", encoding="utf-8")
+    assert cli.main(["synth", str(inp), "--model-dir", str(tmp_path), "--out-dir", str(tmp_path / "o")]) == 2
