@@ -503,8 +503,60 @@ __global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, cons
   y[(long)o * ldy + c] = acc;
 }
 
+// The same AdaIN + leaky + depthwise transposed conv for the AdaIN-leaky prologue, organised by
+// input row: thread = channel, block = 32 consecutive input rows. Each input value is transformed
+// once (instead of once per output that reads it) and feeds output rows 2i (tap 1), 2i - 1 (tap 0)
+// and 2i + 1 (tap 2); the item's AdaIN terms stay in registers while the item is unchanged. The
+// arithmetic of every output is the one above, operation for operation.
+constexpr int POOL_RB = 32;
+__global__ void __launch_bounds__(256) adain_pool_rows_kernel(const float* __restrict__ x, int C, int L, ConvArgs p,
+                                                              const float* __restrict__ pw,
+                                                              const float* __restrict__ pb, float* __restrict__ y,
+                                                              int ldy) {
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= C) return;
+  const int i0 = blockIdx.x * POOL_RB;
+  const float w0 = pw[c * 3 + 0], w1 = pw[c * 3 + 1], w2 = pw[c * 3 + 2], bias = pb[c];
+  const float nw = p.nw[c], nb = p.nb[c];
+  int cached = -1;
+  float mean = 0.0f, rstd = 0.0f, g1 = 0.0f, gc = 0.0f;
+  auto u_of = [&](int i) -> float {  // pool_in(p, x, L, i, c)
+    if (i < 0 || i >= L) return 0.0f;
+    const int b = dom_item(p.din, i);
+    if (b < 0) return 0.0f;
+    if (b != cached) {
+      cached = b;
+      mean = p.mean[b * C + c];
+      rstd = p.rstd[b * C + c];
+      const float* g = p.gb + (long)b * p.ldgb;
+      g1 = 1.0f + g[c];
+      gc = g[C + c];
+    }
+    float v = x[(long)i * p.ldx + c];
+    v = (v - mean) * rstd;
+    v = g1 * (v * nw + nb) + gc;
+    return leaky(v, p.slope);
+  };
+  float uc = u_of(i0);
+  for (int k = 0; k < POOL_RB; k++) {
+    const int i = i0 + k;
+    if (i >= L) break;
+    const float un = u_of(i + 1);
+    y[(long)(2 * i) * ldy + c] = fmaf(w1, uc, bias);
+    float acc = fmaf(w2, uc, bias);
+    acc = fmaf(w0, un, acc);
+    y[(long)(2 * i + 1) * ldy + c] = acc;
+    uc = un;
+  }
+}
+
 cudaError_t launch_adain_pool(const float* x, int C, int L, const ConvArgs& pro, const float* pw, const float* pb,
                               float* y, int ldy, cudaStream_t st) {
+  if (pro.in_mode == IN_ADAIN_LEAKY) {
+    adain_pool_rows_kernel<<<dim3((unsigned)((L + POOL_RB - 1) / POOL_RB), (unsigned)((C + 255) / 256)), 256, 0, st>>>(
+        x, C, L, pro, pw, pb, y, ldy);
+    return cudaGetLastError();
+  }
   long n = 2L * L * C;
   adain_pool_kernel<<<nblk(n, 256), 256, 0, st>>>(x, C, L, pro, pw, pb, y, ldy);
   return cudaGetLastError();
