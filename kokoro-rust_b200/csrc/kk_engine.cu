@@ -1076,19 +1076,22 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L20 * 256);
     float* xsr = ar.get<float>((size_t)L20 * 256);
+    // statistics of the noise-conv output (the first AdaIN of noise_res) from the conv's epilogue
+    float *xm, *xr;
+    const int len20 = max_n * d20.scale + d20.plus1;
     if (m.noise0_rows.w) {
       // gap rows of the spectrum are zero (stft), so the 6-frame-row view needs no masking
       ConvArgs a = ca(m.noise0_rows);
       a.x = spec_pad, a.ldx = 6 * SPEC_LD, a.in_mode = IN_NOMASK, a.L_in = L20 + 1, a.y = xs, a.ldy = 256,
       a.L_out = L20;
-      run_conv(m.noise0_rows, a);
+      run_conv_stats(m.noise0_rows, a, d20, items, B, len20, &xm, &xr);
     } else {
       ConvArgs a = ca(m.noise0);
       a.x = spec, a.ldx = SPEC_LD, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 256,
       a.L_out = L20;
-      run_conv(m.noise0, a);
+      run_conv_stats(m.noise0, a, d20, items, B, len20, &xm, &xr);
     }
-    snake(m.noise_res[0], xs, xsr, d20, gb_dec, ldgb, items, B, max_n);
+    snake(m.noise_res[0], xs, xsr, d20, gb_dec, ldgb, items, B, max_n, xm, xr);
     ConvArgs u = ca(m.ups[0]);
     u.x = xd, u.ldx = 512, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d2, u.L_in = L2;
     u.y = y0, u.ldy = 2560, u.L_out = L2, u.out_mode = OUT_PLUS, u.sc = xsr, u.ldsc = 2560;
@@ -1120,8 +1123,9 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     ConvArgs a = ca(m.noise1);
     a.x = spec, a.ldx = SPEC_LD, a.in_mode = IN_MASK, a.din = d120, a.L_in = L120, a.y = xs, a.ldy = 128,
     a.L_out = L120;
-    run_conv(m.noise1, a);
-    snake(m.noise_res[1], xs, xsr, d120, gb_dec, ldgb, items, B, max_n);
+    float *xm, *xr;  // statistics of the noise-conv output from the conv's epilogue
+    run_conv_stats(m.noise1, a, d120, items, B, max_n * d120.scale + d120.plus1, &xm, &xr);
+    snake(m.noise_res[1], xs, xsr, d120, gb_dec, ldgb, items, B, max_n, xm, xr);
     float* u1 = xs;  // noise-conv output no longer needed
     ConvArgs u = ca(m.ups[1]);
     u.x = x1, u.ldx = 256, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d20, u.L_in = L20;
