@@ -17,6 +17,7 @@ and AdaIN parameters; relative L2 difference of the outputs, both with bf16 oper
 
 Run on a GPU box from the repository root:
     python oracle/time_ref_conv.py --out gpurun_out/ref_conv.json
+    python oracle/time_ref_conv.py --single 3     # one launch of this engine's conv, for ncu
 """
 import argparse
 import ctypes
@@ -157,8 +158,21 @@ def main():
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--out", default=None)
+    ap.add_argument("--single", type=int, default=0, metavar="K",
+                    help="only one launch of this engine's conv (128 channels, dilation 1, y = conv) on "
+                         "8 items of 48,000 rows: the small case for an ncu capture")
     args = ap.parse_args()
     rng = np.random.default_rng(7)
+    if args.single:
+        C, K = 128, args.single
+        items = item_table(8, 48000, 240)
+        x = rng.standard_normal((len(items), C), dtype=np.float32)
+        bias = (0.1 * rng.standard_normal(C)).astype(np.float32)
+        prm = adain_params(rng, 8, C)
+        w = (rng.standard_normal((C, C, K)) * 0.05).astype(np.float32)
+        y, _ = run_ours(False, x, w, bias, items, prm, K, 1, 0)
+        print(json.dumps({"case": "single", "K": K, "rows": len(items), "mean_abs_y": float(np.abs(y).mean())}))
+        return
     rc = RefConv()
     lines = []
 
