@@ -16,7 +16,7 @@ A small case first checks that the two kernels compute the same convolution (sam
 and AdaIN parameters; relative L2 difference of the outputs, both with bf16 operands).
 
 Run on a GPU box from the repository root:
-    python oracle/time_ref_conv.py --out gpurun_out/ref_conv.json
+    python oracle/time_ref_conv.py --out ref_conv.json
     python oracle/time_ref_conv.py --single 3     # one launch of this engine's conv, for ncu
 """
 import argparse
