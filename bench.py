@@ -5,7 +5,10 @@ the full ragged forward over 251 synthetic lines (token lengt
 median 110, sigma 0.6, clamped to [8, 510]; ids uniform in [1, 177]; one style per file;
 model-predicted durations). Under torchrun each rank runs its own 251-line shard (weak scaling,
 no collectives on the hot path; the process group only carries the barrier and the max-over-ranks
-timing). ``--workload config2`` times the vocoder-only op (decoder + generator, B = 32, T = 400).
+timing). ``--workload config2`` times the vocoder-only op (decoder + generator, B = 32, T = 400);
+``--workload config3`` runs the full forward on the text-side configuration (256 sequences,
+lengths uniform in [16, 510]) and adds ``text_side``: tokens/s and TFLOP/s of the ALBERT,
+duration and text-encoder stages, from the profiled step's stage boundaries (``stage_ms``).
 
 Metric: audio-seconds per wall-second (audio-s = samples / 24000), whole job. ``value`` uses
 device-resident inputs with the audio left on the device; ``e2e`` goes through the public C ABI
@@ -56,6 +59,25 @@ def config4_lines(seed: int, n_lines: int = 251):
     toks = [rng.integers(1, 178, n) for n in lens]
     style = (rng.standard_normal(256) * 0.1).astype(np.float32)
     return toks, style
+
+
+def config3_lines(seed: int, n_lines: int = 256):
+    """The text-side configuration: 256 sequences with token lengths uniform in [16, 510], ids
+    uniform in [1, 177], one style vector (N(0, 0.1^2))."""
+    rng = np.random.default_rng(seed)
+    lens = rng.integers(16, 511, n_lines)
+    toks = [rng.integers(1, 178, n) for n in lens]
+    style = (rng.standard_normal(256) * 0.1).astype(np.float32)
+    return toks, style
+
+
+# Text-side FLOPs per token from the layer shapes: ALBERT (embedding projection + 12 layers of QKV,
+# attention output and FFN GEMMs) 132.3 M, its attention 36,864 * T (QK^T and PV, 12 layers, T =
+# the sequence's length), text encoder (3 convs k 5 + BiLSTM) 11.0 M, duration side (bert_encoder,
+# 3 AdaLN + BiLSTM layers, predictor LSTM, logits) 15.5 M.
+TEXT_FLOP_PER_TOKEN = 132.3e6 + 11.0e6 + 15.5e6
+ATTN_FLOP_PER_TOKEN_PER_T = 36864.0
+TEXT_STAGES = ("stage:albert", "stage:durations", "stage:text encoder")
 
 
 def config2_inputs(seed: int, B: int = 32, T: int = 400):
@@ -166,7 +188,7 @@ def main():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--workload", default="config4", choices=["config4", "config2"])
+    ap.add_argument("--workload", default="config4", choices=["config4", "config3", "config2"])
     ap.add_argument("--precision", default=os.environ.get("KK_PRECISION", "bf16"), choices=["bf16", "fp32"])
     ap.add_argument("--cpu-lines", type=int, default=3, help="lines in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -228,16 +250,21 @@ def main():
             dist.barrier()
         torch.cuda.synchronize()
 
-    if args.workload == "config4":
-        toks, style = config4_lines(seed=1000 + rank)
+    if args.workload in ("config4", "config3"):
+        if args.workload == "config4":
+            toks, style = config4_lines(seed=1000 + rank)
+            workload_desc = ("config4: full ragged forward, 251 synthetic lines per rank (lognormal lengths median "
+                             "110 sigma 0.6 clamped [8,510]), predicted durations, one batch")
+        else:
+            toks, style = config3_lines(seed=3000 + rank)
+            workload_desc = ("config3: 256 sequences per rank, token lengths uniform in [16,510], full ragged "
+                             "forward with predicted durations, one batch; text side reported from stage times")
         items = [kk.BatchItem(np.concatenate([[0], t, [0]]), style, 1.0, kk.ItemNoise(seed=kk.mix_seed(rank, i)))
                  for i, t in enumerate(toks)]
 
         def step(fetch):
             outs = eng.forward_batch(items, fetch=fetch)
             return sum(o.audio.shape[0] for o in outs) / 24000.0
-        workload_desc = ("config4: full ragged forward, 251 synthetic lines per rank (lognormal lengths median 110 "
-                         "sigma 0.6 clamped [8,510]), predicted durations, one batch")
     else:
         asr, f0s, ns, s_dec = config2_inputs(seed=2000 + rank, B=args.items, T=args.frames)
 
@@ -348,9 +375,21 @@ def main():
             a, tt = time_oracle(ckpt, lines, style, threads)
             cpu = {"value": a / tt, "unit": "audio-s/s", "cores": threads, "kind": "port",
                    "sample": f"{len(lines)} median-length lines of config 4 ({a:.1f} audio-s in {tt:.1f} s)"}
+        stages = {k[len("stage:"):]: v[1] for k, v in prof.items() if k.startswith("stage:")}
+        kprof = {k: v for k, v in prof.items() if not k.startswith("stage:")}
+        text_side = None
+        if args.workload == "config3":
+            # rank 0's own shard, from the profiled step's stage boundaries
+            n_tok = sum(len(t) + 2 for t in toks)
+            fl = sum((len(t) + 2) * (TEXT_FLOP_PER_TOKEN + ATTN_FLOP_PER_TOKEN_PER_T * (len(t) + 2)) for t in toks)
+            t_ms = sum(stages.get(s[len("stage:"):], 0.0) for s in TEXT_STAGES)
+            text_side = {"tokens": n_tok, "stages": [s[len("stage:"):] for s in TEXT_STAGES], "ms": t_ms,
+                         "tokens_per_s": n_tok / max(t_ms, 1e-9) * 1000.0, "tflop": fl / 1e12,
+                         "tflops": fl / max(t_ms, 1e-9) / 1e9}
         res = {
-            "metric": "audio-sec per wall-sec" + (" (full ragged forward)" if args.workload == "config4" else
-                                                  " (vocoder-only decoder+generator)"),
+            "metric": "audio-sec per wall-sec" + {"config4": " (full ragged forward)",
+                                                  "config3": " (full ragged forward, text-side configuration)",
+                                                  "config2": " (vocoder-only decoder+generator)"}[args.workload],
             "value": value, "unit": "audio-s/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": max_ms / args.steps, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "bf16" if "tcgen05" in eng.identity else "f32", "data": "synthetic",
@@ -365,9 +404,11 @@ def main():
             "gpu_launches": launches,
             "kernel_profile_steps": 1,
             "kernel_profile": {k: {"launches": v[0], "ms": v[1], "tflops": v[2] / max(v[1], 1e-9) / 1e9}
-                               for k, v in prof.items()},
+                               for k, v in kprof.items()},
+            "stage_ms": stages,
             "clocks": clk.summary(),
             "device_memory": mem,
+            **({"text_side": text_side} if text_side else {}),
         }
         print(json.dumps(res))
     eng.close()

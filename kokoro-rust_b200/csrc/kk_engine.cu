@@ -309,6 +309,7 @@ struct Engine {
   std::vector<std::string> prof_names;
   std::vector<long long> prof_launches;
   std::vector<double> prof_ms, prof_flops;
+  cudaEvent_t stage_ev = nullptr;  // profile: the last stage boundary (intervals become "stage:<name>")
   // results of the last forward
   float* audio_host = nullptr;
   size_t audio_host_cap = 0;
@@ -447,6 +448,11 @@ void Engine::times_begin() {
 void Engine::times_compute_begin() {
   if (noalloc_active) return;
   KK_CUDA(cudaEventRecord(ev[1], st));
+  stage_ev = nullptr;
+  if (profile) {
+    stage_ev = pool_event();
+    KK_CUDA(cudaEventRecord(stage_ev, st));
+  }
 }
 void Engine::times_compute_end() {
   if (noalloc_active) return;
@@ -758,7 +764,16 @@ void Engine::dump(const char* name, const void* p, long long rows, int cols, int
   }
 }
 
+// Stage boundary: with the profile on, the device time since the previous boundary is recorded as
+// class "stage:<what>" (launch count 1, no FLOPs); with KK_OPT_SYNC_EACH_STAGE the stream is
+// synchronised so an error is reported against the stage that raised it.
 void Engine::stage_sync(const char* what) {
+  if (profile && stage_ev && !noalloc_active) {
+    cudaEvent_t b = pool_event();
+    KK_CUDA(cudaEventRecord(b, st));
+    prof_pending.push_back({prof_class((std::string("stage:") + what).c_str()), stage_ev, b, 0.0, 0.0});
+    stage_ev = b;
+  }
   if (!sync_each) return;
   cudaError_t s = cudaStreamSynchronize(st);
   if (s != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(s));
@@ -1432,6 +1447,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     dump("logits", logits, LT, 50, 50);
     ar.rewind(mk);
   }
+  stage_sync("durations");
   // ---- durations to the host: the one mid-forward synchronisation (src/gpu_batch.rs:243-248)
   std::vector<int> dur_h(LT, 0);
   if (forced) {
