@@ -4,7 +4,7 @@ The compute lives in ``libkokoro_b200.so`` (CUDA for sm_100a, built from ``csrc/
 holds the host-side mirror of the reference engine API (``engine``), WAV output (``wav``), the
 checkpoint manifest and seeded random-init generator (``weights``) and the build step (``build``).
 """
-from . import pth, shard, wav, weights  # noqa: F401
+from . import multi, pth, shard, wav, weights  # noqa: F401
 from .engine import (BatchItem, BatchPolicy, Engine, GpuKokoro, ItemNoise, KokoroError, Output, Synth, Voice,
                      load_library, mix_seed, plan_batches)
 

@@ -196,24 +196,34 @@ def whole_file_output(inp: InputFile, out_dir: str, state_dir: str, entries: lis
 
 
 def synth(args, engine=None) -> int:
-    """Run the pipeline; engine (an ``Engine``) is created from ``args.model_dir`` when not given."""
-    fmt = {"pcm16": wav.Format.Pcm16, "float32": wav.Format.Float32}[args.format]
+    """Run the pipeline; engine (an ``Engine``, or a ``multi.MultiEngine`` with ``--cuda-devices``)
+    is created from ``args.model_dir`` when not given."""
     if args.input_format != "phonemes":
         raise JobError("--input-format text needs the text frontend, which is not part of this build "
                        "(use --input-format phonemes)")
+    t_load = time.time()
+    if engine is not None:
+        return _synth(args, engine, t_load)
+    d = args.model_dir
+    weights = os.path.join(d, "kokoro-v1_0.pth")
+    if not os.path.exists(weights):
+        st = sorted(f for f in os.listdir(d) if f.endswith(".safetensors"))
+        if not st:
+            raise JobError(f"{d} has neither kokoro-v1_0.pth nor a .safetensors checkpoint")
+        weights = os.path.join(d, st[0])
+    devices = [int(x) for x in args.cuda_devices.split(",")] if args.cuda_devices else [args.cuda_device]
+    if len(devices) > 1:
+        from .multi import MultiEngine
+        with MultiEngine(weights, devices, args.precision, model_dir=d) as eng:
+            return _synth(args, eng, t_load)
+    from .engine import Engine
+    return _synth(args, Engine(weights, devices[0], args.precision, model_dir=d), t_load)
+
+
+def _synth(args, engine, t_load: float) -> int:
+    fmt = {"pcm16": wav.Format.Pcm16, "float32": wav.Format.Float32}[args.format]
     inp = read_input(args.input)
     os.makedirs(args.out_dir, exist_ok=True)
-    t_load = time.time()
-    if engine is None:
-        from .engine import Engine
-        d = args.model_dir
-        weights = os.path.join(d, "kokoro-v1_0.pth")
-        if not os.path.exists(weights):
-            st = sorted(f for f in os.listdir(d) if f.endswith(".safetensors"))
-            if not st:
-                raise JobError(f"{d} has neither kokoro-v1_0.pth nor a .safetensors checkpoint")
-            weights = os.path.join(d, st[0])
-        engine = Engine(weights, args.cuda_device, args.precision, model_dir=d)
     voice_sha = engine.voice(args.voice).sha256
     load_s = time.time() - t_load
     cfg = {"engine": f"{ENGINE_VERSION} [{engine.identity()}]", "model_sha256": engine.model_sha256,
@@ -457,6 +467,9 @@ def build_parser() -> argparse.ArgumentParser:
     s.add_argument("--voice", default="af_heart")
     s.add_argument("--speed", type=float, default=1.0)
     s.add_argument("--cuda-device", type=int, default=0)
+    s.add_argument("--cuda-devices", default=None,
+                   help="comma-separated CUDA ordinals: one engine process per GPU, each batch window "
+                        "spread over them (longest first to the least-loaded GPU), results in line order")
     s.add_argument("--precision", choices=["bf16", "fp32"], default="bf16")
     s.add_argument("--batch-phonemes", type=int, default=8000)
     s.add_argument("--batch-items", type=int, default=64)
