@@ -57,7 +57,7 @@ class MultiEngine:
     worker's engine instead of ``Engine(weights, ...)`` (tests on hosts without a GPU)."""
 
     def __init__(self, weights_path: str, devices: Sequence[int], precision: str = "bf16",
-                 model_dir: Optional[str] = None, standin: Optional[str] = None):
+                 model_dir: Optional[str] = None, standin: Optional[str] = None, start_timeout: float = 600.0):
         if not devices:
             raise ValueError("no devices")
         visible = os.environ.get("CUDA_VISIBLE_DEVICES")
@@ -83,7 +83,7 @@ class MultiEngine:
         infos = []
         for w in range(len(self.procs)):
             try:
-                rep = self._recv(w)
+                rep = self._recv(w, timeout=start_timeout)
             except WorkerLost as e:
                 rep = ("fatal", str(e))
             infos.append(rep)
@@ -108,10 +108,15 @@ class MultiEngine:
             self._drop(w)
             raise WorkerLost(f"worker for cuda device {self.devices[w]} exited ({e})") from None
 
-    def _recv(self, w: int):
+    def _recv(self, w: int, timeout: Optional[float] = None):
         p = self.procs[w]
         if p is None:
             raise WorkerLost(f"worker for cuda device {self.devices[w]} is gone")
+        if timeout is not None:  # only before the first message, when nothing is buffered yet
+            import select
+            if not select.select([p.stdout], [], [], timeout)[0]:
+                self._drop(w)
+                raise WorkerLost(f"worker for cuda device {self.devices[w]} did not answer within {timeout:.0f} s")
         try:
             return pickle.load(p.stdout)
         except (EOFError, pickle.UnpicklingError, OSError) as e:
@@ -221,10 +226,11 @@ class MultiEngine:
         self.close()
 
     def __del__(self):
-        try:
-            self.close()
-        except Exception:  # noqa: BLE001
-            pass
+        if getattr(self, "procs", None):
+            try:
+                self.close()
+            except Exception:  # noqa: BLE001
+                pass
 
 
 def worker_main(argv: List[str]) -> int:

@@ -79,6 +79,14 @@ def test_worker_that_cannot_start_is_reported(kk, tmp_path):
         MultiEngine("/nonexistent.safetensors", [0, 1], standin=str(bad))
 
 
+def test_worker_that_never_answers_is_ended(kk, tmp_path):
+    from kokoro_rust_b200.multi import MultiEngine
+    slow = tmp_path / "slow_standin.py"
+    slow.write_text("import time\ndef make_engine(kk, device):\n    time.sleep(3600)\n")
+    with pytest.raises(RuntimeError, match="did not answer within 2 s"):
+        MultiEngine("/nonexistent.safetensors", [0], standin=str(slow), start_timeout=2.0)
+
+
 def test_synth_pipeline_over_two_workers_matches_one_engine(kk, tmp_path):
     from kokoro_rust_b200 import cli
     from kokoro_rust_b200.multi import MultiEngine
