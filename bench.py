@@ -369,7 +369,7 @@ def main():
                 for r in plog:
                     f.write(f"{r[0]},{r[1]:.6f},{r[2]:.6g},{r[3]:.6g}\n")
         cpu = None
-        if not args.no_cpu_baseline and args.workload == "config4":
+        if not args.no_cpu_baseline and args.workload == "config4" and world == 1:  # N = 1 only
             threads = torch.get_num_threads()
             lines = cpu_sample_lines(toks, args.cpu_lines)
             a, tt = time_oracle(ckpt, lines, style, threads)
