@@ -60,10 +60,14 @@ class MultiEngine:
                  model_dir: Optional[str] = None, standin: Optional[str] = None, start_timeout: float = 600.0):
         if not devices:
             raise ValueError("no devices")
+        self.procs: List[Optional[subprocess.Popen]] = []
+        if standin is None and os.environ.get("KK_NO_BUILD") != "1" and os.path.isdir(os.path.join(HERE, "csrc")):
+            # bring the library up to date here, once, so the workers never compile concurrently
+            from . import build as _build
+            _build.build()
         visible = os.environ.get("CUDA_VISIBLE_DEVICES")
         vis = [v.strip() for v in visible.split(",")] if visible else None
         self.devices = list(devices)
-        self.procs: List[Optional[subprocess.Popen]] = []
         for d in self.devices:
             env = dict(os.environ)
             if vis is not None:
