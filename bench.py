@@ -240,6 +240,8 @@ def main():
                                 device_id=torch.device("cuda", local_rank))
     if rank == 0:
         kk.weights.write_random_checkpoint(ckpt, 0)
+        if world > 1:  # the library is brought up to date by one rank, before the others load it
+            kk.engine.load_library()
     if world > 1:
         dist.barrier()
     eng = kk.GpuKokoro(ckpt, local_rank, args.precision)
