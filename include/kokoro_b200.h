@@ -36,7 +36,8 @@ typedef enum {
   KK_ERR_INVALID_ARG = 1, /* bad shapes / ids / speed (src/gpu_batch.rs:183-187) */
   KK_ERR_OOM = 2,         /* device or pinned-host allocation failed */
   KK_ERR_CUDA = 3,        /* any other CUDA runtime error */
-  KK_ERR_TIMEOUT = 4,     /* a bounded in-kernel wait (LSTM step barrier) gave up */
+  KK_ERR_TIMEOUT = 4,     /* a bounded in-kernel wait (a tcgen05 pipeline, attention or LSTM recurrence
+                             mbarrier) gave up; the message names the error-flag code */
   KK_ERR_IO = 5           /* weight file missing, unreadable or malformed */
 } kk_status;
 
@@ -83,7 +84,9 @@ KK_API const char* kk_identity(const kk_engine* e);
  *  speed          [n_items], finite and > 0
  *  seeds          [n_items] counter-noise seeds (ItemNoise::Counter), NULL = all zero
  *  noise          NULL, or replayed sine-noise draws (ItemNoise::Fixed) for every item,
- *                 concatenated, 600 * 9 * N_b floats per item; requires forced_dur
+ *                 concatenated, 600 * 9 * N_b floats per item; requires forced_dur, because the
+ *                 concatenated buffer carries no per-item lengths (kk_forward_batch_noise takes
+ *                 per-item draws with predicted durations, as the reference does)
  *  forced_dur     NULL, or per-token durations (>= 0, each item's sum >= 1), laid out like ids;
  *                 replaces the predicted durations (vocoder comparison mode)
  *  dur_out        [sum ids_len] durations used (predicted or forced), like ids; may be NULL
@@ -95,6 +98,24 @@ KK_API kk_status kk_forward_batch(kk_engine* e, int n_items, const int64_t* ids,
                            const float* ref_s, const float* speed, const uint64_t* seeds,
                            const float* noise, const int64_t* forced_dur, int64_t* dur_out,
                            int64_t* n_samples_out);
+
+/*
+ * kk_forward_batch_noise -- kk_forward_batch with the reference's per-item noise choice
+ * (ItemNoise, src/gpu_batch.rs:14-17; its use at src/gpu_batch.rs:325-340): item i replays
+ * noise[i] (ItemNoise::Fixed) when noise is not NULL and noise[i] is not NULL, else it draws the
+ * counter stream of seeds[i] (ItemNoise::Counter), so one batch may mix both. A replayed item's
+ * draw count noise_len[i] must equal 600 * 9 * N_i for the durations the call uses, predicted or
+ * forced, else the call fails with KK_ERR_INVALID_ARG ("fixed noise size mismatch for item i")
+ * after the durations are known, as the reference's check does. rand_ini ([n_items][9] or NULL) is
+ * the Fixed variant's initial phase: it must be finite and is otherwise unused, because the
+ * reference adds it to the rad curve at sample 0 only, and the linear x1/300 downsample of the
+ * phase never reads sample 0 (its first source position is 149.5). Other arguments as
+ * kk_forward_batch.
+ */
+KK_API kk_status kk_forward_batch_noise(kk_engine* e, int n_items, const int64_t* ids, const int32_t* ids_len,
+                                        const float* ref_s, const float* speed, const uint64_t* seeds,
+                                        const float* const* noise, const int64_t* noise_len, const float* rand_ini,
+                                        const int64_t* forced_dur, int64_t* dur_out, int64_t* n_samples_out);
 
 /* Copy item `item`'s audio of the last forward into `dst` (capacity `cap` floats). */
 KK_API kk_status kk_fetch_audio(kk_engine* e, int item, float* dst, int64_t cap);
@@ -194,9 +215,11 @@ KK_API kk_status kk_decode_batch(kk_engine* e, int n_items, const int32_t* n_fra
  * kk_decode_batch.
  *
  * The first call on a device looks up the array's device address (once per device, with that
- * device current); make that first call before any stream capture. All calls on a device share
- * the array and it keeps the last call's contents: calls whose GPU work overlaps (two threads or
- * two engines on one device) race on it and must be serialised by the caller.
+ * device current); make that first call before any stream capture. The address is kept for the
+ * life of the process and belongs to the device's primary context: a host application that resets
+ * the device (cudaDeviceReset) must not call this entry point again in that process. All calls on a
+ * device share the array and it keeps the last call's contents: calls whose GPU work overlaps (two
+ * threads or two engines on one device) race on it and must be serialised by the caller.
  */
 KK_API kk_status kk_decode_batch_noalloc(kk_engine* e, int n_items, const int32_t* n_frames, const float* asr,
                                          const float* f0, const float* n, const float* s_dec,
@@ -208,9 +231,17 @@ typedef enum {
   KK_OPT_SYNC_EACH_STAGE = 2,      /* 1: synchronise after each stage (error localisation) */
   KK_OPT_PROFILE = 3,              /* 1: time every convolution / LSTM / attention launch with
                                       CUDA events on the engine stream (see kk_profile_entry) */
-  KK_OPT_OUTPUT_PCM16 = 4          /* 1: forward converts the audio to PCM_16 on the device (the WAV
+  KK_OPT_OUTPUT_PCM16 = 4,         /* 1: forward converts the audio to PCM_16 on the device (the WAV
                                       rule of kk_wav_encode) and copies only int16 to the host; read
                                       it with kk_fetch_audio_pcm16 (kk_fetch_audio then refuses) */
+  KK_OPT_GAP_CANARY = 5,           /* tests, 1: every device buffer the engine takes for a call is
+                                      first filled with NaN, so any element (a gap row above all) that
+                                      a kernel reads before writing it poisons the output; outputs
+                                      must not change. No counterpart in the reference */
+  KK_OPT_NEGCTL_NOMASK = 6         /* tests, 1 (FP32 mode only): convolutions read the gap rows of
+                                      their input as they are instead of as zeros, the negative control
+                                      of the reference's KOKORO_BATCH_NEGCTL_NOMASK
+                                      (src/gpu_batch.rs:62-66): batched outputs must then change */
 } kk_option;
 KK_API kk_status kk_set_option(kk_engine* e, int option, int64_t value);
 
@@ -297,6 +328,15 @@ KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int3
  */
 KK_API kk_status kk_lstm_selftest(int cuda_ordinal, int tc, int n_items, const int32_t* len, const float* gx,
                                   const float* whh, const float* bhh, float* out);
+/*
+ * kk_wait_selftest -- diagnostics of the failure path: one kernel on the engine's stream waits, with
+ * the bounded mbarrier wait every tcgen05 pipeline uses but a limit of limit_ns (1 us .. 100 ms), on
+ * a barrier that nothing arrives on. The wait gives up, sets the engine's error flag and returns; the
+ * call then returns KK_ERR_TIMEOUT with the flag's message, exactly as a forward whose wait expired
+ * would, and the engine stays usable. No trap, no fault. No counterpart in the reference.
+ */
+KK_API kk_status kk_wait_selftest(kk_engine* e, int64_t limit_ns);
+
 /* Message of the last kk_conv_selftest / kk_attention_selftest / kk_lstm_selftest failure on this thread. */
 KK_API const char* kk_conv_selftest_error(void);
 

@@ -106,6 +106,9 @@ struct ConvArgs {
   // OUT_GELU_PRE: output planes in the same layout, ypre_rows rows per plane
   void* ypre;
   long ypre_rows;
+  // negative control (tests, SIMT path): gap rows of the input are read as they are instead of as
+  // zeros (the reference's KOKORO_BATCH_NEGCTL_NOMASK, src/gpu_batch.rs:62-66)
+  int nomask;
 };
 
 __device__ __forceinline__ float leaky(float v, float s) { return v < 0.0f ? v * s : v; }

@@ -45,6 +45,7 @@ __global__ void __launch_bounds__(256) conv_simt_kernel(ConvArgs a) {
         } else {
           int b = dom_item(a.din, r);
           if (b >= 0) v = prologue(a, a.x[(long)(a.in_up2 ? (r >> 1) : r) * a.ldx + c], b, c);
+          else if (a.nomask) v = a.x[(long)(a.in_up2 ? (r >> 1) : r) * a.ldx + c];
         }
       }
       xs[i] = v;

@@ -10,6 +10,7 @@
 #include <cstring>
 #include <algorithm>
 #include <memory>
+#include <mutex>
 #include <numeric>
 #include <string>
 #include <vector>
@@ -56,15 +57,26 @@ class Arena {
     ext_used_ = 0;
   }
   void clear_external() { ext_base_ = nullptr; }
+  // Gap canary (tests): with a stream set, every buffer handed out is first filled with NaN bytes on
+  // that stream, so an element read before any kernel wrote it poisons the result.
+  void set_poison(cudaStream_t st) { poison_st_ = st; }
   void* alloc(size_t bytes) {
+    void* p = alloc_raw(bytes);
+    if (poison_st_) {
+      cudaError_t e = cudaMemsetAsync(p, 0xFF, (bytes + 255) & ~size_t(255), poison_st_);
+      if (e != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string("gap canary fill: ") + cudaGetErrorString(e));
+    }
+    return p;
+  }
+  void* alloc_raw(size_t bytes) {
     bytes = (bytes + 255) & ~size_t(255);
     if (bytes == 0) bytes = 256;
     if (ext_base_) {
+      // the peak statistic describes the allocating arena only, never the static scratch
       if (ext_used_ + bytes > ext_cap_)
         throw KKError(KK_ERR_INVALID_ARG, "static scratch exhausted (batch above the no-allocation limit)");
       void* p = ext_base_ + ext_used_;
       ext_used_ += bytes;
-      if (ext_used_ > peak_) peak_ = ext_used_;
       return p;
     }
     while (cur_ < blocks_.size()) {
@@ -144,6 +156,7 @@ class Arena {
   char* ext_base_ = nullptr;
   size_t ext_cap_ = 0, ext_used_ = 0;
   size_t peak_ = 0;
+  cudaStream_t poison_st_ = nullptr;
 };
 
 // Pinned host staging for the uploads and downloads of one call (reset per call).
@@ -277,6 +290,8 @@ struct Engine {
   std::string ident;
   bool keep_audio_dev = false, sync_each = false;
   bool pcm16_out = false;                // KK_OPT_OUTPUT_PCM16
+  bool gap_canary = false;               // KK_OPT_GAP_CANARY (tests): arena buffers start as NaN
+  bool negctl_nomask = false;            // KK_OPT_NEGCTL_NOMASK (tests, FP32 mode): convs read gap rows unmasked
   int16_t* audio_host16 = nullptr;       // pinned PCM_16 of the last forward
   size_t audio_host16_cap = 0;
   std::vector<long long> out_clipped;    // per item, with KK_OPT_OUTPUT_PCM16
@@ -370,14 +385,30 @@ struct Engine {
                      const long long* noise_off_d);
   // pcm16: honour KK_OPT_OUTPUT_PCM16 (the forward); the vocoder entry returns f32 to its caller
   void finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& items_h, const int* col_item_n, bool pcm16);
+  // noise: null, or per item a pointer to replayed draws (null = the item's counter stream) with
+  // noise_len[b] floats, checked against 600 * 9 * N_b once the durations are known
   void forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
-               const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
-               int64_t* nsamp_out);
+               const uint64_t* seeds, const float* const* noise, const int64_t* noise_len, const float* rand_ini,
+               const int64_t* forced, int64_t* dur_out, int64_t* nsamp_out);
   void decode(int B, const int32_t* n_frames, const float* asr, const float* f0, const float* n, const float* s_dec,
               const uint64_t* seeds, const float* noise, float* audio_out);
   void decode_noalloc(int B, const int32_t* n_frames, const float* asr, const float* f0, const float* n,
                       const float* s_dec, const uint64_t* seeds, const float* noise, float* audio_out);
+  void wait_selftest(long long limit_ns);
+  // replayed noise of the items that carry it (noise[b] != null), -1 offsets for counter-noise items
+  void upload_noise(int B, const std::vector<ItemTab>& items_h, const float* const* noise, float** noise_d,
+                    long long** noise_off_d);
 };
+
+// Message of a nonzero engine error flag (set by a bounded in-kernel wait that gave up).
+static std::string wait_error(int code) {
+  switch (code) {
+    case 2: return "a tcgen05 pipeline barrier wait timed out (error flag 2)";
+    case 3: return "a tensor-core attention MMA wait timed out (error flag 3)";
+    case 4: return "an LSTM recurrence wait timed out (error flag 4)";
+    default: return "a bounded device wait timed out (error flag " + std::to_string(code) + ")";
+  }
+}
 
 Engine::~Engine() {
   if (dev >= 0) cudaSetDevice(dev);
@@ -787,6 +818,7 @@ ConvArgs Engine::ca(const Conv& c) {
   a.in_mode = IN_NOMASK;
   a.out_mode = OUT_STORE;
   a.oscale = 1.0f;
+  a.nomask = negctl_nomask ? 1 : 0;
   return a;
 }
 
@@ -1235,8 +1267,7 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
   out_clipped.assign(items_h.size(), 0);
   if (clip_h)
     for (size_t b = 0; b < items_h.size(); b++) out_clipped[b] = (long long)clip_h[b];
-  if (errh) throw KKError(KK_ERR_TIMEOUT, errh == 1 ? "an LSTM step barrier timed out"
-                                                    : "a tcgen05 convolution pipeline wait timed out");
+  if (errh) throw KKError(KK_ERR_TIMEOUT, wait_error(errh));
   float t_all = 0, t_comp = 0;
   KK_CUDA(cudaEventElapsedTime(&t_all, ev[0], ev[3]));
   KK_CUDA(cudaEventElapsedTime(&t_comp, ev[1], ev[2]));
@@ -1244,12 +1275,36 @@ void Engine::finish_audio(float* audio_d, int LN, const std::vector<ItemTab>& it
   prof_collect();
 }
 
+void Engine::upload_noise(int B, const std::vector<ItemTab>& items_h, const float* const* noise, float** noise_d,
+                          long long** noise_off_d) {
+  std::vector<long long> off(B, -1);
+  long long tot = 0;
+  for (int b = 0; b < B; b++)
+    if (noise[b]) off[b] = tot, tot += 600LL * 9 * items_h[b].n;
+  float* d = ar.get<float>((size_t)std::max(tot, 1LL));
+  for (int b = 0; b < B; b++) {
+    if (!noise[b]) continue;
+    const size_t bytes = sizeof(float) * 600 * 9 * (size_t)items_h[b].n;
+    void* s = pin.alloc(bytes);
+    memcpy(s, noise[b], bytes);
+    KK_CUDA(cudaMemcpyAsync(d + off[b], s, bytes, cudaMemcpyHostToDevice, st));
+    h2d_bytes += (double)bytes;
+  }
+  *noise_d = d;
+  *noise_off_d = upload(off.data(), B);
+}
+
 void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const float* ref_s, const float* speed,
-                     const uint64_t* seeds, const float* noise, const int64_t* forced, int64_t* dur_out,
-                     int64_t* nsamp_out) {
+                     const uint64_t* seeds, const float* const* noise, const int64_t* noise_len,
+                     const float* rand_ini, const int64_t* forced, int64_t* dur_out, int64_t* nsamp_out) {
   KK_REQUIRE(B > 0, "empty batch");
   KK_REQUIRE(ids && ids_len && ref_s && speed, "null input pointer");
-  KK_REQUIRE(!(noise && !forced), "replayed noise requires forced durations");
+  KK_REQUIRE(!noise || noise_len, "replayed noise without its lengths");
+  // rand_ini of ItemNoise::Fixed is validated and otherwise unused: the reference adds it to the rad
+  // curve at sample 0 only, which the linear x1/300 downsample of the phase never reads (its first
+  // source position is 149.5), so it cannot change the output
+  if (rand_ini)
+    for (int i = 0; i < 9 * B; i++) KK_REQUIRE(std::isfinite(rand_ini[i]), "rand_ini must be finite");
   long long total_ids = 0;
   for (int b = 0; b < B; b++) {
     KK_REQUIRE(ids_len[b] >= 2 && ids_len[b] <= 512, "input_ids length outside [2, 512]");
@@ -1271,6 +1326,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   }
   KK_CUDA(cudaSetDevice(dev));
   ar.reset();
+  ar.set_poison(gap_canary ? st : nullptr);
   pin.reset();
   prof_pending.clear();
   ev_used = 0;
@@ -1462,8 +1518,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     KK_CUDA(cudaMemcpyAsync(dh, dur_d, sizeof(int) * LT, cudaMemcpyDeviceToHost, st));
     KK_CUDA(cudaMemcpyAsync(eh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
     KK_CUDA(cudaStreamSynchronize(st));
-    if (*eh) throw KKError(KK_ERR_TIMEOUT, *eh == 1 ? "an LSTM step barrier timed out"
-                                                    : "a tcgen05 convolution pipeline wait timed out");
+    if (*eh) throw KKError(KK_ERR_TIMEOUT, wait_error(*eh));
     memcpy(dur_h.data(), dh, sizeof(int) * LT);
   }
   if (dur_out) {
@@ -1485,6 +1540,11 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   }
   last_frames = 0;
   for (int b = 0; b < B; b++) last_frames += items_h[b].n;
+  if (noise)
+    for (int b = 0; b < B; b++)
+      KK_REQUIRE(!noise[b] || noise_len[b] == 600LL * 9 * items_h[b].n,
+                 "fixed noise size mismatch for item " + std::to_string(b) + " (needs 600 * 9 * " +
+                     std::to_string(items_h[b].n) + " draws)");
   if (nsamp_out)
     for (int b = 0; b < B; b++) nsamp_out[b] = 600LL * items_h[b].n;
   std::vector<int> col_item_h(LN, -1), src_row_h(LN, -1);
@@ -1500,6 +1560,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
   items_d = upload(items_h.data(), B);
   int* col_item_d = upload(col_item_h.data(), LN);
   int* src_row_d = upload(src_row_h.data(), LN);
+  stage_sync("frame layout");  // durations read-back, host layout build and upload
   const Dom dN{col_item_d, LN, 1, 0, LN};
   const Dom d2{col_item_d, LN, 2, 0, 2 * LN};
   std::vector<int> fstart(B), flen(B);
@@ -1554,22 +1615,17 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     }
     float* t_en = nxt;
     lstm(m.te_lstm, cur, 512, LT, tstart, tlen, t_en, 512);
+    dump("t_en", t_en, LT, 512, 512);
     check(launch_gather_rows(t_en, 512, src_row_d, LN, 512, xcat0, X0_LD, st), "gather_rows");
     ar.rewind(mk);
   }
   stage_sync("text encoder");
-  // ---- noise inputs
+  // ---- noise inputs (ItemNoise per item, src/gpu_batch.rs:325-340)
   uint64_t* seeds_d = nullptr;
   if (seeds) seeds_d = upload(seeds, B);
   float* noise_d = nullptr;
   long long* noise_off_d = nullptr;
-  if (noise) {
-    std::vector<long long> off(B);
-    long long tot = 0;
-    for (int b = 0; b < B; b++) off[b] = tot, tot += 600LL * 9 * items_h[b].n;
-    noise_d = upload(noise, (size_t)tot);
-    noise_off_d = upload(off.data(), B);
-  }
+  if (noise) upload_noise(B, items_h, noise, &noise_d, &noise_off_d);
   float* audio = decode_core(B, items_h, items_d, col_item_d, LN, xcat0, f0, nc, gb_dec, wdec, seeds_d, noise_d,
                              noise_off_d);
   finish_audio(audio, LN, items_h, col_item_d, true);
@@ -1592,6 +1648,7 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
   last_frames = tot;
   KK_CUDA(cudaSetDevice(dev));
   ar.reset();
+  ar.set_poison(gap_canary ? st : nullptr);
   pin.reset();
   prof_pending.clear();
   ev_used = 0;
@@ -1657,17 +1714,25 @@ constexpr int NOALLOC_MAX_ITEMS = 8;
 constexpr int NOALLOC_MAX_FRAMES = 120;  // N-domain frames of a call, 2 gap frames per item included
 static __device__ __align__(256) unsigned char g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
 
-// Device address of g_noalloc_scratch on the current device, looked up once per device (the
-// host-side symbol is only a stand-in and must never be handed to a kernel).
+// Device address of g_noalloc_scratch on device `dev` (which must be current), looked up once per
+// device under a std::once_flag, so threads driving engines on one device cannot race on the cache
+// (a failed lookup throws and is retried by the next call). The host-side symbol is only a stand-in
+// and must never be handed to a kernel. The cached address belongs to the device's primary context:
+// a host application that resets the device (cudaDeviceReset) must not call this entry point again
+// in the same process.
 static void* noalloc_scratch(int dev) {
+  static std::once_flag once[64];
   static void* addr[64] = {};
   if (dev < 0 || dev >= 64) throw KKError(KK_ERR_INVALID_ARG, "device ordinal above 63");
-  if (!addr[dev]) {
+  std::call_once(once[dev], [dev] {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) throw KKError(KK_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    if (e != cudaSuccess) {
+      cudaGetLastError();
+      throw KKError(KK_ERR_CUDA, std::string("cudaGetSymbolAddress: ") + cudaGetErrorString(e));
+    }
     addr[dev] = p;
-  }
+  });
   return addr[dev];
 }
 
@@ -1699,6 +1764,7 @@ void Engine::decode_noalloc(int B, const int32_t* n_frames, const float* asr, co
     }
   } guard{this};
   ar.set_external(noalloc_scratch(dev), NOALLOC_SCRATCH_BYTES);
+  ar.set_poison(gap_canary ? st : nullptr);
   noalloc_active = true;
   KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
   int col_item[NOALLOC_MAX_FRAMES], tab1[NOALLOC_MAX_FRAMES], tab2[2 * NOALLOC_MAX_FRAMES];
@@ -1754,7 +1820,22 @@ void Engine::decode_noalloc(int B, const int32_t* n_frames, const float* asr, co
   int errh = 0;
   KK_CUDA(cudaMemcpyAsync(&errh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
   KK_CUDA(cudaStreamSynchronize(st));
-  if (errh) throw KKError(KK_ERR_TIMEOUT, "a tcgen05 convolution pipeline wait timed out");
+  if (errh) throw KKError(KK_ERR_TIMEOUT, wait_error(errh));
+}
+
+// Bounded-wait self-test: a kernel on the engine stream waits, through the pipelines' own bounded
+// mbarrier wait, on a barrier that nothing arrives on, with a limit of limit_ns; the wait gives up,
+// raises the engine's error flag and returns, and the flag is read back exactly as after a forward.
+void Engine::wait_selftest(long long limit_ns) {
+  KK_REQUIRE(limit_ns >= 1000 && limit_ns <= 100000000LL, "wait limit outside [1 us, 100 ms]");
+  KK_CUDA(cudaSetDevice(dev));
+  KK_CUDA(cudaMemsetAsync(err_flag, 0, sizeof(int), st));
+  check(launch_wait_selftest(err_flag, (unsigned long long)limit_ns, st), "wait_selftest");
+  int errh = 0;
+  KK_CUDA(cudaMemcpyAsync(&errh, err_flag, sizeof(int), cudaMemcpyDeviceToHost, st));
+  KK_CUDA(cudaStreamSynchronize(st));
+  if (errh) throw KKError(KK_ERR_TIMEOUT, wait_error(errh));
+  throw KKError(KK_ERR_CUDA, "wait self-test: the unarrived barrier wait did not expire");
 }
 
 }  // namespace kk
@@ -1841,8 +1922,44 @@ kk_status kk_forward_batch(kk_engine* h, int n_items, const int64_t* ids, const 
   return guarded(h, [&] {
     h->e->out_off.clear();
     h->e->out_len.clear();
-    h->e->forward(n_items, ids, ids_len, ref_s, speed, seeds, noise, forced_dur, dur_out, n_samples_out);
+    std::vector<const float*> nz;
+    std::vector<int64_t> nl;
+    if (noise) {
+      // concatenated draws: each item's share follows from its forced durations
+      KK_REQUIRE(forced_dur, "replayed noise in kk_forward_batch requires forced durations (kk_forward_batch_noise "
+                             "takes per-item draws with predicted durations)");
+      KK_REQUIRE(n_items > 0 && ids_len, "null input pointer");
+      long long o = 0, off = 0;
+      for (int b = 0; b < n_items; b++) {
+        long long nf = 0;
+        for (int i = 0; i < ids_len[b]; i++) nf += forced_dur[o + i];
+        o += ids_len[b];
+        nz.push_back(noise + off);
+        nl.push_back(600LL * 9 * nf);
+        off += 600LL * 9 * nf;
+      }
+    }
+    h->e->forward(n_items, ids, ids_len, ref_s, speed, seeds, noise ? nz.data() : nullptr,
+                  noise ? nl.data() : nullptr, nullptr, forced_dur, dur_out, n_samples_out);
   });
+}
+
+kk_status kk_forward_batch_noise(kk_engine* h, int n_items, const int64_t* ids, const int32_t* ids_len,
+                                 const float* ref_s, const float* speed, const uint64_t* seeds,
+                                 const float* const* noise, const int64_t* noise_len, const float* rand_ini,
+                                 const int64_t* forced_dur, int64_t* dur_out, int64_t* n_samples_out) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    h->e->out_off.clear();
+    h->e->out_len.clear();
+    h->e->forward(n_items, ids, ids_len, ref_s, speed, seeds, noise, noise_len, rand_ini, forced_dur, dur_out,
+                  n_samples_out);
+  });
+}
+
+kk_status kk_wait_selftest(kk_engine* h, int64_t limit_ns) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] { h->e->wait_selftest(limit_ns); });
 }
 
 kk_status kk_fetch_audio(kk_engine* h, int item, float* dst, int64_t cap) {
@@ -1891,7 +2008,12 @@ kk_status kk_set_option(kk_engine* h, int option, int64_t value) {
     else if (option == KK_OPT_SYNC_EACH_STAGE) h->e->sync_each = value != 0;
     else if (option == KK_OPT_PROFILE) h->e->profile = value != 0;
     else if (option == KK_OPT_OUTPUT_PCM16) h->e->pcm16_out = value != 0;
-    else throw kk::KKError(KK_ERR_INVALID_ARG, "unknown option");
+    else if (option == KK_OPT_GAP_CANARY) h->e->gap_canary = value != 0;
+    else if (option == KK_OPT_NEGCTL_NOMASK) {
+      if (value != 0 && h->e->precision != KK_PRECISION_FP32)
+        throw kk::KKError(KK_ERR_INVALID_ARG, "the no-mask negative control exists on the FP32 path only");
+      h->e->negctl_nomask = value != 0;
+    } else throw kk::KKError(KK_ERR_INVALID_ARG, "unknown option");
   });
 }
 

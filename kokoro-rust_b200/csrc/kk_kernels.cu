@@ -677,7 +677,8 @@ __device__ __forceinline__ unsigned long long splitmix_at(unsigned long long see
 
 // har[t] = tanh(sum_h lw[h] * (sin(phase(t, h)) * 0.1 * uv + amp * noise[t*9 + h]) + lb)
 // (sine_har_source + gen_noise, kernels/kokoro.cu:228-254, 282-302), noise generated in place
-// from the item's counter stream or read from replayed draws. One thread per sample of the 600N
+// from the item's counter stream or read from replayed draws (items whose noise_off is -1 use the
+// counter stream, so one batch can mix both). One thread per sample of the 600N
 // domain; gap samples -> 0. sin / tanh / log / sqrt / cos are evaluated in f64 and rounded once
 // to f32 (correctly rounded results), so the source is reproducible on any IEEE CPU.
 __global__ void har_source_kernel(const float* f0, const float* pp, int L2, const ItemTab* items,
@@ -709,7 +710,7 @@ __global__ void har_source_kernel(const float* f0, const float* pp, int L2, cons
   const int i1 = i0 < D - 1 ? i0 + 1 : i0;
   const float l0 = __fsub_rn(1.0f, l1);
   float nz[9];
-  if (noise) {
+  if (noise && noise_off[b] >= 0) {  // replayed draws (ItemNoise::Fixed); offset -1: the counter stream
     const float* nb = noise + noise_off[b] + (long)t * 9;
 #pragma unroll
     for (int h = 0; h < 9; h++) nz[h] = nb[h];

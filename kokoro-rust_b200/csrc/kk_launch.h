@@ -141,6 +141,10 @@ cudaError_t launch_pcm16(const float* audio, long n, const int* col_item_n, int1
 cudaError_t launch_copy_cols(const float* src, int lds, int c0s, float* dst, int ldd, int c0d, int rows,
                              int ncol, cudaStream_t st);
 
+// Bounded-wait self-test: one thread waits, with the pipelines' bounded mbarrier wait and a limit of
+// limit_ns, on a barrier nothing arrives on; the wait expires and sets *err (code 2).
+cudaError_t launch_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st);
+
 // f64 twiddles [cos 11x20 | sin 11x20] and the periodic Hann window (src/gpu.rs:93-103)
 cudaError_t upload_stft_constants(cudaStream_t st);
 

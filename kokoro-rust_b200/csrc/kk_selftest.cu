@@ -14,6 +14,32 @@
 #include "kk_launch.h"
 #include "kk_tc.h"
 
+#include "kk_tc_ptx.cuh"
+
+namespace kk {
+
+// One thread initialises an mbarrier that expects one arrival, then waits on its first phase with
+// the bounded wait every tcgen05 pipeline uses; nothing ever arrives, so the wait must give up after
+// limit_ns, raise the error flag and return (no trap, no fault, no TMA or TMEM in flight).
+__global__ void wait_selftest_kernel(int* err, unsigned long long limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_lim(&bar, 0, &abort_flag, err, limit_ns);
+  __syncthreads();
+}
+
+cudaError_t launch_wait_selftest(int* err, unsigned long long limit_ns, cudaStream_t st) {
+  wait_selftest_kernel<<<1, 32, 0, st>>>(err, limit_ns);
+  return cudaGetLastError();
+}
+
+}  // namespace kk
+
 namespace {
 
 thread_local std::string g_selftest_error;

@@ -51,19 +51,25 @@ __device__ __forceinline__ bool mbar_try_sleep(uint64_t* b, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Bounded wait: returns false (and raises the CTA abort flag + engine error flag) on expiry.
-__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
+// Bounded wait with an explicit limit (ns): returns false (and raises the CTA abort flag + engine
+// error flag, code 2) once the phase has not completed within limit_ns.
+__device__ __forceinline__ bool mbar_wait_lim(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,
+                                              unsigned long long limit_ns) {
   if (mbar_try(b, parity)) return true;
   const unsigned long long t0 = tc_now();
   while (true) {
     if (mbar_try_sleep(b, parity)) return true;
     if (*abort_flag) return false;
-    if (tc_now() - t0 > KK_WAIT_TIMEOUT_NS) {
+    if (tc_now() - t0 > limit_ns) {
       *abort_flag = 1;
       atomicExch(err, 2);
       return false;
     }
   }
+}
+// Bounded wait of every pipeline barrier: gives up after KK_WAIT_TIMEOUT_NS.
+__device__ __forceinline__ bool mbar_wait(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err) {
+  return mbar_wait_lim(b, parity, abort_flag, err, KK_WAIT_TIMEOUT_NS);
 }
 // mbar_wait that adds the cycles it waited to *acc (when acc is not null).
 __device__ __forceinline__ bool mbar_wait_t(uint64_t* b, uint32_t parity, volatile int* abort_flag, int* err,

@@ -28,6 +28,7 @@ LIB_PATH = os.path.join(HERE, "libkokoro_b200.so")
 KK_OK, KK_ERR_INVALID_ARG, KK_ERR_OOM, KK_ERR_CUDA, KK_ERR_TIMEOUT, KK_ERR_IO = range(6)
 KK_PRECISION_FP32, KK_PRECISION_BF16 = 0, 1
 KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE, KK_OPT_PROFILE, KK_OPT_OUTPUT_PCM16 = 1, 2, 3, 4
+KK_OPT_GAP_CANARY, KK_OPT_NEGCTL_NOMASK = 5, 6
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "TIMEOUT", 5: "IO"}
 
 MAX_PHONEMES = 510  # src/engine.rs:12
@@ -43,6 +44,8 @@ _SIGS = {
     "kk_last_error": (ctypes.c_char_p, [_P]),
     "kk_identity": (ctypes.c_char_p, [_P]),
     "kk_forward_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_forward_batch_noise": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
+    "kk_wait_selftest": (ctypes.c_int, [_P, ctypes.c_int64]),
     "kk_fetch_audio": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64]),
     "kk_decode_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_decode_batch_noalloc": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
@@ -187,11 +190,15 @@ def _ptr(a: Optional[np.ndarray]):
 
 @dataclass
 class ItemNoise:
-    """Per-item excitation noise: a counter stream keyed by ``seed`` (product path) or replayed
-    draws ``sine`` [600 * N * 9] (parity tests) (src/gpu_batch.rs:12-17)."""
+    """Per-item excitation noise (src/gpu_batch.rs:12-17): a counter stream keyed by ``seed``
+    (ItemNoise::Counter, the product path) or, when ``sine`` is set, replayed draws
+    [600 * N * 9] with their initial phases ``rand_ini`` [9] (ItemNoise::Fixed, parity tests). The
+    draw count must match the durations the forward uses, predicted or forced; rand_ini cannot
+    change the output (the reference adds it at a sample its phase downsample never reads)."""
 
     seed: int = 0
     sine: Optional[np.ndarray] = None
+    rand_ini: Optional[np.ndarray] = None
 
 
 @dataclass
@@ -291,6 +298,12 @@ class GpuKokoro:
     def profile_reset(self):
         self.lib.kk_profile_reset(self.h)
 
+    def wait_selftest(self, limit_ns: int = 5000):
+        """Drive the bounded in-kernel wait to expiry on a barrier nothing arrives on
+        (kk_wait_selftest); raises KokoroError with status KK_ERR_TIMEOUT, as a forward whose wait
+        expired would."""
+        self._check(self.lib.kk_wait_selftest(self.h, int(limit_ns)))
+
     def forward_batch(self, items: Sequence[BatchItem], forced_dur: Optional[Sequence[np.ndarray]] = None,
                       fetch: bool = True, pcm16: bool = False) -> List[Output]:
         """Batched ragged forward; results in input order (src/gpu_batch.rs:179-421). pcm16=True
@@ -305,16 +318,26 @@ class GpuKokoro:
                                      np.zeros((0, 256), np.float32))
         speed = np.ascontiguousarray([it.speed for it in items], dtype=np.float32)
         seeds = np.ascontiguousarray([it.noise.seed & ((1 << 64) - 1) for it in items], dtype=np.uint64)
-        noise = None
-        if n and all(it.noise.sine is not None for it in items):
-            noise = np.ascontiguousarray(np.concatenate([np.asarray(it.noise.sine, np.float32) for it in items]))
         fd = None
         if forced_dur is not None:
             fd = np.ascontiguousarray(np.concatenate([np.asarray(d, np.int64) for d in forced_dur]))
         dur = np.zeros(ids.shape[0], np.int64)
         ns = np.zeros(n, np.int64)
-        self._check(self.lib.kk_forward_batch(self.h, n, _ptr(ids), _ptr(lens), _ptr(ref_s), _ptr(speed),
-                                              _ptr(seeds), _ptr(noise), _ptr(fd), _ptr(dur), _ptr(ns)))
+        if any(it.noise.sine is not None for it in items):
+            # per-item ItemNoise (kk_forward_batch_noise): replayed draws where given, counter elsewhere
+            sines = [None if it.noise.sine is None else np.ascontiguousarray(it.noise.sine, np.float32)
+                     for it in items]
+            ptrs = (ctypes.c_void_p * n)(*[None if a is None else a.ctypes.data for a in sines])
+            nlen = np.ascontiguousarray([0 if a is None else a.size for a in sines], dtype=np.int64)
+            ri = np.ascontiguousarray(np.stack([np.zeros(9, np.float32) if it.noise.rand_ini is None else
+                                                np.asarray(it.noise.rand_ini, np.float32).reshape(9)
+                                                for it in items]))
+            self._check(self.lib.kk_forward_batch_noise(self.h, n, _ptr(ids), _ptr(lens), _ptr(ref_s), _ptr(speed),
+                                                        _ptr(seeds), ctypes.cast(ptrs, ctypes.c_void_p), _ptr(nlen),
+                                                        _ptr(ri), _ptr(fd), _ptr(dur), _ptr(ns)))
+        else:
+            self._check(self.lib.kk_forward_batch(self.h, n, _ptr(ids), _ptr(lens), _ptr(ref_s), _ptr(speed),
+                                                  _ptr(seeds), None, _ptr(fd), _ptr(dur), _ptr(ns)))
         outs = []
         o = 0
         for i in range(n):

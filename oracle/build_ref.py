@@ -13,15 +13,25 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 OUT_DIR = os.path.join(HERE, "_ref")
 CUBIN = os.path.join(OUT_DIR, "kokoro_ref.cubin")
-REF_SRC = os.environ.get("KOKORO_REFERENCE", "/root/reference") + "/kernels/kokoro.cu"
+def reference_dir():
+    """The reference checkout: $KOKORO_REFERENCE, else a ``reference`` directory beside this
+    repository; None when neither exists (a GPU box carries only the prebuilt oracle/_ref)."""
+    d = os.environ.get("KOKORO_REFERENCE") or os.path.join(os.path.dirname(os.path.dirname(HERE)), "reference")
+    return d if os.path.isdir(d) else None
+
+
+def ref_src():
+    d = reference_dir()
+    return None if d is None else os.path.join(d, "kernels", "kokoro.cu")
 
 
 def build() -> str:
-    if not os.path.exists(REF_SRC):
-        raise FileNotFoundError(f"reference kernel source not found: {REF_SRC}")
+    src = ref_src()
+    if src is None or not os.path.exists(src):
+        raise FileNotFoundError("reference kernel source not found (set KOKORO_REFERENCE)")
     os.makedirs(OUT_DIR, exist_ok=True)
-    cmd = ["/usr/local/cuda/bin/nvcc", "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-fmad=true",
-           "-O3", REF_SRC, "-o", CUBIN]
+    cmd = [os.environ.get("NVCC", "nvcc"), "-cubin", "-gencode", "arch=compute_100a,code=sm_100a", "-fmad=true",
+           "-O3", src, "-o", CUBIN]
     subprocess.run(cmd, check=True)
     return CUBIN
 

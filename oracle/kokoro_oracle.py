@@ -575,6 +575,7 @@ class KokoroOracle:
         self._rec("nc", n, False)
         t_en = self.text_encoder(ids)
         asr = t_en[src].T.contiguous()
+        self._rec("t_en", t_en, False)
         if noise is None:
             noise = counter_noise(seed, SAMPLES_PER_FRAME * N * HARMONICS)
         audio = self.decode(asr, f0, n, s_dec, noise)
@@ -585,4 +586,14 @@ class KokoroOracle:
             out["dur_q"] = q
         if "f0" in want:
             out["f0"], out["n"] = f0.numpy(), n.numpy()
+        if "asr" in want:  # text encoder output per token [T, 512] and aligned per frame [512, N]
+            out["t_en"], out["asr"] = t_en.numpy(), asr.numpy()
         return out
+
+    @torch.no_grad()
+    def durations(self, ids, ref_s, speed=1.0):
+        """Predicted durations only (src/gpu_batch.rs:216-248, src/model.rs:90-99): (dur, unrounded)."""
+        ids = np.asarray(ids, np.int64)
+        ref_s = np.asarray(ref_s, F32)
+        _d, logits = self.duration_side(ids, torch.from_numpy(ref_s[STYLE_DIM:].copy()), speed)
+        return durations_from_logits(logits.numpy(), speed)

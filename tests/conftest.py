@@ -63,6 +63,33 @@ def oracle(state_dict, oracle_mod):
     return oracle_mod.KokoroOracle(state_dict, threads=min(8, os.cpu_count() or 1))
 
 
+@pytest.fixture(scope="session")
+def bench_mod():
+    """bench.py's workload definitions (config 2's input distributions)."""
+    if ROOT not in sys.path:
+        sys.path.insert(0, ROOT)
+    import bench  # noqa: E402
+
+    return bench
+
+
+def spec_mean_abs_db(a, b, n=1024, hop=256):
+    """G-SPEC (reference tests/common_gates.rs:12-49): periodic Hann 1024, hop 256, frames fully
+    inside, 20 log10(max(|X|, 1e-5)), mean |dB_a - dB_b|."""
+    w = 0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n) / n)
+    frames = 1 + (len(a) - n) // hop
+    fa = np.stack([np.fft.rfft(a[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
+    fb = np.stack([np.fft.rfft(b[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
+    da = 20 * np.log10(np.maximum(np.abs(fa), 1e-5))
+    db = 20 * np.log10(np.maximum(np.abs(fb), 1e-5))
+    return float(np.abs(da - db).mean())
+
+
+@pytest.fixture(scope="session")
+def spec_db():
+    return spec_mean_abs_db
+
+
 def synth_item(rng, n_tokens, style_sd=0.1):
     """Token ids uniform in [1, 177] framed by pad 0, style ~ N(0, 0.1^2)."""
     ids = np.concatenate([[0], rng.integers(1, 178, n_tokens), [0]]).astype(np.int64)

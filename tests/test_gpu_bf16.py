@@ -2,8 +2,9 @@
 accumulation; LSTM recurrence with bf16 hi / lo split operands) against the CPU oracle, end to end.
 
 Bounds, measured on this checkpoint and stated with headroom:
-* predicted integer durations equal the oracle's (ALBERT, text encoder, duration LSTMs in BF16),
-  except where the oracle's unrounded duration lies within 0.02 of a rounding tie;
+* predicted integer durations equal the oracle's (ALBERT, duration LSTMs in BF16), except where
+  the oracle's unrounded duration lies within 0.02 of a rounding tie; every duration, ties included,
+  is within 1 frame of the oracle's;
 * F0 / N curves (the predictor's outputs, forced durations) within 2.5e-2 / 8e-2 relative L2
   (measured about 1.2e-2 / 4e-2: bf16 operands through ALBERT, the predictor LSTMs and the
   AdaIN resblocks; the reference's own mixed-precision build moves F0 by the same order);

@@ -1,18 +1,20 @@
-"""CUDA engine vs the CPU oracle through the C ABI.
+"""CUDA engine vs the CPU oracle through the C ABI (fp32 path, small cases; BASELINE's own
+configurations are in test_gpu_configs.py, batch semantics in test_gpu_batching.py).
 
-fp32 path, per BASELINE's tolerances:
 * vocoder comparison (decoder + generator on identical asr / F0 / N / style / noise inputs):
   waveform max-abs <= 1e-3;
-* full forward: integer durations bit-exact (outside round-half-even ties closer than 1e-4),
-  F0 / N curves within 1e-4 relative L2. The full-forward waveform is compared spectrally:
-  the harmonic source integrates F0 over every sample, so an F0 that differs by fp32
-  accumulation order (~1e-5 relative) moves phases of near-zero STFT bins across the +-pi
-  branch cut; the G-SPEC distance (reference tests/common_gates.rs) bounds that.
+* replayed noise equals the counter stream it was drawn from;
+* full forward with forced durations: the waveform is compared spectrally (G-SPEC < 1 dB): the
+  harmonic source integrates F0 over every sample, so an F0 that differs by fp32 accumulation
+  order (~1e-6 relative) moves phases of near-zero STFT bins across the +-pi branch cut; the
+  G-SPEC distance (reference tests/common_gates.rs) bounds that;
+* predicted integer durations bit-exact outside round-half-even ties closer than 1e-4;
+* memory statistics of a forward and the free-VRAM batch budget built from them.
 """
 import numpy as np
 import pytest
 
-from conftest import synth_item
+from conftest import spec_mean_abs_db, synth_item
 
 pytestmark = pytest.mark.gpu
 
@@ -63,18 +65,6 @@ def test_decode_replayed_noise_matches_counter(kk, eng32, oracle_mod):
     noise = oracle_mod.counter_noise(5, 600 * 7 * 9)
     b = eng32.decode_batch([asr], [f0], [n], s_dec[None], noise=[noise])[0]
     assert np.abs(a - b).max() <= 1e-5
-
-
-def spec_mean_abs_db(a, b, n=1024, hop=256):
-    """G-SPEC (reference tests/common_gates.rs:12-49): periodic Hann 1024, hop 256, frames fully
-    inside, 20 log10(max(|X|, 1e-5)), mean |dB_a - dB_b|."""
-    w = 0.5 - 0.5 * np.cos(2 * np.pi * np.arange(n) / n)
-    frames = 1 + (len(a) - n) // hop
-    fa = np.stack([np.fft.rfft(a[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
-    fb = np.stack([np.fft.rfft(b[f * hop:f * hop + n].astype(np.float64) * w) for f in range(frames)])
-    da = 20 * np.log10(np.maximum(np.abs(fa), 1e-5))
-    db = 20 * np.log10(np.maximum(np.abs(fb), 1e-5))
-    return float(np.abs(da - db).mean())
 
 
 def test_forward_forced_durations(kk, eng32, oracle):

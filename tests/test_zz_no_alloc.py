@@ -2,7 +2,10 @@
 (a streaming audio thread must not wait on cudaMalloc; a GPU shared under a fixed memory budget
 must not let the engine's arena grow). It runs on a static device scratch array, so this test
 checks it against kk_decode_batch on two calls in a row (the second call reuses the scratch the
-first one left behind) and checks that batches above its stated limit are refused."""
+first one left behind), checks that it allocates nothing (the engine's arena stays as it was, at
+zero bytes on an engine that never ran an allocating call, and the device's free memory does not
+move across calls once the library's code is loaded), and checks that batches above its stated
+limit are refused."""
 import numpy as np
 import pytest
 
@@ -57,3 +60,33 @@ def test_noalloc_refuses_batches_above_its_limit(kk, eng):
     got = eng.decode_batch_noalloc(asr, f0, nc, s_dec, seeds=[2])[0]
     ref = eng.decode_batch(asr, f0, nc, s_dec, seeds=[2])[0]
     assert np.abs(got - ref).max() <= TOL
+
+
+def test_noalloc_allocates_nothing(kk, ckpt_path, eng):
+    rng = np.random.default_rng(9)
+    fresh = kk.GpuKokoro(ckpt_path, 0, "bf16")  # an engine that only ever calls the no-allocation entry
+    try:
+        for frames in ([50, 40], [118]):
+            asr, f0, nc, s_dec = inputs(rng, frames)
+            fresh.decode_batch_noalloc(asr, f0, nc, s_dec, seeds=list(range(len(frames))))
+            st = fresh.memory_stats()
+            assert st["arena_bytes"] == 0 and st["peak_bytes"] == 0, st
+        free0, _ = fresh.device_memory()
+        for frames in ([60, 20], [118]):
+            asr, f0, nc, s_dec = inputs(rng, frames)
+            fresh.decode_batch_noalloc(asr, f0, nc, s_dec, seeds=list(range(len(frames))))
+            assert fresh.device_memory()[0] == free0
+        assert fresh.memory_stats()["arena_bytes"] == 0
+    finally:
+        fresh.close()
+    # an engine whose arena already holds a larger call: the no-allocation calls leave it as it is
+    asr, f0, nc, s_dec = inputs(rng, [200, 150])
+    eng.decode_batch(asr, f0, nc, s_dec, seeds=[1, 2])
+    before = eng.memory_stats()
+    free0, _ = eng.device_memory()
+    for frames in ([30, 30, 30], [118]):
+        asr, f0, nc, s_dec = inputs(rng, frames)
+        eng.decode_batch_noalloc(asr, f0, nc, s_dec, seeds=list(range(len(frames))))
+    after = eng.memory_stats()
+    assert after["arena_bytes"] == before["arena_bytes"] and after["peak_bytes"] == before["peak_bytes"]
+    assert eng.device_memory()[0] == free0
