@@ -43,7 +43,8 @@ typedef enum {
 
 typedef enum {
   KK_PRECISION_FP32 = 0, /* fp32 everywhere (SIMT FFMA); the parity path */
-  KK_PRECISION_BF16 = 1  /* bf16 tensor-core (tcgen05) convs and GEMMs, fp32 accumulation */
+  KK_PRECISION_BF16 = 1  /* bf16 tensor-core (tcgen05) convs and GEMMs, fp32 accumulation; the LSTM
+                            recurrence on tensor cores at fp32-level accuracy */
 } kk_precision;
 
 typedef struct kk_engine kk_engine;
@@ -238,10 +239,14 @@ typedef enum {
                                       first filled with NaN, so any element (a gap row above all) that
                                       a kernel reads before writing it poisons the output; outputs
                                       must not change. No counterpart in the reference */
-  KK_OPT_NEGCTL_NOMASK = 6         /* tests, 1 (FP32 mode only): convolutions read the gap rows of
+  KK_OPT_NEGCTL_NOMASK = 6,        /* tests, 1 (FP32 mode only): convolutions read the gap rows of
                                       their input as they are instead of as zeros, the negative control
                                       of the reference's KOKORO_BATCH_NEGCTL_NOMASK
                                       (src/gpu_batch.rs:62-66): batched outputs must then change */
+  KK_OPT_ATTENTION_F32 = 7         /* diagnostics, 1: the BF16 mode runs ALBERT's attention with the fp32
+                                      kernel (the reference's f32 attention, src/gpu.rs:199-230) instead
+                                      of the tcgen05 one, to measure what the bf16 Q / K / V / P of the
+                                      tensor-core attention change. No counterpart in the reference */
 } kk_option;
 KK_API kk_status kk_set_option(kk_engine* e, int option, int64_t value);
 
@@ -320,8 +325,8 @@ KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int3
                                        float* ctx);
 /*
  * kk_lstm_selftest -- diagnostics: one bidirectional LSTM recurrence (hidden 256) over 1 to 32
- * items, on host buffers. tc = 0: the fp32 cluster kernel (both precision modes' semantics);
- * tc = 1: the BF16 mode's tcgen05 recurrence. gx [sum len][2048] gate inputs (W_ih x + b_ih;
+ * items, on host buffers. tc = 0: the fp32 cluster kernel (the FP32 mode's); tc = 1: the BF16 mode's
+ * tcgen05 recurrence (fp32-level accuracy from fp16 split operands; |whh| must stay below 2^15). gx [sum len][2048] gate inputs (W_ih x + b_ih;
  * direction d, gate g (i, f, g, o), unit j at column d*1024 + g*256 + j), whh [2][1024][256],
  * bhh [2][1024]; out [sum len][512] receives h (direction d, unit j at d*256 + j). No counterpart in
  * the reference (kernel-level test of kernels/kokoro.cu:400-450's recurrence).

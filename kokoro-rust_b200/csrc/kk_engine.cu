@@ -232,6 +232,7 @@ struct Lstm {
   Conv ih;  // both directions: cout = 2 * 4H (W_ih fwd | W_ih reverse), bias b_ih
   float* whh = nullptr;
   float* bhh = nullptr;
+  bool f16_ok = false;  // every |W_hh| <= 2^15: the tensor-core recurrence's fp16 split operands hold it
 };
 
 struct Model {
@@ -292,6 +293,7 @@ struct Engine {
   bool pcm16_out = false;                // KK_OPT_OUTPUT_PCM16
   bool gap_canary = false;               // KK_OPT_GAP_CANARY (tests): arena buffers start as NaN
   bool negctl_nomask = false;            // KK_OPT_NEGCTL_NOMASK (tests, FP32 mode): convs read gap rows unmasked
+  bool attn_f32 = false;                 // KK_OPT_ATTENTION_F32 (diagnostics): BF16 mode with the fp32 attention
   int16_t* audio_host16 = nullptr;       // pinned PCM_16 of the last forward
   size_t audio_host16_cap = 0;
   std::vector<long long> out_clipped;    // per item, with KK_OPT_OUTPUT_PCM16
@@ -603,6 +605,9 @@ Lstm Engine::load_lstm(const Checkpoint& ck, const std::string& p, int din) {
   l.ih = conv_from(wih, bih.data(), din, 8 * H, 1, 1, 0, 1);
   l.whh = up(whh);
   l.bhh = up(bhh);
+  float wmax = 0.0f;
+  for (float v : whh) wmax = std::max(wmax, std::fabs(v));
+  l.f16_ok = wmax <= 32768.0f;  // NaN fails the test too
   return l;
 }
 
@@ -1049,7 +1054,7 @@ void Engine::lstm(const Lstm& L, const float* x, int ldx, int rows, const std::v
   a.glen = upload(glen.data(), glen.size());
   a.gact = upload(gact.data(), gact.size());
   a.G = G, a.IPG = IPG, a.Tmax = Tmax;
-  a.tc = precision == KK_PRECISION_BF16 && tc_ok;
+  a.tc = precision == KK_PRECISION_BF16 && tc_ok && L.f16_ok;
   a.err = err_flag;
   cudaEvent_t e0;
   prof_begin(&e0);
@@ -1394,6 +1399,8 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     const size_t planes768 = (size_t)(768 / 64) * 8 * pre_rows * 16;
     void *hpre = nullptr, *ctxpre = nullptr, *apre = nullptr, *fpre = nullptr;
     bool planes = false;
+    // tensor-core attention (BF16 mode); KK_OPT_ATTENTION_F32 keeps the fp32 kernel for comparisons
+    const bool attn_tc = precision == KK_PRECISION_BF16 && tc_ok && !attn_f32;
     auto pre_args = [&](const Conv& c, const void* xp, float* y, int ldy, int out_mode, const float* sc, void* yp) {
       ConvArgs t = ca(c);
       t.in_mode = IN_PRE, t.xpre = xp, t.pre_rows = pre_rows, t.L_in = LT;
@@ -1410,14 +1417,14 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       ConvArgs t1 = pre_args(m.dense, ctxpre, a, 768, OUT_PLUS, h, nullptr);
       ConvArgs t2 = pre_args(m.ffn, apre, nullptr, 0, OUT_GELU_PRE, nullptr, fpre);
       ConvArgs t3 = pre_args(m.ffn_out, fpre, h, 768, OUT_PLUS, a, nullptr);
-      planes = tc_route(m.qkv, t0) && tc_route(m.dense, t1) && tc_route(m.ffn, t2) && tc_route(m.ffn_out, t3);
+      planes = attn_tc && tc_route(m.qkv, t0) && tc_route(m.dense, t1) && tc_route(m.ffn, t2) &&
+               tc_route(m.ffn_out, t3);
     }
     if (!planes) f = ar.get<float>((size_t)LT * 2048);
     linear(m.map_in, emb, 128, LT, h, 768);
     int max_t = 0;
     for (int b = 0; b < B; b++) max_t = std::max(max_t, ids_len[b]);
     // tensor-core attention: (item, first query row) per 128-query tile, in length buckets
-    const bool attn_tc = precision == KK_PRECISION_BF16 && tc_ok;
     int n_work[3] = {0, 0, 0};
     const int2* work_d = nullptr;
     if (attn_tc) {
@@ -2009,6 +2016,7 @@ kk_status kk_set_option(kk_engine* h, int option, int64_t value) {
     else if (option == KK_OPT_PROFILE) h->e->profile = value != 0;
     else if (option == KK_OPT_OUTPUT_PCM16) h->e->pcm16_out = value != 0;
     else if (option == KK_OPT_GAP_CANARY) h->e->gap_canary = value != 0;
+    else if (option == KK_OPT_ATTENTION_F32) h->e->attn_f32 = value != 0;
     else if (option == KK_OPT_NEGCTL_NOMASK) {
       if (value != 0 && h->e->precision != KK_PRECISION_FP32)
         throw kk::KKError(KK_ERR_INVALID_ARG, "the no-mask negative control exists on the FP32 path only");

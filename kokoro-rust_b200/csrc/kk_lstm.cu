@@ -21,6 +21,7 @@
 #include <stdlib.h>
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <string.h>
 
 #include "kk_launch.h"
@@ -199,13 +200,18 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
 
 // ------------------------------------------------------------------------------ tcgen05 variant
 //
-// BF16 precision mode. Same clusters, groups and cell arithmetic; the recurrent product of a step,
-// G[128 gate rows][32 items] = W_hh[rows of this CTA's 32 units][256] x H[256][32 items], runs on
-// the tensor cores with both operands split into bf16 pairs (x = hi + lo, hi = bf16(x),
-// lo = bf16(x - hi)): G = Wh Hh + Wh Hl + Wl Hh accumulated in fp32 in TMEM (the dropped Wl Hl term
-// is below 2^-16 relative). The H image of a step holds Hh in its rows 0..31 and Hl in rows 32..63,
-// so each K step is two MMAs: Wh x [Hh | Hl] (N 64, columns 0..63) and Wl x Hh (N 32, accumulated
-// into columns 0..31); G = columns 0..31 + columns 32..63. A rows are ordered unit * 4 + gate, so
+// BF16 precision mode. Same clusters, groups and cell arithmetic (the fp32 cell functions); the
+// recurrent product of a step, G[128 gate rows][32 items] = W_hh[rows of this CTA's 32 units][256] x
+// H[256][32 items], runs on the tensor cores with fp32-level accuracy by the split-operand method
+// published for tensor cores as "3xTF32" (CUTLASS), here with fp16 halves: each operand is split
+// into a big and a scaled small fp16 part, x = hi + lo / 2^11 with hi = fp16(x) and
+// lo = fp16((x - hi) * 2^11), so hi + lo carries 22 significant bits; the products of fp16 values are
+// exact in the fp32 accumulator, and G = Wh Hh + (Wh Hl + Wl Hh) / 2^11, dropping Wl Hl / 2^22
+// (2^-22 relative, next to fp32's 2^-24 rounding). The scaled small parts keep every piece in fp16's
+// normal range (|h| < 1; the engine routes weights with |W| above 2^15 to the fp32 kernel). The H
+// image of a step holds Hh in its rows 0..31 and Hl in rows 32..63, so each K step is two MMAs:
+// Wh x [Hh | Hl] (N 64, columns 0..63) and Wl x Hh (N 32, accumulated into columns 32..63);
+// G = columns 0..31 + columns 32..63 / 2^11. A rows are ordered unit * 4 + gate, so
 // the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane transpose through shared
 // memory hands each thread one unit's four gates for 4 items. The new h is split into bf16 hi / lo
 // and written into this CTA's 4 KB slice of its own next H image; one bulk copy per other CTA
@@ -219,22 +225,20 @@ constexpr int LT_HROWS = 2 * LC_IPG;             // H image rows: 32 items hi, t
 constexpr int LT_BBYTES = LT_KC * LT_HROWS * 16; // one H image (32 KB)
 constexpr int LT_GXLD = 17;                      // transpose staging row (floats)
 constexpr int LT_SLICE = 4 * LT_HROWS * 16;      // one CTA's 32 units of an H image (4 KB)
-constexpr uint32_t LT_IDESC_HL = idesc_bf16(LT_ROWS, LT_HROWS);  // Wh x [Hh | Hl]
-constexpr uint32_t LT_IDESC_H = idesc_bf16(LT_ROWS, LC_IPG);     // Wl x Hh
+constexpr uint32_t LT_IDESC_HL = idesc_f16(LT_ROWS, LT_HROWS);  // Wh x [Hh | Hl]
+constexpr uint32_t LT_IDESC_H = idesc_f16(LT_ROWS, LC_IPG);     // Wl x Hh
+constexpr float LT_LO_SCALE = 2048.0f;                          // small parts are stored times 2^11
+constexpr float LT_LO_INV = 1.0f / 2048.0f;
 
 __host__ __device__ constexpr size_t lt_smem() {
   return 2 * (size_t)LT_ABYTES + 2 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
 }
 
-__device__ __forceinline__ uint32_t bf16_bits(float x) {
-  __nv_bfloat16 h = __float2bfloat16_rn(x);
-  unsigned short u;
-  memcpy(&u, &h, 2);
-  return u;
+// fp16 bits of x (round to nearest even) and the fp16 bits of its scaled remainder
+__device__ __forceinline__ uint32_t f16_bits(float x) { return (uint32_t)__half_as_ushort(__float2half_rn(x)); }
+__device__ __forceinline__ uint32_t f16_lo_bits(float x, uint32_t hi) {
+  return f16_bits((x - __half2float(__ushort_as_half((unsigned short)hi))) * LT_LO_SCALE);
 }
-__device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
-// tanh x = 2 sigma(2x) - 1 (absolute error about 1e-7, below the split-operand product error)
-__device__ __forceinline__ float tanh_fast(float x) { return fmaf(2.0f, sigm_fast(2.0f * x), -1.0f); }
 
 __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_kernel(const LstmArgs a) {
   extern __shared__ __align__(1024) uint8_t sm8[];
@@ -252,16 +256,15 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   const int dir = cl & 1, g = cl >> 1;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // W_hh rows of this CTA's units as bf16 hi / lo operand images (K-major, 8-row x 16-byte cores)
+  // W_hh rows of this CTA's units as fp16 hi / scaled-lo operand images (K-major, 8-row x 16-byte cores)
   {
     const float* W = a.whh + (size_t)dir * 4 * LC_H * LC_H;
     for (int idx = tid; idx < LT_ROWS * LC_H; idx += 256) {
       const int ar = idx >> 8, k = idx & 255;
       const int u = rank * 32 + (ar >> 2), gate = ar & 3;
       const float w = W[(size_t)(gate * LC_H + u) * LC_H + k];
-      const uint32_t hi = bf16_bits(w);
-      const float whi = __uint_as_float(hi << 16);
-      const uint32_t lo = bf16_bits(w - whi);
+      const uint32_t hi = f16_bits(w);
+      const uint32_t lo = f16_lo_bits(w, hi);
       const size_t off = (size_t)(k >> 3) * (LT_ROWS * 16) + ar * 16 + (k & 7) * 2;
       *reinterpret_cast<unsigned short*>(Ahi + off) = (unsigned short)hi;
       *reinterpret_cast<unsigned short*>(Alo + off) = (unsigned short)lo;
@@ -360,8 +363,8 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       constexpr uint64_t dA = (2 * LT_ROWS * 16) >> 4, dB = (2 * LT_HROWS * 16) >> 4;
 #pragma unroll
       for (int kk = 0; kk < LT_KC / 2; kk++) {
-        mma_bf16(tmem, ah, bd, LT_IDESC_HL, kk > 0);
-        mma_bf16(tmem, al, bd, LT_IDESC_H, 1);
+        mma_bf16(tmem, ah, bd, LT_IDESC_HL, kk > 0);       // Wh x [Hh | Hl] -> columns 0..63
+        mma_bf16(tmem + LC_IPG, al, bd, LT_IDESC_H, 1);    // Wl x Hh -> columns 32..63
         ah += dA, al += dA, bd += dB;
       }
       mma_commit(&bar);
@@ -370,14 +373,15 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
     tc_fence_after();
     __syncthreads();  // bad is uniform from here on
     if (!bad) {
-      // lane (unit 8q + lane / 4, gate lane % 4) reads its 16 items of this half (hi columns and
-      // lo columns), then a 4-lane transpose gives each lane one unit's 4 gates for items i0 .. i0 + 3
+      // lane (unit 8q + lane / 4, gate lane % 4) reads its 16 items of this half (big-part columns
+      // and scaled small-part columns), then a 4-lane transpose gives each lane one unit's 4 gates
+      // for items i0 .. i0 + 3
       float v[16], w[16];
       tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + hf * 16, v);
       tmem_ld16(tmem + ((uint32_t)(q * 32) << 16) + LC_IPG + hf * 16, w);
       float* gw = Gx + warp * 32 * LT_GXLD;
 #pragma unroll
-      for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = v[j] + w[j];
+      for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = fmaf(w[j], LT_LO_INV, v[j]);
       __syncwarp();
 #pragma unroll
       for (int m = 0; m < 4; m++) {
@@ -385,12 +389,12 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
           float d[4];
 #pragma unroll
           for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
-          const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
-          const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
-          const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
-          const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
+          const float ig = sigm(gxv[m][0] + (d[0] + bh[0]));
+          const float fg = sigm(gxv[m][1] + (d[1] + bh[1]));
+          const float cg = tanhf(gxv[m][2] + (d[2] + bh[2]));
+          const float og = sigm(gxv[m][3] + (d[3] + bh[3]));
           c[m] = fg * c[m] + ig * cg;
-          Tile[(i0 + m) * LC_TLD + ul] = og * tanh_fast(c[m]);
+          Tile[(i0 + m) * LC_TLD + ul] = og * tanhf(c[m]);
         }
       }
     }
@@ -405,12 +409,10 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       uint32_t w4[4];
 #pragma unroll
       for (int e = 0; e < 8; e += 2) {
-        uint32_t b0, b1;
-        if (part == 0) {
-          b0 = bf16_bits(hp[e]), b1 = bf16_bits(hp[e + 1]);
-        } else {
-          b0 = bf16_bits(hp[e] - __uint_as_float(bf16_bits(hp[e]) << 16));
-          b1 = bf16_bits(hp[e + 1] - __uint_as_float(bf16_bits(hp[e + 1]) << 16));
+        uint32_t b0 = f16_bits(hp[e]), b1 = f16_bits(hp[e + 1]);
+        if (part == 1) {
+          b0 = f16_lo_bits(hp[e], b0);
+          b1 = f16_lo_bits(hp[e + 1], b1);
         }
         w4[e >> 1] = b0 | (b1 << 16);
       }

@@ -227,6 +227,9 @@ extern "C" KK_API kk_status kk_lstm_selftest(int cuda_ordinal, int tc, int n_ite
   using namespace kk;
   if (n_items < 1 || n_items > LSTM_IPG || !len || !gx || !whh || !bhh || !out)
     return fail(KK_ERR_INVALID_ARG, "bad arguments (1 to 32 items)");
+  if (tc)
+    for (size_t i = 0; i < (size_t)2 * 1024 * 256; i++)
+      if (!(fabsf(whh[i]) <= 32768.0f)) return fail(KK_ERR_INVALID_ARG, "tc = 1 needs |whh| <= 2^15 (fp16 split operands)");
   int rows = 0, Tmax = 0;
   std::vector<int> gstart(LSTM_IPG, 0), glen(LSTM_IPG, 0);
   std::vector<int> order(n_items);

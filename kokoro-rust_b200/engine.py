@@ -28,7 +28,7 @@ LIB_PATH = os.path.join(HERE, "libkokoro_b200.so")
 KK_OK, KK_ERR_INVALID_ARG, KK_ERR_OOM, KK_ERR_CUDA, KK_ERR_TIMEOUT, KK_ERR_IO = range(6)
 KK_PRECISION_FP32, KK_PRECISION_BF16 = 0, 1
 KK_OPT_KEEP_AUDIO_ON_DEVICE, KK_OPT_SYNC_EACH_STAGE, KK_OPT_PROFILE, KK_OPT_OUTPUT_PCM16 = 1, 2, 3, 4
-KK_OPT_GAP_CANARY, KK_OPT_NEGCTL_NOMASK = 5, 6
+KK_OPT_GAP_CANARY, KK_OPT_NEGCTL_NOMASK, KK_OPT_ATTENTION_F32 = 5, 6, 7
 STATUS_NAMES = {0: "OK", 1: "INVALID_ARG", 2: "OOM", 3: "CUDA", 4: "TIMEOUT", 5: "IO"}
 
 MAX_PHONEMES = 510  # src/engine.rs:12

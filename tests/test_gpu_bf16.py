@@ -87,3 +87,35 @@ def test_bf16_vocoder_snr(eng16, oracle, oracle_mod):
         snr = 10 * np.log10((r ** 2).sum() / ((a - r) ** 2).sum())
         print(f"frames {asr.shape[0]}: vocoder SNR {snr:.1f} dB")
         assert a.shape == r.shape and snr >= 40.0
+
+
+def test_bf16_attention_kernel_effect(kk, eng16, cases):
+    """What the tensor-core attention (bf16 Q, K, V, P) changes against the reference's f32
+    attention (src/gpu.rs:199-230), everything else of the BF16 mode equal: durations and F0 against
+    the oracle with each attention kernel (KK_OPT_ATTENTION_F32 selects the fp32 one)."""
+    items, refs = cases
+    res = {}
+    for name, opt in (("tcgen05", 0), ("f32", 1)):
+        eng16.set_option(kk.engine.KK_OPT_ATTENTION_F32, opt)
+        try:
+            outs = eng16.forward_batch(items)
+            d = tempfile.mkdtemp()
+            os.environ["KK_DEBUG_DUMP_DIR"] = d
+            try:
+                eng16.forward_batch(items, forced_dur=[r["dur"] for r in refs])
+            finally:
+                del os.environ["KK_DEBUG_DUMP_DIR"]
+        finally:
+            eng16.set_option(kk.engine.KK_OPT_ATTENTION_F32, 0)
+        f0 = np.fromfile(os.path.join(d, "f0.f32"), np.float32)
+        diff = sum(int((o.pred_dur != r["dur"]).sum()) for o, r in zip(outs, refs))
+        a, e0 = 0, []
+        for r in refs:
+            n = int(r["dur"].sum())
+            rf = r["f0"].reshape(-1)
+            e0.append(float(np.linalg.norm(f0[2 * a:2 * (a + n)] - rf) / np.linalg.norm(rf)))
+            a += n + GAP_N
+        res[name] = (diff, max(e0))
+        print(f"attention {name}: {diff} of {sum(len(r['dur']) for r in refs)} durations differ from the oracle, "
+              f"F0 rel-L2 max {max(e0):.3g}")
+    assert res["tcgen05"][1] <= 2.5e-2 and res["f32"][1] <= 2.5e-2

@@ -2,9 +2,11 @@
 kernels/kokoro.cu:400-450 (gates = gx + (W_hh h + b_hh), order i, f, g, o; c = f c + i g;
 h = o tanh(c); the reverse direction runs each item backwards), on ragged items.
 
-Tolerances (max-abs on h, which lies in (-1, 1)): the fp32 cluster kernel 1e-5 (fp32 rounding over
-up to 100 recurrent steps); the BF16 mode's tcgen05 kernel 2e-3 (bf16 hi / lo split operands keep
-about 16 mantissa bits of each recurrent product, fp32 accumulation).
+Tolerances (max-abs on h, which lies in (-1, 1)): 1e-5 for both kernels. The fp32 cluster kernel
+rounds in fp32 over up to 100 recurrent steps; the BF16 mode's tcgen05 kernel splits both operands
+of the recurrent product into fp16 big and scaled small parts (22 significant bits each, exact
+products, fp32 accumulation: the "3xTF32" split-operand method with fp16 halves), so it must reach
+the same fp32-level error, and the test prints both errors side by side.
 """
 import numpy as np
 import pytest
@@ -33,7 +35,7 @@ def reference(lens, gx, whh, bhh):
     return out
 
 
-@pytest.mark.parametrize("tc,tol", [(0, 1e-5), (1, 2e-3)], ids=["fp32", "tcgen05"])
+@pytest.mark.parametrize("tc,tol", [(0, 1e-5), (1, 1e-5)], ids=["fp32", "tcgen05"])
 def test_lstm_recurrence_matches_reference(kk, tc, tol):
     import kokoro_rust_b200.engine as E
     rng = np.random.default_rng(7)
@@ -45,6 +47,7 @@ def test_lstm_recurrence_matches_reference(kk, tc, tol):
     got = E.lstm_selftest(0, tc, lens, gx, whh, bhh)
     ref = reference(lens, gx, whh, bhh)
     err = np.abs(got - ref).max()
+    print(f"lstm {'tcgen05' if tc else 'fp32'}: max-abs error {err:.3g} against float64")
     assert err <= tol, err
 
 
