@@ -122,6 +122,14 @@ KK_API kk_status kk_forward_batch_noise(kk_engine* e, int n_items, const int64_t
 KK_API kk_status kk_fetch_audio(kk_engine* e, int item, float* dst, int64_t cap);
 
 /*
+ * Copy every item's audio of the last forward at once: item i into dst[i] (capacity cap[i] floats),
+ * on several host threads (the reference's forward_batch returns owned per-item Vec<f32>,
+ * src/gpu_batch.rs:408-420; filling fresh caller buffers is page-fault bound, so the copies of
+ * different items run in parallel). No counterpart in the reference.
+ */
+KK_API kk_status kk_fetch_audio_all(kk_engine* e, float* const* dst, const int64_t* cap);
+
+/*
  * Item `item`'s audio of the last forward run with KK_OPT_OUTPUT_PCM16, as PCM_16 samples
  * (capacity `cap`), and how many of its samples were clipped. The conversion is the reference's WAV
  * rule (src/wav.rs:76-84), done on the GPU so half the bytes cross PCIe. No counterpart in the

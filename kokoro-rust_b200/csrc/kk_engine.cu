@@ -12,6 +12,7 @@
 #include <memory>
 #include <mutex>
 #include <numeric>
+#include <thread>
 #include <string>
 #include <vector>
 
@@ -22,6 +23,37 @@
 #include "kk_weights.h"
 
 namespace kk {
+
+// Copies n[i] bytes from src[i] to dst[i] for every i on up to 8 host threads, split into
+// contiguous runs of items of about equal bytes: the destinations are usually freshly allocated
+// caller arrays, so the page faults of first touch dominate and are served in parallel.
+static void parallel_copy(int count, void* const* dst, const void* const* src, const size_t* n) {
+  size_t total = 0;
+  for (int i = 0; i < count; i++) total += n[i];
+  const size_t per_thread = size_t(8) << 20;  // below 8 MiB a thread is not worth starting
+  int T = (int)std::min<size_t>({size_t(8), (size_t)std::max(1u, std::thread::hardware_concurrency()),
+                                 std::max<size_t>(1, total / per_thread)});
+  if (T <= 1 || count <= 1) {
+    for (int i = 0; i < count; i++) memcpy(dst[i], src[i], n[i]);
+    return;
+  }
+  std::vector<std::thread> th;
+  int first = 0;
+  size_t done = 0;
+  for (int t = 0; t < T && first < count; t++) {
+    const size_t goal = total * (size_t)(t + 1) / (size_t)T;
+    int last = first;
+    size_t acc = done;
+    while (last < count && (acc < goal || last == first)) acc += n[last++];
+    if (t == T - 1) last = count;
+    th.emplace_back([=] {
+      for (int i = first; i < last; i++) memcpy(dst[i], src[i], n[i]);
+    });
+    for (int i = first; i < last; i++) done += n[i];
+    first = last;
+  }
+  for (auto& x : th) x.join();
+}
 
 #define KK_CUDA(expr)                                                                         \
   do {                                                                                        \
@@ -1704,11 +1736,15 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
                              noise_off_d);
   finish_audio(audio, LN, items_h, col_item_d, false);
   if (audio_out && !keep_audio_dev) {
+    std::vector<void*> dst(B);
+    std::vector<const void*> src(B);
+    std::vector<size_t> nb(B);
     long long o = 0;
     for (int b = 0; b < B; b++) {
-      memcpy(audio_out + o, audio_host + out_off[b], sizeof(float) * out_len[b]);
+      dst[b] = audio_out + o, src[b] = audio_host + out_off[b], nb[b] = sizeof(float) * out_len[b];
       o += out_len[b];
     }
+    parallel_copy(B, dst.data(), src.data(), nb.data());
   }
 }
 
@@ -1978,6 +2014,26 @@ kk_status kk_fetch_audio(kk_engine* h, int item, float* dst, int64_t cap) {
     KK_REQUIRE(!e.pcm16_out, "the last forward produced PCM_16 (KK_OPT_OUTPUT_PCM16): use kk_fetch_audio_pcm16");
     KK_REQUIRE(dst && cap >= e.out_len[item], "destination too small");
     memcpy(dst, e.audio_host + e.out_off[item], sizeof(float) * e.out_len[item]);
+  });
+}
+
+kk_status kk_fetch_audio_all(kk_engine* h, float* const* dst, const int64_t* cap) {
+  if (!h) return KK_ERR_INVALID_ARG;
+  return guarded(h, [&] {
+    kk::Engine& e = *h->e;
+    KK_REQUIRE(!e.out_off.empty(), "no forward result");
+    KK_REQUIRE(!e.keep_audio_dev, "audio was kept on the device (KK_OPT_KEEP_AUDIO_ON_DEVICE)");
+    KK_REQUIRE(!e.pcm16_out, "the last forward produced PCM_16 (KK_OPT_OUTPUT_PCM16): use kk_fetch_audio_pcm16");
+    KK_REQUIRE(dst && cap, "null argument");
+    const int B = (int)e.out_off.size();
+    std::vector<void*> d(B);
+    std::vector<const void*> s(B);
+    std::vector<size_t> nb(B);
+    for (int b = 0; b < B; b++) {
+      KK_REQUIRE(dst[b] && cap[b] >= e.out_len[b], "destination too small");
+      d[b] = dst[b], s[b] = e.audio_host + e.out_off[b], nb[b] = sizeof(float) * e.out_len[b];
+    }
+    kk::parallel_copy(B, d.data(), s.data(), nb.data());
   });
 }
 

@@ -47,6 +47,7 @@ _SIGS = {
     "kk_forward_batch_noise": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_wait_selftest": (ctypes.c_int, [_P, ctypes.c_int64]),
     "kk_fetch_audio": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64]),
+    "kk_fetch_audio_all": (ctypes.c_int, [_P, _P, _P]),
     "kk_decode_batch": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_decode_batch_noalloc": (ctypes.c_int, [_P, ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P]),
     "kk_set_option": (ctypes.c_int, [_P, ctypes.c_int, ctypes.c_int64]),
@@ -348,10 +349,13 @@ class GpuKokoro:
                     self._check(self.lib.kk_fetch_audio_pcm16(self.h, i, _ptr(a), a.shape[0], ctypes.byref(clipped)))
             else:
                 a = np.empty(int(ns[i]), np.float32)
-                if fetch:
-                    self._check(self.lib.kk_fetch_audio(self.h, i, _ptr(a), a.shape[0]))
             outs.append(Output(a, dur[o:o + lens[i]].copy(), int(clipped.value)))
             o += lens[i]
+        if fetch and not pcm16 and n:
+            # every item's audio in one call (the library copies items on several threads)
+            dst = (ctypes.c_void_p * n)(*[o_.audio.ctypes.data for o_ in outs])
+            cap = np.ascontiguousarray(ns, dtype=np.int64)
+            self._check(self.lib.kk_fetch_audio_all(self.h, ctypes.cast(dst, ctypes.c_void_p), _ptr(cap)))
         return outs
 
     def decode_batch(self, asr: Sequence[np.ndarray], f0: Sequence[np.ndarray], n_curve: Sequence[np.ndarray],

@@ -90,6 +90,21 @@ def spec_db():
     return spec_mean_abs_db
 
 
+def gspec_floor(oracle_mod, state_dict, ids, ref_s, seed, dur):
+    """The floor pair of the reference's G-SPEC gate (tests/common_gates.rs:1-10: a result passes at
+    <= 2 x the distance between two runs of the same CPU implementation that differ only in thread
+    count): the oracle at 1 thread and at the fixture's thread count on the same forced-duration
+    input. Returns (floor dB, the multi-threaded oracle's output)."""
+    import torch
+    threads = min(8, os.cpu_count() or 1)
+    outs = []
+    for th in (1, threads):
+        outs.append(oracle_mod.KokoroOracle(state_dict, threads=th).forward(ids, ref_s, 1.0, seed=seed, forced_dur=dur,
+                                                                           want=("f0", "asr")))
+    torch.set_num_threads(threads)
+    return spec_mean_abs_db(outs[0]["audio"], outs[1]["audio"]), outs[1]
+
+
 def synth_item(rng, n_tokens, style_sd=0.1):
     """Token ids uniform in [1, 177] framed by pad 0, style ~ N(0, 0.1^2)."""
     ids = np.concatenate([[0], rng.integers(1, 178, n_tokens), [0]]).astype(np.int64)
