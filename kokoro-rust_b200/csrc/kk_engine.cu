@@ -305,9 +305,11 @@ static const int SPEC_LD = 24;
 static const int POST_LD = 24;
 static inline int ld16(int c) { return (c + 3) & ~3; }  // row stride of a c-channel f32 buffer
 // Layers with more output channels than this pre-transform their input once (IN_PRE) instead of
-// in the conv's producer warps (which redo it for every 128-channel output tile). Measured on B200:
-// at 256 channels the two routes are within 10% of each other (the extra bf16 pass costs about
-// what the second transform does); from 512 channels on the pre-transform route is 1.7x faster.
+// in the conv's producer warps (which redo it for every 128-channel output tile); so do the K <= 3
+// layers of exactly this many. Measured on B200 (kk_conv_selftest, 300,000 rows): at 256 channels
+// with K = 3 the pre-transform route is 10% faster (its MMAs are too few to hide two transforms per
+// input element), with K = 7 / 11 the fused route is 9-13% faster; from 512 channels on the
+// pre-transform route is 1.7x faster.
 static const int TC_PRE_MIN_COUT = 256;
 
 struct Engine {
@@ -878,7 +880,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       tr = ar.get<unsigned long long>(16);
       KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
     }
-    if (c.cout > TC_PRE_MIN_COUT && a.in_mode != IN_PRE) {
+    if ((c.cout > TC_PRE_MIN_COUT || (c.cout == TC_PRE_MIN_COUT && c.K <= 3)) && a.in_mode != IN_PRE) {
       // several 128-channel output tiles share each input window: transform the input once into
       // bf16 window planes instead of once per output tile
       auto mk = ar.mark();

@@ -90,19 +90,33 @@ def spec_db():
     return spec_mean_abs_db
 
 
-def gspec_floor(oracle_mod, state_dict, ids, ref_s, seed, dur):
-    """The floor pair of the reference's G-SPEC gate (tests/common_gates.rs:1-10: a result passes at
-    <= 2 x the distance between two runs of the same CPU implementation that differ only in thread
-    count): the oracle at 1 thread and at the fixture's thread count on the same forced-duration
-    input. Returns (floor dB, the multi-threaded oracle's output)."""
+def config1():
+    """64 ids uniform in [1, 177] from numpy's default_rng(0) framed by pad 0, the
+    256-d style N(0, 0.1^2) from the same generator after the ids, durations forced to [0, 3 x 64, 0]
+    (192 frames, 115,200 samples)."""
+    rng = np.random.default_rng(0)
+    ids = np.concatenate([[0], rng.integers(1, 178, 64), [0]]).astype(np.int64)
+    ref_s = (rng.standard_normal(256) * 0.1).astype(np.float32)
+    dur = np.array([0] + [3] * 64 + [0], np.int64)
+    return ids, ref_s, dur
+
+
+@pytest.fixture(scope="session")
+def gspec(oracle_mod, state_dict):
+    """The reference's G-SPEC gate (tests/common_gates.rs:1-10): a full-forward waveform passes at a
+    mean |dB| distance of at most twice the floor pair's, the floor pair being two runs of the same
+    CPU implementation that differ only in thread count (1 and 8) on one fixed floor case. The
+    floor case here is BASELINE config 1 (counter noise seed 0). Returns {"floor": dB, "gate": dB,
+    "config1": the 8-thread oracle's config-1 output (audio, durations, F0 / N, t_en / asr)}."""
     import torch
     threads = min(8, os.cpu_count() or 1)
-    outs = []
-    for th in (1, threads):
-        outs.append(oracle_mod.KokoroOracle(state_dict, threads=th).forward(ids, ref_s, 1.0, seed=seed, forced_dur=dur,
-                                                                           want=("f0", "asr")))
+    ids, ref_s, dur = config1()
+    outs = [oracle_mod.KokoroOracle(state_dict, threads=th).forward(ids, ref_s, 1.0, seed=0, forced_dur=dur,
+                                                                    want=("f0", "asr"))
+            for th in (1, threads)]
     torch.set_num_threads(threads)
-    return spec_mean_abs_db(outs[0]["audio"], outs[1]["audio"]), outs[1]
+    floor = spec_mean_abs_db(outs[0]["audio"], outs[1]["audio"])
+    return {"floor": floor, "gate": 2.0 * floor, "config1": outs[1]}
 
 
 def synth_item(rng, n_tokens, style_sd=0.1):

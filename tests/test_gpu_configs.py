@@ -7,10 +7,11 @@
   - full forward: F0 / N curves within 1e-4 relative L2, the text encoder output ``t_en`` and its
     frame alignment ``asr`` within 1e-4 relative L2 (the reference's ``text_encoder_b``,
     src/gpu_batch.rs:457-481), waveform under the reference's G-SPEC gate: at most twice the
-    spectral distance between two oracle runs that differ only in thread count (the gate's floor
-    pair, tests/common_gates.rs:1-10). The waveform itself drifts in phase: an F0 that differs in
-    the sixth digit (accumulation order) moves the phase of near-zero STFT bins across +-pi, which
-    the noise convolutions consume; the oracle against itself at 1 and 8 threads shows the same;
+    spectral distance between two oracle runs on this case that differ only in thread count (the
+    gate's floor pair, tests/common_gates.rs:1-10; config 1 is the floor case). The waveform itself
+    drifts in phase: an F0 that differs in the sixth digit (accumulation order) moves the phase of
+    near-zero STFT bins across +-pi, which the noise convolutions consume; the oracle against
+    itself at 1 and 8 threads shows the same;
   - BF16 mode: ``t_en`` / ``asr`` within 2e-2 relative L2 (bf16 conv operands, fp32 LayerNorm,
     the split-operand LSTM recurrence).
 * Config 2's shape: 4 items of T = 400 frames with config 2's input distributions (the bench's
@@ -29,25 +30,12 @@ pytestmark = pytest.mark.gpu
 FP32_TOL = 1e-3
 
 
-def config1():
-    rng = np.random.default_rng(0)
-    ids = np.concatenate([[0], rng.integers(1, 178, 64), [0]]).astype(np.int64)
-    ref_s = (rng.standard_normal(256) * 0.1).astype(np.float32)
-    dur = np.array([0] + [3] * 64 + [0], np.int64)
-    return ids, ref_s, dur
+from conftest import config1
 
 
 @pytest.fixture(scope="module")
-def c1_floor(oracle_mod, state_dict):
-    """(G-SPEC floor dB, the oracle's config-1 output)."""
-    from conftest import gspec_floor
-    ids, ref_s, dur = config1()
-    return gspec_floor(oracle_mod, state_dict, ids, ref_s, 0, dur)
-
-
-@pytest.fixture(scope="module")
-def c1_ref(c1_floor):
-    return c1_floor[1]
+def c1_ref(gspec):
+    return gspec["config1"]
 
 
 @pytest.fixture(scope="module")
@@ -94,7 +82,7 @@ def test_config1_vocoder_fp32(eng32, c1_ref):
     assert err <= FP32_TOL
 
 
-def test_config1_forward_fp32(kk, eng32, c1_ref, c1_floor, spec_db):
+def test_config1_forward_fp32(kk, eng32, c1_ref, gspec, spec_db):
     ids, ref_s, dur = config1()
     out, load = forward_dumps(kk, eng32, ids, ref_s, dur)
     assert out.audio.shape == (115_200,) and np.array_equal(out.pred_dur, dur)
@@ -104,13 +92,12 @@ def test_config1_forward_fp32(kk, eng32, c1_ref, c1_floor, spec_db):
     e_ten = rel_l2(load("t_en")[:T], c1_ref["t_en"])
     e_asr = rel_l2(load("xcat0")[:N, :512], c1_ref["asr"].T)
     d = spec_db(out.audio, c1_ref["audio"])
-    floor = c1_floor[0]
     print(f"config 1 forward fp32: F0 {e_f0:.3g} N {e_n:.3g} t_en {e_ten:.3g} asr {e_asr:.3g} (rel-L2), "
-          f"spectral {d:.3f} dB (G-SPEC floor pair {floor:.3f} dB, gate {2 * floor:.3f} dB), "
+          f"spectral {d:.3f} dB (G-SPEC floor pair {gspec['floor']:.3f} dB, gate {gspec['gate']:.3f} dB), "
           f"max-abs {np.abs(out.audio - c1_ref['audio']).max():.3g}")
     assert e_f0 <= 1e-4 and e_n <= 1e-4
     assert e_ten <= 1e-4 and e_asr <= 1e-4
-    assert d <= 2.0 * floor
+    assert d <= gspec["gate"]
 
 
 def test_config1_text_encoder_bf16(kk, eng16, c1_ref):
