@@ -506,9 +506,13 @@ __global__ void adain_pool_kernel(const float* x, int C, int L, ConvArgs p, cons
 // The same AdaIN + leaky + depthwise transposed conv for the AdaIN-leaky prologue, organised by
 // input row: thread = channel, block = 32 consecutive input rows. Each input value is transformed
 // once (instead of once per output that reads it) and feeds output rows 2i (tap 1), 2i - 1 (tap 0)
-// and 2i + 1 (tap 2); the item's AdaIN terms stay in registers while the item is unchanged. The
-// arithmetic of every output is the one above, operation for operation.
+// and 2i + 1 (tap 2); the item's AdaIN terms stay in registers while the item is unchanged. Rows
+// go in chunks of 8: the items and input values of a chunk's 9 rows (8 + the next one) are all
+// loaded before any is used, so each thread has 9 loads in flight instead of one (the pass is bound
+// by memory latency otherwise). The arithmetic of every output is the one above, operation for
+// operation.
 constexpr int POOL_RB = 32;
+constexpr int POOL_CH = 8;  // rows per chunk
 __global__ void __launch_bounds__(256) adain_pool_rows_kernel(const float* __restrict__ x, int C, int L, ConvArgs p,
                                                               const float* __restrict__ pw,
                                                               const float* __restrict__ pb, float* __restrict__ y,
@@ -520,33 +524,48 @@ __global__ void __launch_bounds__(256) adain_pool_rows_kernel(const float* __res
   const float nw = p.nw[c], nb = p.nb[c];
   int cached = -1;
   float mean = 0.0f, rstd = 0.0f, g1 = 0.0f, gc = 0.0f;
-  auto u_of = [&](int i) -> float {  // pool_in(p, x, L, i, c)
-    if (i < 0 || i >= L) return 0.0f;
-    const int b = dom_item(p.din, i);
-    if (b < 0) return 0.0f;
-    if (b != cached) {
-      cached = b;
-      mean = p.mean[b * C + c];
-      rstd = p.rstd[b * C + c];
-      const float* g = p.gb + (long)b * p.ldgb;
-      g1 = 1.0f + g[c];
-      gc = g[C + c];
+  for (int k0 = 0; k0 < POOL_RB && i0 + k0 < L; k0 += POOL_CH) {
+    int bv[POOL_CH + 1];
+    float xv[POOL_CH + 1];
+#pragma unroll
+    for (int u = 0; u <= POOL_CH; u++) {
+      const int i = i0 + k0 + u;
+      bv[u] = i < L ? dom_item(p.din, i) : -1;
     }
-    float v = x[(long)i * p.ldx + c];
-    v = (v - mean) * rstd;
-    v = g1 * (v * nw + nb) + gc;
-    return leaky(v, p.slope);
-  };
-  float uc = u_of(i0);
-  for (int k = 0; k < POOL_RB; k++) {
-    const int i = i0 + k;
-    if (i >= L) break;
-    const float un = u_of(i + 1);
-    y[(long)(2 * i) * ldy + c] = fmaf(w1, uc, bias);
-    float acc = fmaf(w2, uc, bias);
-    acc = fmaf(w0, un, acc);
-    y[(long)(2 * i + 1) * ldy + c] = acc;
-    uc = un;
+#pragma unroll
+    for (int u = 0; u <= POOL_CH; u++) {
+      const int i = i0 + k0 + u;
+      xv[u] = bv[u] >= 0 ? x[(long)i * p.ldx + c] : 0.0f;
+    }
+    float uu[POOL_CH + 1];  // pool_in(p, x, L, i, c) of the chunk's rows
+#pragma unroll
+    for (int u = 0; u <= POOL_CH; u++) {
+      const int b = bv[u];
+      if (b < 0) {
+        uu[u] = 0.0f;
+        continue;
+      }
+      if (b != cached) {
+        cached = b;
+        mean = p.mean[b * C + c];
+        rstd = p.rstd[b * C + c];
+        const float* g = p.gb + (long)b * p.ldgb;
+        g1 = 1.0f + g[c];
+        gc = g[C + c];
+      }
+      float v = (xv[u] - mean) * rstd;
+      v = g1 * (v * nw + nb) + gc;
+      uu[u] = leaky(v, p.slope);
+    }
+#pragma unroll
+    for (int u = 0; u < POOL_CH; u++) {
+      const int i = i0 + k0 + u;
+      if (i >= L) break;
+      y[(long)(2 * i) * ldy + c] = fmaf(w1, uu[u], bias);
+      float acc = fmaf(w2, uu[u], bias);
+      acc = fmaf(w0, uu[u + 1], acc);
+      y[(long)(2 * i + 1) * ldy + c] = acc;
+    }
   }
 }
 
