@@ -234,6 +234,7 @@ class PinnedArena {
 
 struct Conv {
   int cin = 0, cout = 0, K = 1, dil = 1, pad = 0, stride = 1;
+  bool simt_only = false;  // always the fp32 kernel (the per-item style projections: one row per item)
   double macs_per_row = 0;  // algorithmic multiply-adds per output row
   float* w = nullptr;  // fp32 [K][cin][cout]
   float* b = nullptr;
@@ -311,6 +312,12 @@ static inline int ld16(int c) { return (c + 3) & ~3; }  // row stride of a c-cha
 // input element), with K = 7 / 11 the fused route is 9-13% faster; from 512 channels on the
 // pre-transform route is 1.7x faster.
 static const int TC_PRE_MIN_COUT = 256;
+// The token and frame layouts hold at least this many rows (trailing gap rows make up the rest):
+// the tensor-core path takes layers of 64 rows or more, so in BF16 mode every layer runs the same
+// arithmetic whatever the size of the batch (a one-item batch of a short line would otherwise run
+// its token-domain layers on the fp32 kernel and give a different result than the same line in a
+// larger batch).
+static const int MIN_LAYOUT_ROWS = 64;
 
 struct Engine {
   int dev = 0;
@@ -783,9 +790,11 @@ void Engine::load(const Checkpoint& ck) {
     for (int j = 0; j < 3; j++)
       m.rb[i * 3 + j] = load_snake(ck, g + ".resblocks." + std::to_string(i * 3 + j), 512 >> (i + 1), ks[j], fdw, fdb);
   m.post = load_conv(ck, g + ".conv_post", 128, 22, 7, 1, 3, 1, true);
-  // fused style projections
+  // fused style projections: one row per item, so in fp32 on the SIMT kernel whatever the batch
+  // size (the tensor-core path would take them only for batches of 64 items or more)
   m.fc_dec = conv_from(fdw, fdb.data(), 128, (int)fdb.size(), 1, 1, 0, 1);
   m.fc_pro = conv_from(fpw, fpb.data(), 128, (int)fpb.size(), 1, 1, 0, 1);
+  m.fc_dec.simt_only = m.fc_pro.simt_only = true;
   KK_CUDA(upload_stft_constants(st));
   KK_CUDA(cudaStreamSynchronize(st));
 }
@@ -868,7 +877,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   // algorithmic bytes: f32 input rows read once, output rows written once (read too when
   // accumulated into), shortcut rows read once, weights once (bf16 image or f32)
   const bool res = a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS;
-  const bool tc_path = precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc);
+  const bool tc_path = tc_route(c, a);
   const double in_rows = a.in_up2 ? (double)((a.L_in + 1) / 2) : (double)a.L_in;
   // bf16 window planes in or out: 2 bytes per element
   const double in_b = a.in_mode == IN_PRE ? 2.0 : 4.0, out_b = a.out_mode == OUT_GELU_PRE ? 2.0 : 4.0;
@@ -924,7 +933,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
 }
 
 bool Engine::tc_route(const Conv& c, const ConvArgs& a) const {
-  return precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && tc_supported(a, c.tc);
+  return precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && !c.simt_only && tc_supported(a, c.tc);
 }
 
 // Run a convolution and produce the AdaIN statistics of its output [L_out][cout] (ldy == cout):
@@ -1380,6 +1389,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     LT += ids_len[b] + GAP_T;
     last_tokens += ids_len[b];
   }
+  LT = std::max(LT, MIN_LAYOUT_ROWS);
   std::vector<int> row_item_h(LT, -1), ids_h(LT, 0);
   {
     long long o = 0;
@@ -1579,6 +1589,7 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     items_h[b].n = (int)n;
     LN += (int)n + GAP_N;
   }
+  LN = std::max(LN, MIN_LAYOUT_ROWS);
   last_frames = 0;
   for (int b = 0; b < B; b++) last_frames += items_h[b].n;
   if (noise)
@@ -1685,6 +1696,7 @@ void Engine::decode(int B, const int32_t* n_frames, const float* asr, const floa
     LN += n_frames[b] + GAP_N;
     tot += n_frames[b];
   }
+  LN = std::max(LN, MIN_LAYOUT_ROWS);
   last_tokens = 0;
   last_frames = tot;
   KK_CUDA(cudaSetDevice(dev));
@@ -1798,6 +1810,7 @@ void Engine::decode_noalloc(int B, const int32_t* n_frames, const float* asr, co
     tot += n_frames[b];
     max_n = std::max(max_n, n_frames[b]);
   }
+  LN = std::max(LN, MIN_LAYOUT_ROWS);  // as kk_decode_batch lays out the same call
   last_tokens = 0;
   last_frames = tot;
   KK_CUDA(cudaSetDevice(dev));

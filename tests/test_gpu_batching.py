@@ -149,3 +149,19 @@ def test_bounded_wait_expires_and_engine_recovers(kk, eng32, eng16, precision):
     for a, b in zip(after, before):
         assert np.isfinite(a.audio).all()
         assert np.abs(a.audio - b.audio).max() <= (0.0 if precision == "fp32" else 1e-3)
+
+
+def test_batch_vs_single_bf16(kk, eng16):
+    """BF16 mode: every layer runs the same arithmetic whatever the batch (the layouts hold at
+    least 64 rows, so no layer of a small batch falls back to the fp32 kernel; the style
+    projections are fp32 for every batch). Durations are equal; the audio differs only through the
+    fused AdaIN sums, which group rows by tile (last-bit changes of the statistics)."""
+    items, durs = three_items(kk)
+    single = eng16.forward_batch([items[1]], forced_dur=[durs[1]])[0]
+    batch = eng16.forward_batch(items, forced_dur=durs)
+    d = float(np.abs(batch[1].audio - single.audio).max())
+    print(f"bf16 batch vs single: max-abs {d:.3g}")
+    assert d <= 1e-3
+    p1 = eng16.forward_batch([items[1]])[0]
+    pb = eng16.forward_batch(items)
+    assert np.array_equal(pb[1].pred_dur, p1.pred_dur)
