@@ -155,13 +155,17 @@ def test_batch_vs_single_bf16(kk, eng16):
     """BF16 mode: every layer runs the same arithmetic whatever the batch (the layouts hold at
     least 64 rows, so no layer of a small batch falls back to the fp32 kernel; the style
     projections are fp32 for every batch). Durations are equal; the audio differs only through the
-    fused AdaIN sums, which group rows by tile (last-bit changes of the statistics)."""
+    fused AdaIN sums of the tensor-core epilogue, which group rows by absolute tile: a last-bit
+    change of a statistic flips the bf16 rounding of a few convolution inputs, a bf16-sized
+    perturbation, so the bound is the BF16 mode's own (SNR >= 40 dB)."""
     items, durs = three_items(kk)
     single = eng16.forward_batch([items[1]], forced_dur=[durs[1]])[0]
     batch = eng16.forward_batch(items, forced_dur=durs)
-    d = float(np.abs(batch[1].audio - single.audio).max())
-    print(f"bf16 batch vs single: max-abs {d:.3g}")
-    assert d <= 1e-3
+    r = single.audio.astype(np.float64)
+    err = float(((batch[1].audio - r) ** 2).sum())
+    snr = 10 * np.log10((r ** 2).sum() / err) if err > 0 else float("inf")
+    print(f"bf16 batch vs single: max-abs {np.abs(batch[1].audio - r).max():.3g}, SNR {snr:.1f} dB")
+    assert snr >= 40.0
     p1 = eng16.forward_batch([items[1]])[0]
     pb = eng16.forward_batch(items)
     assert np.array_equal(pb[1].pred_dur, p1.pred_dur)
