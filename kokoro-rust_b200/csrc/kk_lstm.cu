@@ -330,18 +330,11 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   const uint32_t tmem = tslot;
   volatile int abort_flag = 0;
   uint32_t hph[2] = {0, 0};  // phase parity of each H-image barrier
-  cluster_sync();  // every CTA of the cluster is running and initialised before remote stores
-
-  for (int s = 0; s < a.Tmax; s++) {
+  // gate inputs of this thread's cells for step s (items still running at s); loaded one step
+  // ahead, so their latency hides behind the previous step's exchange and product
+  float gxv[4][4];
+  auto load_gx = [&](int s) {
     const int na = act[s];
-    if (na == 0) break;  // same for the whole group, so for every CTA of the cluster
-    const int cur = s & 1;
-    if (s > 0) {  // this step's H image: all 8 CTAs' slices of step s - 1 have landed
-      if (!bad && !mbar_wait(&hbar[cur], hph[cur], &abort_flag, a.err)) bad = 1;
-      hph[cur] ^= 1;
-    }
-    // gate inputs of this thread's cells, loaded ahead of the product
-    float gxv[4][4];
 #pragma unroll
     for (int m = 0; m < 4; m++) {
 #pragma unroll
@@ -352,6 +345,18 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
 #pragma unroll
         for (int gt = 0; gt < 4; gt++) gxv[m][gt] = __ldg(gp + gt * LC_H);
       }
+    }
+  };
+  if (a.Tmax > 0) load_gx(0);
+  cluster_sync();  // every CTA of the cluster is running and initialised before remote stores
+
+  for (int s = 0; s < a.Tmax; s++) {
+    const int na = act[s];
+    if (na == 0) break;  // same for the whole group, so for every CTA of the cluster
+    const int cur = s & 1;
+    if (s > 0) {  // this step's H image: all 8 CTAs' slices of step s - 1 have landed
+      if (!bad && !mbar_wait(&hbar[cur], hph[cur], &abort_flag, a.err)) bad = 1;
+      hph[cur] ^= 1;
     }
     if (tid == 0 && !bad) {
       fence_proxy_async();  // the H image arrived through generic-proxy stores
@@ -398,6 +403,7 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
         }
       }
     }
+    if (s + 1 < a.Tmax) load_gx(s + 1);  // consumed by the next step's cells
     // re-arm image `cur` (consumed this step) for the pushes of step s + 1, before the barrier that
     // releases this CTA's own step-s pushes: no CTA can push step s + 1 before it has received them
     if (tid == 0 && !bad && push_bytes(s + 1)) mbar_arrive_expect_tx(&hbar[cur], push_bytes(s + 1));
