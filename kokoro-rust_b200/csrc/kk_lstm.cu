@@ -330,11 +330,10 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   const uint32_t tmem = tslot;
   volatile int abort_flag = 0;
   uint32_t hph[2] = {0, 0};  // phase parity of each H-image barrier
-  // gate inputs of this thread's cells for step s (items still running at s); loaded one step
-  // ahead, so their latency hides behind the previous step's exchange and product
+  // gate inputs of this thread's cells for step s (items still running at s), loaded while the
+  // step's MMAs run: after the MMA issue, so the issuing thread's proxy fence does not wait on them
   float gxv[4][4];
-  auto load_gx = [&](int s) {
-    const int na = act[s];
+  auto load_gx = [&](int s, int na) {
 #pragma unroll
     for (int m = 0; m < 4; m++) {
 #pragma unroll
@@ -347,7 +346,6 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       }
     }
   };
-  if (a.Tmax > 0) load_gx(0);
   cluster_sync();  // every CTA of the cluster is running and initialised before remote stores
 
   for (int s = 0; s < a.Tmax; s++) {
@@ -374,6 +372,7 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
       }
       mma_commit(&bar);
     }
+    load_gx(s, na);
     if (!bad && !mbar_wait(&bar, (uint32_t)(s & 1), &abort_flag, a.err)) bad = 1;
     tc_fence_after();
     __syncthreads();  // bad is uniform from here on
@@ -403,7 +402,6 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
         }
       }
     }
-    if (s + 1 < a.Tmax) load_gx(s + 1);  // consumed by the next step's cells
     // re-arm image `cur` (consumed this step) for the pushes of step s + 1, before the barrier that
     // releases this CTA's own step-s pushes: no CTA can push step s + 1 before it has received them
     if (tid == 0 && !bad && push_bytes(s + 1)) mbar_arrive_expect_tx(&hbar[cur], push_bytes(s + 1));
