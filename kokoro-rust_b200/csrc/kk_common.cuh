@@ -142,15 +142,4 @@ __device__ __forceinline__ float gelu_new(float a) {
   return 0.5f * a * (1.0f + tanhf(c * (a + 0.044715f * a * a * a)));
 }
 
-// gelu_new for a result that is rounded to bf16 right after (the ALBERT FFN's bf16 operand planes):
-// tanh u = 1 - 2 / (1 + e^(2u)) with the hardware exp and divide, within about 1e-7 absolute of
-// tanhf (the rounding step of the result near 1 is 6e-8), three orders of magnitude below the
-// bf16 rounding step it feeds; saturates to +-1 for large |u|.
-__device__ __forceinline__ float gelu_new_for_bf16(float a) {
-  const float c = 0.797884560802865355f;
-  const float u = c * (a + 0.044715f * a * a * a);
-  const float t = 1.0f - __fdividef(2.0f, 1.0f + __expf(2.0f * u));
-  return 0.5f * a * (1.0f + t);
-}
-
 }  // namespace kk

@@ -510,17 +510,25 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           if (trc) t_res += clock64() - tq, tq = clock64();
           if (out_mode == OUT_GELU_PRE) {
             // bf16 window planes for the next layer: lane l holds channel co0 + l, which is element
-            // 4 * h + l % 4 of chunk l / 4 of 64-channel block co0 / 64 (h = 32-channel half); each
-            // lane stores its own 2 bytes, four lanes filling one 8-byte run of a plane row
+            // 4 * h + l % 4 of chunk l / 4 of 64-channel block co0 / 64 (h = 32-channel half); four
+            // lanes make one 8-byte store per row
             const int h = (co0 >> 5) & 1;
             uint8_t* pl = (uint8_t*)a.ypre + ((size_t)((co0 >> 6) * 8 + (lane >> 2)) * a.ypre_rows + PRE_PAD_FRONT) * 16 +
-                          h * 8 + (lane & 3) * 2;
+                          h * 8;
 #pragma unroll
             for (int jj = 0; jj < TC_EC; jj++) {
-              const float r = gelu_new_for_bf16(v[sub * TC_EC + jj] + bias);
+              const float r = gelu_new(v[sub * TC_EC + jj] + bias);
+              const float r1 = __shfl_down_sync(0xffffffffu, r, 1);
+              const float r2 = __shfl_down_sync(0xffffffffu, r, 2);
+              const float r3 = __shfl_down_sync(0xffffffffu, r, 3);
               const int t = t0 + c * TC_EC + jj;
-              if (t < L_out && co0 < a.cout)
-                *reinterpret_cast<__nv_bfloat16*>(pl + (size_t)t * 16) = __float2bfloat16_rn(r);
+              if ((lane & 3) == 0 && t < L_out && co0 < a.cout) {
+                __nv_bfloat162 p0 = __floats2bfloat162_rn(r, r1), p1 = __floats2bfloat162_rn(r2, r3);
+                uint2 u;
+                memcpy(&u.x, &p0, 4);
+                memcpy(&u.y, &p1, 4);
+                *reinterpret_cast<uint2*>(pl + (size_t)t * 16) = u;
+              }
             }
             continue;
           }
