@@ -366,9 +366,11 @@ def main():
         torch.cuda.set_device(local_rank)
         dist.init_process_group("nccl", timeout=__import__("datetime").timedelta(seconds=600),
                                 device_id=torch.device("cuda", local_rank))
-    if rank == 0:
+    if local_rank == 0:
+        # one process per node writes the node's checkpoint file and brings the library up to date,
+        # before the node's other ranks read or load them
         kk.weights.write_random_checkpoint(ckpt, 0)
-        if world > 1:  # the library is brought up to date by one rank, before the others load it
+        if world > 1:
             kk.engine.load_library()
     if world > 1:
         dist.barrier()
