@@ -155,9 +155,12 @@ def test_batch_vs_single_bf16(kk, eng16):
     """BF16 mode: every layer runs the same arithmetic whatever the batch (the layouts hold at
     least 64 rows, so no layer of a small batch falls back to the fp32 kernel; the style
     projections are fp32 for every batch). Durations are equal; the audio differs only through the
-    fused AdaIN sums of the tensor-core epilogue, which group rows by absolute tile: a last-bit
-    change of a statistic flips the bf16 rounding of a few convolution inputs, a bf16-sized
-    perturbation, so the bound is the BF16 mode's own (SNR >= 40 dB)."""
+    fused AdaIN sums of the tensor-core epilogue, which add f32 partial sums of absolute 128-row
+    tiles: a last-bit change of a statistic flips the bf16 rounding of a few convolution inputs, a
+    bf16-sized perturbation, so the bound is the BF16 mode's own (SNR >= 40 dB). The reference's own
+    BF16x product depends on the batch composition too, durations included
+    (docs/design/BATCHING.md:7-13); element-wise f64 sums would make this mode batch-invariant bit
+    for bit (measured) at 4-5 ms per config-4 forward, and are not used."""
     items, durs = three_items(kk)
     single = eng16.forward_batch([items[1]], forced_dur=[durs[1]])[0]
     batch = eng16.forward_batch(items, forced_dur=durs)
@@ -169,3 +172,15 @@ def test_batch_vs_single_bf16(kk, eng16):
     p1 = eng16.forward_batch([items[1]])[0]
     pb = eng16.forward_batch(items)
     assert np.array_equal(pb[1].pred_dur, p1.pred_dur)
+
+
+def test_bf16_reproducible_across_runs(kk, eng16):
+    """The same batch twice gives the same audio bit for bit (the reference's reproducibility gate,
+    tests/bf16x_regression.rs:35-46): every reduction of the path has a fixed order, and the AdaIN
+    sums' f64 accumulation of f32 partials does not depend on the order of the atomic adds."""
+    items, durs = three_items(kk)
+    a = eng16.forward_batch(items)
+    b = eng16.forward_batch(items)
+    for x, y in zip(a, b):
+        assert np.array_equal(x.pred_dur, y.pred_dur)
+        assert np.array_equal(x.audio, y.audio)
