@@ -385,8 +385,11 @@ def main():
     toks = None
     if args.workload in ("config4", "config3", "config5"):
         if args.workload == "config4":
-            # 251 lines per rank: 251 x N lines built once, LPT-sharded by tokens (N = 1: all 251)
-            all_toks, style = config4_lines(seed=1000, n_lines=251 * world)
+            # 251 lines per rank: 251 x N lines built once, LPT-sharded by tokens (N = 1: all 251);
+            # the style (one voice per file) is config 4's at every N, so the per-rank work does
+            # not change with N (the generator draws the style after the lines)
+            all_toks, _ = config4_lines(seed=1000, n_lines=251 * world)
+            _, style = config4_lines(seed=1000)
             mine = rank_shard(all_toks, world, rank)
             workload_desc = ("config4: full ragged forward, 251 synthetic lines per rank (lognormal lengths median "
                              "110 sigma 0.6 clamped [8,510]; 251 x N lines LPT-sharded by tokens), predicted "
