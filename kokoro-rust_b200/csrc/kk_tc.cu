@@ -507,6 +507,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             if (__any_sync(0xffffffffu, !got)) bad = true;
             rr = rsb + sl * TC_EC * 32;
           }
+          const uint32_t rrl = smem_u32(rr) + 4u * lane;
           if (trc) t_res += clock64() - tq, tq = clock64();
           if (out_mode == OUT_GELU_PRE) {
             // bf16 window planes for the next layer: lane l holds channel co0 + l, which is element
@@ -533,6 +534,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             continue;
           }
           float* sb = stg + (c & 1) * TC_EC * 32;
+          const uint32_t sbl = smem_u32(sb) + 4u * lane;
           if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
           __syncwarp();
           if (trc) t_stbuf += clock64() - tq;
@@ -540,11 +542,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
 #pragma unroll
           for (int jj = 0; jj < TC_EC; jj++) {
             float r = v[sub * TC_EC + jj] + bias;
-            if (out_mode == OUT_ADD) r = rr[jj * 32 + lane] + r;
-            else if (out_mode == OUT_PLUS) r = (r + rr[jj * 32 + lane]) * oscale;
+            if (out_mode == OUT_ADD) r = lds_f32(rrl + 128u * jj) + r;
+            else if (out_mode == OUT_PLUS) r = (r + lds_f32(rrl + 128u * jj)) * oscale;
             else if (out_mode == OUT_GELU) r = gelu_new(r);
             vals[jj] = r;
-            sb[jj * 32 + lane] = r;
+            sts_f32(sbl + 128u * jj, r);
           }
           if (stat) {
             if (single) {
@@ -618,7 +620,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       const InSpan sp = in_span(p, tile, in_up2, BOXR);
       const int bf = lt & 1;
       if (!mbar_wait_t(&meta_full[bf], (lt >> 1) & 1, abort_flag, p.err, trc ? &tpw : nullptr)) break;
-      const int* ri = ritem + bf * TC_MAX_WIN;
+      const uint32_t ri = smem_u32(ritem + bf * TC_MAX_WIN);
       const float2* ct = ctab + bf * TC_TAB;
       const int titem = tab ? mitem[bf] : -1;
       for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
@@ -627,7 +629,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           ok = false;
           break;
         }
-        uint8_t* xb = xbuf + xs * xbytes + (size_t)j * 16 * p.win_pad;
+        const uint32_t xb = smem_u32(xbuf + xs * xbytes) + (uint32_t)j * 16u * (uint32_t)p.win_pad;
         // this thread's 8 channels: chA .. chA + 3 and chA + 32 .. chA + 35
         const int chA = cb * TC_KB + 4 * j;
         int chs[8];
@@ -676,7 +678,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         }
         // prologue of one window row r from the 8 input values v, stored as bf16
         auto emit = [&](int r, const float (&v)[8]) {
-          const int b = ri[r];
+          const int b = lds_s32(ri + 4u * (uint32_t)r);
           float o[8];
           if (b < 0) {
 #pragma unroll
@@ -718,7 +720,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           memcpy(&pk.y, &h1, 4);
           memcpy(&pk.z, &h2, 4);
           memcpy(&pk.w, &h3, 4);
-          *reinterpret_cast<uint4*>(xb + (size_t)r * 16) = pk;
+          sts_u4(xb + (uint32_t)r * 16u, pk);
         };
         for (int i = 0; i < sp.nbox; i++) {
           const int sl = in_sl;
@@ -727,12 +729,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             break;
           }
           if (++in_sl == RST) in_sl = 0, in_ph ^= 1;
-          const float* box = (const float*)(inring + sl * INBOX);
+          const uint32_t box = smem_u32(inring + sl * INBOX) + (uint32_t)(prow * TC_KB + 4 * j) * 4u;
 #pragma unroll
           for (int hh = 0; hh < BOXR / TC_PROWS; hh++) {
             const int br = prow + TC_PROWS * hh;
-            const float4 lo = *reinterpret_cast<const float4*>(box + br * TC_KB + 4 * j);
-            const float4 hi = *reinterpret_cast<const float4*>(box + br * TC_KB + 32 + 4 * j);
+            const float4 lo = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB) * 4u);
+            const float4 hi = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB + 32) * 4u);
             const float v[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
             if (!up2) {
               const int r = i * BOXR + br;
