@@ -159,8 +159,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   volatile int* abort_flag = (volatile int*)(tmem_slot + 1);
   int* mitem = (int*)(tmem_slot + 2);                         // [2] item whose coefficients ctab holds
   int* ritem = (int*)(tmem_slot + 4);                         // [2][TC_MAX_WIN] item of each window row
-  float2* ctab = (float2*)(ritem + 2 * TC_MAX_WIN);           // [2][TC_TAB] AdaIN (scale, shift) of mitem
-  float2* atab = ctab + 2 * TC_TAB;                           // [TC_TAB] Snake (alpha, 1 / alpha)
+  // The coefficient tables are pair-interleaved: channels 2i and 2i + 1 as one float4 {scale0, scale1,
+  // shift0, shift1} ({alpha0, alpha1, 1 / alpha0, 1 / alpha1}), so a producer's 16-byte load yields the
+  // register pairs its packed f32x2 arithmetic takes.
+  float* ctab = (float*)(ritem + 2 * TC_MAX_WIN);             // [2][TC_TAB] AdaIN (scale, shift) of mitem
+  float* atab = ctab + 2 * 2 * TC_TAB;                        // [TC_TAB] Snake (alpha, 1 / alpha)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ntiles = p.n_cot * p.n_tt;
@@ -371,7 +374,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         av[k] = c < cin ? a.alpha[c] : 1.0f;
       }
 #pragma unroll
-      for (int k = 0; k < TC_TAB / 32; k++) atab[lane + 32 * k] = make_float2(av[k], 1.0f / av[k]);
+      for (int k = 0; k < TC_TAB / 32; k++) {
+        const int c = lane + 32 * k;
+        atab[(c >> 1) * 4 + (c & 1)] = av[k];
+        atab[(c >> 1) * 4 + 2 + (c & 1)] = 1.0f / av[k];
+      }
     }
     uint32_t lt = 0;
     for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, lt++) {
@@ -398,9 +405,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           const int c = lane + 32 * k;
           cv[k] = (item >= 0 && c < cin) ? a.coef[(long)item * cin + c] : make_float2(0.0f, 0.0f);
         }
-        float2* ct = ctab + bf * TC_TAB;
+        float* ct = ctab + bf * 2 * TC_TAB;
 #pragma unroll
-        for (int k = 0; k < TC_TAB / 32; k++) ct[lane + 32 * k] = cv[k];
+        for (int k = 0; k < TC_TAB / 32; k++) {
+          const int c = lane + 32 * k;
+          ct[(c >> 1) * 4 + (c & 1)] = cv[k].x;
+          ct[(c >> 1) * 4 + 2 + (c & 1)] = cv[k].y;
+        }
         if (lane == 0) mitem[bf] = item;
       }
       __syncwarp();
@@ -621,7 +632,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       const int bf = lt & 1;
       if (!mbar_wait_t(&meta_full[bf], (lt >> 1) & 1, abort_flag, p.err, trc ? &tpw : nullptr)) break;
       const uint32_t ri = smem_u32(ritem + bf * TC_MAX_WIN);
-      const float2* ct = ctab + bf * TC_TAB;
+      const uint32_t ct = smem_u32(ctab + bf * 2 * TC_TAB);
       const int titem = tab ? mitem[bf] : -1;
       for (int cb = 0; cb < p.ncb && ok; cb++, xit++) {
         const int xs = xit % XST;
@@ -635,22 +646,22 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         int chs[8];
 #pragma unroll
         for (int e = 0; e < 8; e++) chs[e] = chA + (e < 4 ? e : 28 + e);
-        float al[8], ial[8], ca[8], cbb[8];
+        // channel pairs q = 0 .. 3: (chA, chA + 1), (chA + 2, chA + 3), (chA + 32, chA + 33), (chA + 34, chA + 35)
+        float2 al[4], ial[4], ca[4], cbb[4];
         int cached = -1;
         if (snake) {
-          if (tab) {  // (alpha, 1 / alpha) of chA .. chA + 3 and chA + 32 .. chA + 35: 4 x 16 bytes
+          if (tab) {  // (alpha, 1 / alpha) of the four pairs: 4 x 16 bytes
 #pragma unroll
-            for (int h = 0; h < 2; h++)
-#pragma unroll
-              for (int e2 = 0; e2 < 4; e2 += 2) {
-                const float4 q4 = *reinterpret_cast<const float4*>(atab + chA + 32 * h + e2);
-                al[4 * h + e2] = q4.x, ial[4 * h + e2] = q4.y, al[4 * h + e2 + 1] = q4.z, ial[4 * h + e2 + 1] = q4.w;
-              }
+            for (int q = 0; q < 4; q++) {
+              const float4 q4 = lds_f4(smem_u32(atab) + (uint32_t)((chs[2 * q] >> 1) * 16));
+              al[q] = make_float2(q4.x, q4.y), ial[q] = make_float2(q4.z, q4.w);
+            }
           } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-              al[e] = chs[e] < cin ? a.alpha[chs[e]] : 1.0f;
-              ial[e] = 1.0f / al[e];
+              const float av = chs[e] < cin ? a.alpha[chs[e]] : 1.0f;
+              (e & 1 ? al[e >> 1].y : al[e >> 1].x) = av;
+              (e & 1 ? ial[e >> 1].y : ial[e >> 1].x) = 1.0f / av;
             }
           }
         }
@@ -658,17 +669,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
         auto load_coef = [&](int b) {
           if (tab && b == titem) {
 #pragma unroll
-            for (int h = 0; h < 2; h++)
-#pragma unroll
-              for (int e2 = 0; e2 < 4; e2 += 2) {
-                const float4 q4 = *reinterpret_cast<const float4*>(ct + chA + 32 * h + e2);
-                ca[4 * h + e2] = q4.x, cbb[4 * h + e2] = q4.y, ca[4 * h + e2 + 1] = q4.z, cbb[4 * h + e2 + 1] = q4.w;
-              }
+            for (int q = 0; q < 4; q++) {
+              const float4 q4 = lds_f4(ct + (uint32_t)((chs[2 * q] >> 1) * 16));
+              ca[q] = make_float2(q4.x, q4.y), cbb[q] = make_float2(q4.z, q4.w);
+            }
           } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) {
               const float2 q2 = chs[e] < cin ? coef[(long)b * cin + chs[e]] : make_float2(0.0f, 0.0f);
-              ca[e] = q2.x, cbb[e] = q2.y;
+              (e & 1 ? ca[e >> 1].y : ca[e >> 1].x) = q2.x;
+              (e & 1 ? cbb[e >> 1].y : cbb[e >> 1].x) = q2.y;
             }
           }
         };
@@ -691,12 +701,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             // packed f32x2 arithmetic (each lane rounds exactly like the scalar fmaf / multiply)
 #pragma unroll
             for (int e = 0; e < 8; e += 2) {
-              float2 t = __ffma2_rn(make_float2(v[e], v[e + 1]), make_float2(ca[e], ca[e + 1]),
-                                    make_float2(cbb[e], cbb[e + 1]));
+              float2 t = __ffma2_rn(make_float2(v[e], v[e + 1]), ca[e >> 1], cbb[e >> 1]);
               if (snake) {
-                const float2 arg = __fmul2_rn(make_float2(al[e], al[e + 1]), t);
+                const float2 arg = __fmul2_rn(al[e >> 1], t);
                 const float2 sn = make_float2(__sinf(arg.x), __sinf(arg.y));
-                t = __ffma2_rn(make_float2(ial[e], ial[e + 1]), __fmul2_rn(sn, sn), t);
+                t = __ffma2_rn(ial[e >> 1], __fmul2_rn(sn, sn), t);
               } else {
                 t.x = leaky(t.x, slope);
                 t.y = leaky(t.y, slope);
