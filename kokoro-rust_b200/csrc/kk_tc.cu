@@ -443,9 +443,20 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     double* const stat = a.stat;
     uint32_t lt = 0;
     bool bad = false;
+    // Items of the first (lane 0) and last (lane 1) of a tile's 128 rows, loaded one tile ahead so
+    // the item-table latency hides behind the previous tile's work. Equal ends mean one item
+    // covers all 128 rows (item spans are contiguous runs); only tiles that straddle an item
+    // boundary or the end build the per-row table.
+    auto edge_item = [&](int tl) {
+      const int r = (tl / p.n_cot) * TC_N + hrow + (lane == 0 ? 0 : TC_EROWS - 1);
+      return (stat && lane < 2 && tl < ntiles && r < L_out) ? dom_item(a.dout, r) : -1;
+    };
+    int edge_next = edge_item(blockIdx.x);
     for (int tile = blockIdx.x; tile < ntiles && !bad; tile += gridDim.x, lt++) {
       const int ab = lt & 1;
       const int cot = tile % p.n_cot, tt = tile / p.n_cot;
+      const int edge = edge_next;
+      edge_next = edge_item(tile + gridDim.x);
       const int co0 = cot * TC_M + q * 32;
       const int co = co0 + lane;
       const int t0 = tt * TC_N + hrow;
@@ -462,14 +473,21 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
       int s_item = -1;
       bool single = false;
       if (stat) {
-        for (int rr = lane; rr < TC_EROWS; rr += 32) {
-          const int t = t0 + rr;
-          eit[rr] = t < L_out ? dom_item(a.dout, t) : -1;
+        const int first = __shfl_sync(0xffffffffu, edge, 0), last = __shfl_sync(0xffffffffu, edge, 1);
+        single = first >= 0 && first == last;
+        if (single) {
+          s_item = first;
+        } else {
+          int iv[TC_EROWS / 32];
+#pragma unroll
+          for (int k = 0; k < TC_EROWS / 32; k++) {
+            const int t = t0 + lane + 32 * k;
+            iv[k] = t < L_out ? dom_item(a.dout, t) : -1;
+          }
+#pragma unroll
+          for (int k = 0; k < TC_EROWS / 32; k++) eit[lane + 32 * k] = iv[k];
+          __syncwarp();
         }
-        __syncwarp();
-        // item spans are contiguous runs, so equal end rows mean one item covers all 128 rows
-        single = eit[0] >= 0 && eit[0] == eit[TC_EROWS - 1];
-        if (single) s_item = eit[0];
       }
       float s_sum = 0.0f, s_sq = 0.0f;
       auto s_flush = [&]() {
