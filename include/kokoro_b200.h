@@ -332,6 +332,13 @@ KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_case* c, const
 KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len, const float* qkv,
                                        float* ctx);
 /*
+ * kk_attention_selftest_bf16 -- the same attention over bf16 qkv rows (bit patterns, 2 bytes per
+ * element), the form the BF16 mode's QKV projection writes. Rows rounded to bf16 to nearest even
+ * give the same ctx as kk_attention_selftest on the f32 rows, bit for bit.
+ */
+KK_API kk_status kk_attention_selftest_bf16(int cuda_ordinal, int n_items, const int32_t* tok_len,
+                                            const uint16_t* qkv, float* ctx);
+/*
  * kk_lstm_selftest -- diagnostics: one bidirectional LSTM recurrence (hidden 256) over 1 to 32
  * items, on host buffers. tc = 0: the fp32 cluster kernel (the FP32 mode's); tc = 1: the BF16 mode's
  * tcgen05 recurrence (fp32-level accuracy from fp16 split operands; |whh| must stay below 2^15). gx [sum len][2048] gate inputs (W_ih x + b_ih;

@@ -2,9 +2,9 @@
 //
 // Per item and head (src/gpu_batch.rs:429-442: scores = Q K^T per head, softmax(scale * scores) over
 // the item's own T tokens, ctx = P V), one CTA of 4 warps handles a tile of 128 query rows:
-//  1. Q (128 x 64), K (Tp x 64) and V^T (64 x Tp) of the head are read from the f32 qkv rows, rounded
-//     to bf16 and stored in the canonical no-swizzle K-major operand layout (Tp = T rounded up to 16,
-//     rows past T are zero);
+//  1. Q (128 x 64), K (Tp x 64) and V^T (64 x Tp) of the head are read from the qkv rows (f32, rounded
+//     to bf16 here, or bf16 rows the QKV projection already rounded the same way) and stored in the
+//     canonical no-swizzle K-major operand layout (Tp = T rounded up to 16, rows past T are zero);
 //  2. one elected thread issues S = Q K^T (M 128, N <= 256 per instruction, K 64) into TMEM;
 //  3. thread r owns query row r = TMEM lane r: it reads its S row from TMEM twice (row maximum, then
 //     p = exp(scale * s - max) in fp32 with the fp32 row sum), and writes P as bf16 over the Q / K
@@ -29,6 +29,11 @@ namespace {
 constexpr int ATT_D = 64;       // head dimension
 constexpr int ATT_HEADS = 12;
 constexpr int ATT_QT = 128;     // query rows per CTA (TMEM lanes)
+// V^T operand: 16-byte rows of 8 keys, 8 dims per core matrix. The 8-dim groups sit 144 bytes
+// apart (128 + 16 of padding, a legal descriptor stride), so eight threads storing the same row of
+// eight consecutive groups hit eight different bank groups; a key chunk spans 8 groups.
+constexpr int ATT_VSB = 144;
+constexpr int ATT_VKC = 8 * ATT_VSB;
 
 __device__ __forceinline__ uint4 pack8_bf16(const float* v) {
   uint4 pk;
@@ -49,18 +54,19 @@ __host__ __device__ constexpr int att_preg() {  // bytes of the P region (Q and 
 }
 template <int TMAX>
 __host__ __device__ constexpr int att_smem() {
-  return att_preg<TMAX>() + TMAX * ATT_D * 2;
+  return att_preg<TMAX>() + (TMAX / 8) * ATT_VKC;
 }
 
-template <int TMAX>
-__global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict__ qkv, int ld, const ItemTab* items,
+// BF: the qkv rows are bf16 (ld in elements); else f32.
+template <int TMAX, bool BF>
+__global__ void __launch_bounds__(128, 1) attn_tc_kernel(const void* __restrict__ qkv, int ld, const ItemTab* items,
                                                          const int2* work, float* ctx, int ldc, int* err,
                                                          uint8_t* ctx_pre, long ctx_pre_rows) {
   extern __shared__ __align__(1024) uint8_t smem[];
   uint8_t* Qs = smem;                          // [8 dim chunks][128 rows][8] bf16
   uint8_t* Ks = smem + 16384;                  // [8 dim chunks][TMAX keys][8]
   uint8_t* Ps = smem;                          // [TMAX / 8 key chunks][128 rows][8] (after S)
-  uint8_t* Vt = smem + att_preg<TMAX>();       // [TMAX / 8 key chunks][64 dims][8 keys]
+  uint8_t* Vt = smem + att_preg<TMAX>();       // [TMAX / 8 key chunks][8 dim groups, ATT_VSB apart][8 dims][8 keys]
   __shared__ uint64_t bar;
   __shared__ uint32_t tslot;
   __shared__ int bad;
@@ -71,7 +77,8 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
   const int T = it.tok_len, q0 = wk.y;
   const int Tp = (T + 15) & ~15;
   const int tid = threadIdx.x, warp = tid >> 5;
-  const float* base = qkv + (long)it.tok_start * ld + h * ATT_D;
+  const float* base = (const float*)qkv + (long)it.tok_start * ld + h * ATT_D;
+  const unsigned short* baseh = (const unsigned short*)qkv + (long)it.tok_start * ld + h * ATT_D;
 
   if (tid == 0) {
     mbar_init(&bar, 1);
@@ -102,21 +109,62 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
       *reinterpret_cast<uint4*>(dst + c * stride + row * 16) = pack8_bf16(v);
     }
   };
-  {
-    float4 rv[16];
-    load_row(q0 + tid, 0, rv);
-    store_row(Qs, ATT_QT * 16, tid, rv);
-  }
-  for (int j = tid; j < Tp; j += 128) {
-    float4 rv[16];
-    load_row(j, 768, rv);
-    store_row(Ks, TMAX * 16, j, rv);
+  // bf16 rows: 8 dims per 16-byte load, already the operand's 16-byte chunk
+  auto copy_row_h = [&](uint8_t* dst, int stride, int row, int drow, int off) {
+    const uint4* p = reinterpret_cast<const uint4*>(baseh + (long)row * ld + off);
+    uint4 rv[8];
+#pragma unroll
+    for (int c = 0; c < 8; c++) rv[c] = row < T ? __ldg(p + c) : make_uint4(0u, 0u, 0u, 0u);
+#pragma unroll
+    for (int c = 0; c < 8; c++) *reinterpret_cast<uint4*>(dst + c * stride + drow * 16) = rv[c];
+  };
+  if constexpr (BF) {
+    copy_row_h(Qs, ATT_QT * 16, q0 + tid, tid, 0);
+    for (int j = tid; j < Tp; j += 128) copy_row_h(Ks, TMAX * 16, j, j, 768);
+  } else {
+    {
+      float4 rv[16];
+      load_row(q0 + tid, 0, rv);
+      store_row(Qs, ATT_QT * 16, tid, rv);
+    }
+    for (int j = tid; j < Tp; j += 128) {
+      float4 rv[16];
+      load_row(j, 768, rv);
+      store_row(Ks, TMAX * 16, j, rv);
+    }
   }
   // V^T: task (key chunk kc, dim d): 8 keys of one dim -> one 16-byte store (a warp covers 32
   // consecutive dims of one key chunk: coalesced loads, conflict-free stores); 4 tasks per thread
   // in flight
   const int ntask = (Tp / 8) * ATT_D;
-  for (int t0 = 0; t0 < ntask; t0 += 4 * 128) {
+  if constexpr (BF) {
+    // task (key chunk kc, dim group dc): eight 16-byte loads (8 dims of 8 keys; the eight threads of a
+    // key chunk read whole 128-byte rows), an 8 x 8 transpose by byte permutes, eight 16-byte
+    // stores (8 keys of one dim each)
+    const int nt = (Tp / 8) * 8;
+#pragma unroll 2
+    for (int t = tid; t < nt; t += 128) {
+      const int dc = t & 7, kc = t >> 3;
+      uint4 in[8];
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        const int j = kc * 8 + e;
+        in[e] = j < T ? __ldg(reinterpret_cast<const uint4*>(baseh + (long)j * ld + 1536 + dc * 8))
+                      : make_uint4(0u, 0u, 0u, 0u);
+      }
+      uint8_t* dst = Vt + kc * ATT_VKC + dc * ATT_VSB;
+      auto wd = [](const uint4& v, int w) { return w == 0 ? v.x : (w == 1 ? v.y : (w == 2 ? v.z : v.w)); };
+#pragma unroll
+      for (int dd = 0; dd < 8; dd++) {
+        const int w = dd >> 1;
+        const uint32_t sel = (dd & 1) ? 0x7632u : 0x5410u;  // high or low bf16 of each word
+        *reinterpret_cast<uint4*>(dst + dd * 16) =
+            make_uint4(__byte_perm(wd(in[0], w), wd(in[1], w), sel), __byte_perm(wd(in[2], w), wd(in[3], w), sel),
+                       __byte_perm(wd(in[4], w), wd(in[5], w), sel), __byte_perm(wd(in[6], w), wd(in[7], w), sel));
+      }
+    }
+  }
+  for (int t0 = 0; !BF && t0 < ntask; t0 += 4 * 128) {
     float v[4][8];
 #pragma unroll
     for (int u = 0; u < 4; u++) {
@@ -130,7 +178,8 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
 #pragma unroll
     for (int u = 0; u < 4; u++) {
       const int t = t0 + u * 128 + tid, kc = t / ATT_D, d = t % ATT_D;
-      if (t < ntask) *reinterpret_cast<uint4*>(Vt + kc * (ATT_D * 16) + d * 16) = pack8_bf16(v[u]);
+      if (t < ntask)
+        *reinterpret_cast<uint4*>(Vt + kc * ATT_VKC + (d >> 3) * ATT_VSB + (d & 7) * 16) = pack8_bf16(v[u]);
     }
   }
   fence_proxy_async();
@@ -195,7 +244,7 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
     const uint32_t id = idesc_bf16(ATT_QT, ATT_D);
     for (int kk = 0; kk < Tp / 16; kk++) {
       const uint64_t ad = sdesc(smem_u32(Ps) + kk * 2 * (ATT_QT * 16), ATT_QT * 16, 128);
-      const uint64_t bd = sdesc(smem_u32(Vt) + kk * 2 * (ATT_D * 16), ATT_D * 16, 128);
+      const uint64_t bd = sdesc(smem_u32(Vt) + kk * 2 * ATT_VKC, ATT_VKC, ATT_VSB);
       mma_bf16(tmem, ad, bd, id, kk > 0);
     }
     mma_commit(&bar);
@@ -245,37 +294,47 @@ __global__ void __launch_bounds__(128, 1) attn_tc_kernel(const float* __restrict
   }
 }
 
-template <int TMAX>
-cudaError_t launch_bucket(const float* qkv, int ld, const ItemTab* items, const int2* work, int n, float* ctx, int ldc,
+template <int TMAX, bool BF>
+cudaError_t launch_bucket(const void* qkv, int ld, const ItemTab* items, const int2* work, int n, float* ctx, int ldc,
                           int* err, cudaStream_t st, void* ctx_pre, long ctx_pre_rows) {
   if (n == 0) return cudaSuccess;
   static bool attr[64] = {false};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 64 && !attr[dev]) {
-    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<TMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+    cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<TMAX, BF>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          att_smem<TMAX>());
     if (e != cudaSuccess) return e;
     attr[dev] = true;
   }
-  attn_tc_kernel<TMAX><<<dim3(n, ATT_HEADS), 128, att_smem<TMAX>(), st>>>(qkv, ld, items, work, ctx, ldc, err,
-                                                                           (uint8_t*)ctx_pre, ctx_pre_rows);
+  attn_tc_kernel<TMAX, BF><<<dim3(n, ATT_HEADS), 128, att_smem<TMAX>(), st>>>(qkv, ld, items, work, ctx, ldc, err,
+                                                                               (uint8_t*)ctx_pre, ctx_pre_rows);
   return cudaGetLastError();
+}
+
+template <bool BF>
+cudaError_t launch_buckets(const void* qkv, int ldqkv, const ItemTab* items, const int2* work, const int n_work[3],
+                           float* ctx, int ldc, int* err, cudaStream_t st, void* ctx_pre, long ctx_pre_rows) {
+  cudaError_t e = launch_bucket<128, BF>(qkv, ldqkv, items, work, n_work[0], ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
+  if (e == cudaSuccess)
+    e = launch_bucket<256, BF>(qkv, ldqkv, items, work + n_work[0], n_work[1], ctx, ldc, err, st, ctx_pre,
+                               ctx_pre_rows);
+  if (e == cudaSuccess)
+    e = launch_bucket<512, BF>(qkv, ldqkv, items, work + n_work[0] + n_work[1], n_work[2], ctx, ldc, err, st, ctx_pre,
+                               ctx_pre_rows);
+  return e;
 }
 
 }  // namespace
 
-cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
+cudaError_t launch_attention_tc(const void* qkv, int ldqkv, bool qkv_bf16, const ItemTab* items, const int2* work,
                                 const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st, void* ctx_pre,
                                 long ctx_pre_rows) {
   if (ctx_pre && (((uintptr_t)ctx_pre) & 15) != 0) return cudaErrorInvalidValue;
-  cudaError_t e = launch_bucket<128>(qkv, ldqkv, items, work, n_work[0], ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
-  if (e == cudaSuccess)
-    e = launch_bucket<256>(qkv, ldqkv, items, work + n_work[0], n_work[1], ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
-  if (e == cudaSuccess)
-    e = launch_bucket<512>(qkv, ldqkv, items, work + n_work[0] + n_work[1], n_work[2], ctx, ldc, err, st, ctx_pre,
-                           ctx_pre_rows);
-  return e;
+  // 16-byte row loads: bf16 rows need a 16-byte aligned base and a row stride of 8 elements
+  if (qkv_bf16 && ((((uintptr_t)qkv) & 15) != 0 || ldqkv % 8 != 0)) return cudaErrorInvalidValue;
+  return qkv_bf16 ? launch_buckets<true>(qkv, ldqkv, items, work, n_work, ctx, ldc, err, st, ctx_pre, ctx_pre_rows)
+                  : launch_buckets<false>(qkv, ldqkv, items, work, n_work, ctx, ldc, err, st, ctx_pre, ctx_pre_rows);
 }
 
 }  // namespace kk

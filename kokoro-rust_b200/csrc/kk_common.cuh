@@ -64,8 +64,10 @@ enum OutMode : int {
   OUT_ADD = 1,       // y += acc + bias
   OUT_PLUS = 2,      // y = ((acc + bias) + sc) * oscale
   OUT_GELU = 3,      // y = gelu_new(acc + bias)
-  OUT_GELU_PRE = 4   // gelu_new(acc + bias) written as bf16 window planes (ypre), the IN_PRE input of a
+  OUT_GELU_PRE = 4,  // gelu_new(acc + bias) written as bf16 window planes (ypre), the IN_PRE input of a
                      // following layer, instead of f32 rows (tensor-core path, cout a multiple of 64)
+  OUT_STORE_BF = 5   // acc + bias rounded to bf16 rows (y holds __nv_bfloat16; tensor-core path, no
+                     // statistics): the attention's Q / K / V, which it rounds to bf16 anyway
 };
 
 struct ConvArgs {

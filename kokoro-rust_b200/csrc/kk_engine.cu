@@ -405,6 +405,7 @@ struct Engine {
   ConvArgs ca(const Conv& c);
   void run_conv(const Conv& c, ConvArgs& a);
   bool tc_route(const Conv& c, const ConvArgs& a) const;
+  bool tc_pre(const Conv& c, const ConvArgs& a) const;
   void run_conv_stats(const Conv& c, ConvArgs& a, const Dom& dout, const ItemTab* items, int B, int max_len,
                       float** mean, float** rstd);
   void stats(const float* x, int ldx, int C, const Dom& d, const ItemTab* items, int B, int max_len, float** mean,
@@ -880,7 +881,8 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   const bool tc_path = tc_route(c, a);
   const double in_rows = a.in_up2 ? (double)((a.L_in + 1) / 2) : (double)a.L_in;
   // bf16 window planes in or out: 2 bytes per element
-  const double in_b = a.in_mode == IN_PRE ? 2.0 : 4.0, out_b = a.out_mode == OUT_GELU_PRE ? 2.0 : 4.0;
+  const double in_b = a.in_mode == IN_PRE ? 2.0 : 4.0,
+               out_b = (a.out_mode == OUT_GELU_PRE || a.out_mode == OUT_STORE_BF) ? 2.0 : 4.0;
   const double bytes = in_b * in_rows * a.cin + out_b * (double)a.L_out * a.cout + (res ? 4.0 * a.L_out * a.cout : 0.0) +
                        (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
   if (tc_path) {
@@ -889,7 +891,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       tr = ar.get<unsigned long long>(16);
       KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
     }
-    if ((c.cout > TC_PRE_MIN_COUT || (c.cout == TC_PRE_MIN_COUT && c.K <= 3)) && a.in_mode != IN_PRE) {
+    if (tc_pre(c, a)) {
       // several 128-channel output tiles share each input window: transform the input once into
       // bf16 window planes instead of once per output tile
       auto mk = ar.mark();
@@ -934,6 +936,13 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
 
 bool Engine::tc_route(const Conv& c, const ConvArgs& a) const {
   return precision == KK_PRECISION_BF16 && tc_ok && c.tc.w && !c.simt_only && tc_supported(a, c.tc);
+}
+
+// Tensor-core layers whose input is first transformed into bf16 window planes (prologue kernel):
+// several 128-channel output tiles share each input window, or a short kernel leaves the fused
+// route's producers too little MMA time to hide behind.
+bool Engine::tc_pre(const Conv& c, const ConvArgs& a) const {
+  return (c.cout > TC_PRE_MIN_COUT || (c.cout == TC_PRE_MIN_COUT && c.K <= 3)) && a.in_mode != IN_PRE;
 }
 
 // Run a convolution and produce the AdaIN statistics of its output [L_out][cout] (ldy == cout):
@@ -1437,7 +1446,9 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     // BF16 mode on the tensor cores: every ALBERT linear reads its input as bf16 window planes
     // written by the stage before it (the attention for the output projection, the LayerNorms for
     // the QKV and FFN projections, the FFN's GELU epilogue for the down projection), so no f32
-    // activation makes a round trip through HBM only to be transformed again
+    // activation makes a round trip through HBM only to be transformed again; the QKV projection
+    // writes bf16 rows, the attention's operand precision (rounded exactly as the attention would
+    // round f32 rows)
     float* f = nullptr;
     const long pre_rows = PRE_PAD_FRONT + (long)LT + PRE_PAD_BACK;
     const size_t planes768 = (size_t)(768 / 64) * 8 * pre_rows * 16;
@@ -1457,12 +1468,14 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       ctxpre = ar.get<uint8_t>(planes768);
       apre = ar.get<uint8_t>(planes768);
       fpre = ar.get<uint8_t>((size_t)(2048 / 64) * 8 * pre_rows * 16);
-      ConvArgs t0 = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE, nullptr, nullptr);
+      ConvArgs t0 = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE_BF, nullptr, nullptr);
       ConvArgs t1 = pre_args(m.dense, ctxpre, a, 768, OUT_PLUS, h, nullptr);
       ConvArgs t2 = pre_args(m.ffn, apre, nullptr, 0, OUT_GELU_PRE, nullptr, fpre);
       ConvArgs t3 = pre_args(m.ffn_out, fpre, h, 768, OUT_PLUS, a, nullptr);
-      planes = attn_tc && tc_route(m.qkv, t0) && tc_route(m.dense, t1) && tc_route(m.ffn, t2) &&
-               tc_route(m.ffn_out, t3);
+      ConvArgs t00 = ca(m.qkv);  // the first layer: f32 rows from map_in, through the pre-transform route
+      t00.x = h, t00.ldx = 768, t00.L_in = LT, t00.y = qkv, t00.ldy = 2304, t00.L_out = LT, t00.out_mode = OUT_STORE_BF;
+      planes = attn_tc && tc_route(m.qkv, t0) && tc_route(m.qkv, t00) && tc_pre(m.qkv, t00) &&
+               tc_route(m.dense, t1) && tc_route(m.ffn, t2) && tc_route(m.ffn_out, t3);
     }
     if (!planes) f = ar.get<float>((size_t)LT * 2048);
     linear(m.map_in, emb, 128, LT, h, 768);
@@ -1487,7 +1500,11 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
     }
     for (int layer = 0; layer < 12; layer++) {
       if (planes && layer > 0) {
-        ConvArgs t = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE, nullptr, nullptr);
+        ConvArgs t = pre_args(m.qkv, hpre, qkv, 2304, OUT_STORE_BF, nullptr, nullptr);
+        run_conv(m.qkv, t);
+      } else if (planes) {
+        ConvArgs t = ca(m.qkv);
+        t.x = h, t.ldx = 768, t.L_in = LT, t.y = qkv, t.ldy = 2304, t.L_out = LT, t.out_mode = OUT_STORE_BF;
         run_conv(m.qkv, t);
       } else {
         linear(m.qkv, h, 768, LT, qkv, 2304);  // the first layer's input comes from map_in
@@ -1495,8 +1512,8 @@ void Engine::forward(int B, const int64_t* ids, const int32_t* ids_len, const fl
       cudaEvent_t e0;
       prof_begin(&e0);
       if (attn_tc) {
-        check(launch_attention_tc(qkv, 2304, items_d, work_d, n_work, ctx, 768, err_flag, st, planes ? ctxpre : nullptr,
-                                  pre_rows),
+        check(launch_attention_tc(qkv, 2304, planes, items_d, work_d, n_work, ctx, 768, err_flag, st,
+                                  planes ? ctxpre : nullptr, pre_rows),
               "attention(tcgen05)");
         launches += (n_work[0] > 0) + (n_work[1] > 0) + (n_work[2] > 0) - 1;  // one kernel per non-empty bucket
       } else

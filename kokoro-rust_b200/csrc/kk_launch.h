@@ -50,7 +50,8 @@ cudaError_t launch_attention_f32(const float* qkv, int ldqkv, const ItemTab* ite
 // T <= 128, T <= 256 and T <= 512 of n_work[0..2] entries. err receives 3 if an MMA wait expires.
 // With ctx_pre set, ctx is written only as bf16 window planes (IN_PRE layout, ctx_pre_rows rows per
 // plane; head h = 64-channel block h) for the output projection, and ctx is not touched.
-cudaError_t launch_attention_tc(const float* qkv, int ldqkv, const ItemTab* items, const int2* work,
+// qkv_bf16: the qkv rows are bf16 (ldqkv elements apart, a multiple of 8), else f32.
+cudaError_t launch_attention_tc(const void* qkv, int ldqkv, bool qkv_bf16, const ItemTab* items, const int2* work,
                                 const int n_work[3], float* ctx, int ldc, int* err, cudaStream_t st,
                                 void* ctx_pre = nullptr, long ctx_pre_rows = 0);
 

@@ -176,8 +176,9 @@ extern "C" KK_API kk_status kk_conv_selftest(int cuda_ordinal, const kk_conv_cas
   return KK_OK;
 }
 
-extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len,
-                                                  const float* qkv, float* ctx) {
+// qkv_bf16: qkv holds bf16 bit patterns (2 bytes per element) instead of f32.
+static kk_status attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len, const void* qkv,
+                                    bool qkv_bf16, float* ctx) {
   using namespace kk;
   if (n_items < 1 || !tok_len || !qkv || !ctx) return fail(KK_ERR_INVALID_ARG, "null argument");
   std::vector<ItemTab> items(n_items);
@@ -204,13 +205,13 @@ extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items,
     if (cudaMalloc(&b.p, n) != cudaSuccess) return false;
     return cudaMemcpy(b.p, h, n, cudaMemcpyHostToDevice) == cudaSuccess;
   };
-  bool ok = put(dq, qkv, sizeof(float) * rows * 2304) && put(di, items.data(), sizeof(ItemTab) * n_items) &&
+  bool ok = put(dq, qkv, (qkv_bf16 ? 2 : 4) * (size_t)rows * 2304) && put(di, items.data(), sizeof(ItemTab) * n_items) &&
             put(dw, all.data(), sizeof(int2) * all.size()) &&
             cudaMalloc(&dc.p, sizeof(float) * rows * 768) == cudaSuccess &&
             cudaMemset(dc.p, 0, sizeof(float) * rows * 768) == cudaSuccess &&
             cudaMalloc(&derr.p, sizeof(int)) == cudaSuccess && cudaMemset(derr.p, 0, sizeof(int)) == cudaSuccess;
   if (!ok) return fail(KK_ERR_OOM, "device allocation / copy failed");
-  cudaError_t e = launch_attention_tc((const float*)dq.p, 2304, (const ItemTab*)di.p, (const int2*)dw.p, n_work,
+  cudaError_t e = launch_attention_tc(dq.p, 2304, qkv_bf16, (const ItemTab*)di.p, (const int2*)dw.p, n_work,
                                       (float*)dc.p, 768, (int*)derr.p, nullptr);
   if (e == cudaSuccess) e = cudaDeviceSynchronize();
   if (e != cudaSuccess) return fail(KK_ERR_CUDA, cudaGetErrorString(e));
@@ -220,6 +221,16 @@ extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items,
   if (cudaMemcpy(ctx, dc.p, sizeof(float) * rows * 768, cudaMemcpyDeviceToHost) != cudaSuccess)
     return fail(KK_ERR_CUDA, "output copy failed");
   return KK_OK;
+}
+
+extern "C" KK_API kk_status kk_attention_selftest(int cuda_ordinal, int n_items, const int32_t* tok_len,
+                                                  const float* qkv, float* ctx) {
+  return attention_selftest(cuda_ordinal, n_items, tok_len, qkv, false, ctx);
+}
+
+extern "C" KK_API kk_status kk_attention_selftest_bf16(int cuda_ordinal, int n_items, const int32_t* tok_len,
+                                                       const uint16_t* qkv, float* ctx) {
+  return attention_selftest(cuda_ordinal, n_items, tok_len, qkv, true, ctx);
 }
 
 extern "C" KK_API kk_status kk_lstm_selftest(int cuda_ordinal, int tc, int n_items, const int32_t* len,

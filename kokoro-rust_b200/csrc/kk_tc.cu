@@ -133,7 +133,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
   const ConvArgs& a = p.a;
   const int in_mode = IM >= 0 ? IM : a.in_mode;
   const int in_up2 = IM >= 0 ? UP : a.in_up2;
-  const int out_mode_k = IM >= 0 ? OM : a.out_mode;
+  // OUT_STORE_BF runs as OUT_STORE with bf16 staging and a bf16 tensor map
+  constexpr bool YB = OM == OUT_STORE_BF;
+  const int out_mode_k = IM >= 0 ? (YB ? OUT_STORE : OM) : a.out_mode;
   const uint32_t xbytes = 8u * p.win_pad * 16u;
   const int RST = p.rst;
   constexpr int BOXR = tc_box_rows(IM, OM);
@@ -563,7 +565,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             continue;
           }
           float* sb = stg + (c & 1) * TC_EC * 32;
-          const uint32_t sbl = smem_u32(sb) + 4u * lane;
+          const uint32_t sbl = smem_u32(sb) + (YB ? 2u : 4u) * lane;  // YB: bf16 chunk, 64 bytes a row
           if (lane == 0) bulk_wait_read1();  // the store issued two chunks ago has read sb
           __syncwarp();
           if (trc) t_stbuf += clock64() - tq;
@@ -575,7 +577,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
             else if (out_mode == OUT_PLUS) r = (r + lds_f32(rrl + 128u * jj)) * oscale;
             else if (out_mode == OUT_GELU) r = gelu_new(r);
             vals[jj] = r;
-            sts_f32(sbl + 128u * jj, r);
+            if constexpr (YB) {
+              const __nv_bfloat16 hb = __float2bfloat16_rn(r);
+              unsigned short u;
+              memcpy(&u, &hb, 2);
+              sts_u16(sbl + 64u * jj, u);
+            } else {
+              sts_f32(sbl + 128u * jj, r);
+            }
           }
           if (stat) {
             if (single) {
@@ -984,6 +993,7 @@ static TcKernelFn pick_kernel(int im, int up, int om, int* idx) {
       {IN_PRE, 0, OUT_PLUS, tc_conv_kernel<IN_PRE, 0, OUT_PLUS>},
       {IN_PRE, 0, OUT_GELU, tc_conv_kernel<IN_PRE, 0, OUT_GELU>},
       {IN_PRE, 0, OUT_GELU_PRE, tc_conv_kernel<IN_PRE, 0, OUT_GELU_PRE>},
+      {IN_PRE, 0, OUT_STORE_BF, tc_conv_kernel<IN_PRE, 0, OUT_STORE_BF>},
   };
   const int n = (int)(sizeof(table) / sizeof(table[0]));
   for (int i = 0; i < n; i++)
@@ -1028,7 +1038,10 @@ static bool tab_of(const ConvArgs& a, int cin_pad) {
   return (a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE) && cin_pad <= TC_TAB;
 }
 
-static bool rows_ok(const void* base, long ld) { return base && ld % 4 == 0 && (((uintptr_t)base) & 15) == 0; }
+// Rows of esize-byte elements that TMA can move: 16-byte aligned base and row stride.
+static bool rows_ok(const void* base, long ld, int esize = 4) {
+  return base && (ld * esize) % 16 == 0 && (((uintptr_t)base) & 15) == 0;
+}
 
 bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (a.stride != 1 || a.K != t.K || a.cin != t.cin || a.cout != t.cout) return false;
@@ -1040,6 +1053,10 @@ bool tc_supported(const ConvArgs& a, const TcWeights& t) {
   if (a.in_mode != IN_PRE && !rows_ok(a.x, a.ldx)) return false;
   if (a.out_mode == OUT_GELU_PRE) {
     if (!a.ypre || (((uintptr_t)a.ypre) & 15) != 0 || a.cout % TC_KB != 0 || a.stat) return false;
+  } else if (a.out_mode == OUT_STORE_BF) {
+    // one instance (IN_PRE input): other inputs take the pre-transform route first (tc_conv refuses
+    // them otherwise)
+    if (a.stat || a.in_up2 || !rows_ok(a.y, a.ldy, 2)) return false;
   } else if (!rows_ok(a.y, a.ldy)) {
     return false;
   }
@@ -1072,15 +1089,17 @@ static EncodeTiledFn encode_fn() {
 
 // f32 rows [rows][cols] with row stride ld floats; box = box_cols x box_rows, no swizzle; elements
 // outside the tensor read as zero.
-static bool make_rows_map(CUtensorMap* m, const float* base, long rows, long cols, long ld, int box_cols,
-                          int box_rows) {
+static bool make_rows_map(CUtensorMap* m, const void* base, long rows, long cols, long ld, int box_cols,
+                          int box_rows, bool bf16_rows = false) {
   EncodeTiledFn fn = encode_fn();
-  if (!fn || !rows_ok(base, ld) || rows <= 0 || cols <= 0) return false;
+  const int es = bf16_rows ? 2 : 4;
+  if (!fn || !rows_ok(base, ld, es) || rows <= 0 || cols <= 0) return false;
   cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  cuuint64_t strides[1] = {(cuuint64_t)ld * es};
   cuuint32_t box[2] = {(cuuint32_t)box_cols, (cuuint32_t)box_rows};
   cuuint32_t estr[2] = {1, 1};
-  return fn(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims, strides, box, estr,
+  return fn(m, bf16_rows ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, (void*)base, dims,
+            strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -1093,9 +1112,11 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   const long x_rows = a.in_up2 ? (a.L_in + 1) / 2 : a.L_in;
   const bool pre = a.in_mode == IN_PRE;
   if (pre && (!a.xpre || (((uintptr_t)a.xpre) & 15) != 0)) return cudaErrorInvalidValue;
+  if (a.out_mode == OUT_STORE_BF && !pre) return cudaErrorInvalidValue;  // its one instance reads IN_PRE planes
   const int box_rows = box_rows_of(a);
   bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, box_rows)) &&
-              (a.out_mode == OUT_GELU_PRE || make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC));
+              (a.out_mode == OUT_GELU_PRE ||
+               make_rows_map(&p.ymap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC, a.out_mode == OUT_STORE_BF));
   if (maps && a.out_mode == OUT_ADD) maps = make_rows_map(&p.rmap, a.y, a.L_out, a.cout, a.ldy, 32, TC_EC);
   if (maps && a.out_mode == OUT_PLUS) maps = make_rows_map(&p.rmap, a.sc, a.L_out, a.cout, a.ldsc, 32, TC_EC);
   if (!maps) return cudaErrorInvalidValue;

@@ -60,6 +60,7 @@ _SIGS = {
     "kk_conv_selftest": (ctypes.c_int, [ctypes.c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int, _P]),
     "kk_conv_selftest_error": (ctypes.c_char_p, []),
     "kk_attention_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P]),
+    "kk_attention_selftest_bf16": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, _P, _P, _P]),
     "kk_lstm_selftest": (ctypes.c_int, [ctypes.c_int, ctypes.c_int, ctypes.c_int, _P, _P, _P, _P, _P]),
     "kk_fetch_audio_pcm16": (ctypes.c_int, [_P, ctypes.c_int, _P, ctypes.c_int64, _P]),
     "kk_wav_header": (ctypes.c_int, [ctypes.c_int, ctypes.c_uint32, ctypes.c_uint64, _P]),
@@ -127,14 +128,16 @@ def conv_selftest(ordinal: int, *, x, w, item_in, item_out, rows_out, pad, dil=1
     return (res, ms.value) if timing_iters > 0 else res
 
 
-def attention_selftest(ordinal: int, tok_len, qkv):
+def attention_selftest(ordinal: int, tok_len, qkv, bf16_rows: bool = False):
     """The BF16 mode's tensor-core attention (kk_attention_selftest): qkv [sum T][2304] f32 of items
-    of tok_len rows each; returns ctx [sum T][768]."""
+    of tok_len rows each; returns ctx [sum T][768]. bf16_rows: qkv is a uint16 array of bf16 bit
+    patterns (kk_attention_selftest_bf16, the QKV projection's output form)."""
     lib = load_library()
     tl = np.ascontiguousarray(tok_len, np.int32)
-    qkv = np.ascontiguousarray(qkv, np.float32)
+    qkv = np.ascontiguousarray(qkv, np.uint16 if bf16_rows else np.float32)
     ctx = np.zeros((qkv.shape[0], 768), np.float32)
-    st = lib.kk_attention_selftest(ordinal, len(tl), tl.ctypes.data, qkv.ctypes.data, ctx.ctypes.data)
+    fn = lib.kk_attention_selftest_bf16 if bf16_rows else lib.kk_attention_selftest
+    st = fn(ordinal, len(tl), tl.ctypes.data, qkv.ctypes.data, ctx.ctypes.data)
     if st != KK_OK:
         raise KokoroError(st, lib.kk_conv_selftest_error().decode())
     return ctx

@@ -49,6 +49,19 @@ def test_tc_attention_matches_reference(kk, lens):
     assert err.max() <= 2.0 ** -8 * vmax, (err.max(), vmax)
 
 
+@pytest.mark.parametrize("lens", [[1, 7, 16, 100, 128], [257, 300, 511, 512]])
+def test_tc_attention_bf16_rows_equal_f32_rows(kk, lens):
+    """The BF16 mode's QKV projection writes bf16 rows (round to nearest even) for the attention:
+    the same ctx bit for bit as the f32 rows the attention rounds itself."""
+    import kokoro_rust_b200.engine as E
+    rng = np.random.default_rng(7 + sum(lens))
+    qkv = (rng.standard_normal((sum(lens), 2304)) * 1.5).astype(np.float32)
+    bits = torch.from_numpy(qkv).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    got = E.attention_selftest(0, lens, bits, bf16_rows=True)
+    want = E.attention_selftest(0, lens, qkv)
+    assert np.array_equal(got, want)
+
+
 def test_tc_attention_rejects_long_items(kk):
     import kokoro_rust_b200.engine as E
     with pytest.raises(E.KokoroError):
