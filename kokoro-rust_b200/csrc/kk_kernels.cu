@@ -743,8 +743,10 @@ __global__ void har_source_kernel(const float* f0, const float* pp, int L2, cons
       float r = (float)sqrt(-2.0 * log((double)u1));
       float th = __fmul_rn(6.2831855f, u2);
       long e0 = 2 * p - q0, e1 = e0 + 1;
-      if (e0 >= 0 && e0 < 9) nz[e0] = __fmul_rn(r, (float)cos((double)th));
-      if (e1 >= 0 && e1 < 9) nz[e1] = __fmul_rn(r, (float)sin((double)th));
+      double sd, cd;  // one argument reduction for both (the same values as cos() and sin())
+      sincos((double)th, &sd, &cd);
+      if (e0 >= 0 && e0 < 9) nz[e0] = __fmul_rn(r, (float)cd);
+      if (e1 >= 0 && e1 < 9) nz[e1] = __fmul_rn(r, (float)sd);
     }
   }
   const float* ppb = pp + 2L * it.a;
