@@ -928,6 +928,9 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
     } else {
       prof_end(e0, "conv_tcgen05", flops, bytes);
     }
+  } else if (rowproj_supported(a)) {  // projections to 1-4 channels: one warp per row
+    check(launch_rowproj(a, st), "conv(row projection)");
+    prof_end(e0, "rowproj", flops, bytes);
   } else {
     check(launch_conv_simt(a, st), "conv(simt)");
     prof_end(e0, "conv_simt", flops, bytes);

@@ -75,11 +75,65 @@ __global__ void gather_rows_kernel(const float* src, int lds, const int* tab, in
   out[(long)r * ldo + j] = s < 0 ? 0.0f : src[(long)s * lds + j];
 }
 
+// The same gather 16 bytes at a time (d, lds, ldo multiples of 4, aligned bases).
+__global__ void gather_rows4_kernel(const float4* src, int lds4, const int* tab, int rows, int d4, float4* out,
+                                    int ldo4) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * d4) return;
+  const int r = i / d4, j = i - r * d4;
+  const int s = tab[r];
+  out[(long)r * ldo4 + j] = s < 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : __ldg(src + (long)s * lds4 + j);
+}
+
 cudaError_t launch_gather_rows(const float* src, int lds, const int* tab, int rows, int d, float* out, int ldo,
                                cudaStream_t st) {
   long n = (long)rows * d;
   if (n == 0) return cudaSuccess;
-  gather_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(src, lds, tab, rows, d, out, ldo);
+  if (d % 4 == 0 && lds % 4 == 0 && ldo % 4 == 0 && ((((uintptr_t)src) | ((uintptr_t)out)) & 15) == 0 &&
+      n / 4 < (1L << 31)) {
+    gather_rows4_kernel<<<nblk(n / 4, 256), 256, 0, st>>>((const float4*)src, lds / 4, tab, rows, d / 4, (float4*)out,
+                                                          ldo / 4);
+  } else {
+    gather_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(src, lds, tab, rows, d, out, ldo);
+  }
+  return cudaGetLastError();
+}
+
+// Projection of each row to a few channels (K = 1, cout <= 4; the F0 / N projections): one warp
+// per row looks up the row's item once, its lanes read the row's channels (128 contiguous bytes
+// per load) and a shuffle reduction sums the products; gap rows read nothing and give the bias.
+__global__ void rowproj_kernel(const ConvArgs a) {
+  const long r = (blockIdx.x * (long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (r >= a.L_out) return;
+  const int b = a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)r);
+  float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  if (b >= 0 || a.nomask) {
+    const float* xr = a.x + r * a.ldx;
+    for (int c = lane; c < a.cin; c += 32) {
+      const float xv = __ldg(xr + c);
+#pragma unroll
+      for (int o = 0; o < 4; o++)
+        if (o < a.cout) acc[o] = fmaf(xv, __ldg(a.w + (long)c * a.cout + o), acc[o]);
+    }
+  }
+#pragma unroll
+  for (int o = 0; o < 4; o++)
+#pragma unroll
+    for (int m = 16; m > 0; m >>= 1) acc[o] += __shfl_xor_sync(0xffffffffu, acc[o], m);
+  if (lane == 0)
+    for (int o = 0; o < a.cout; o++) a.y[r * a.ldy + o] = acc[o] + (a.bias ? a.bias[o] : 0.0f);
+}
+
+bool rowproj_supported(const ConvArgs& a) {
+  return a.K == 1 && a.stride == 1 && a.cout >= 1 && a.cout <= 4 && !a.in_up2 && a.out_mode == OUT_STORE &&
+         (a.in_mode == IN_MASK || a.in_mode == IN_NOMASK) && a.L_out == a.L_in;
+}
+
+cudaError_t launch_rowproj(const ConvArgs& a, cudaStream_t st) {
+  if (!rowproj_supported(a)) return cudaErrorInvalidValue;
+  if (a.L_out == 0) return cudaSuccess;
+  rowproj_kernel<<<nblk((long)a.L_out * 32, 256), 256, 0, st>>>(a);
   return cudaGetLastError();
 }
 
@@ -90,10 +144,24 @@ __global__ void embed_rows_kernel(const int* ids, const int* row_item, int rows,
   out[i] = row_item[r] < 0 ? 0.0f : table[(long)ids[r] * d + j];
 }
 
+// The same lookup 16 bytes at a time (d a multiple of 4, aligned table and output).
+__global__ void embed_rows4_kernel(const int* ids, const int* row_item, int rows, const float4* table, int d4,
+                                   float4* out) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rows * d4) return;
+  const int r = i / d4, j = i - r * d4;
+  out[i] = row_item[r] < 0 ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : __ldg(table + (long)ids[r] * d4 + j);
+}
+
 cudaError_t launch_embed_rows(const int* ids, const int* row_item, int rows, const float* table, int d, float* out,
                               cudaStream_t st) {
   long n = (long)rows * d;
-  embed_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(ids, row_item, rows, table, d, out);
+  if (n == 0) return cudaSuccess;
+  if (d % 4 == 0 && ((((uintptr_t)table) | ((uintptr_t)out)) & 15) == 0 && n / 4 < (1L << 31))
+    embed_rows4_kernel<<<nblk(n / 4, 256), 256, 0, st>>>(ids, row_item, rows, (const float4*)table, d / 4,
+                                                         (float4*)out);
+  else
+    embed_rows_kernel<<<nblk(n, 256), 256, 0, st>>>(ids, row_item, rows, table, d, out);
   return cudaGetLastError();
 }
 

@@ -25,6 +25,10 @@ cudaError_t launch_albert_embed(const int* ids, const int* row_item, const ItemT
 // out[r, 0:d] = src[tab[r], 0:d] (tab < 0 -> 0); tab == null: identity row index with row_item mask
 cudaError_t launch_gather_rows(const float* src, int lds, const int* tab, int rows, int d, float* out,
                                int ldo, cudaStream_t st);
+// y[t, 0:cout] = bias + W x[t] for K = 1 layers with cout <= 4 (the F0 / N projections), one warp
+// per row; x gap rows (IN_MASK) give the bias alone
+bool rowproj_supported(const ConvArgs& a);
+cudaError_t launch_rowproj(const ConvArgs& a, cudaStream_t st);
 // text embedding rows (gap rows -> 0)
 cudaError_t launch_embed_rows(const int* ids, const int* row_item, int rows, const float* table, int d,
                               float* out, cudaStream_t st);
