@@ -73,6 +73,10 @@ enum OutMode : int {
 struct ConvArgs {
   // input [L_in][ldx] f32
   const float* x;
+  // optional (pre-transform route only): the input row is ((x + x_b) + x_c) / 3, the mean of a
+  // generator stage's three resblocks, formed while the input is transformed (same ldx)
+  const float* x_b;
+  const float* x_c;
   int ldx, cin, L_in;
   int in_mode;
   int in_up2;  // read row t/2 (nearest x2 upsample of the input)

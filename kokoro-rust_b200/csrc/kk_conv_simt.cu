@@ -104,7 +104,7 @@ size_t conv_simt_smem(const ConvArgs& a) {
 }
 
 cudaError_t launch_conv_simt(const ConvArgs& a, cudaStream_t st) {
-  if (a.out_mode == OUT_GELU_PRE || a.out_mode == OUT_STORE_BF) return cudaErrorInvalidValue;  // tensor-core modes
+  if (a.out_mode == OUT_GELU_PRE || a.out_mode == OUT_STORE_BF || a.x_b) return cudaErrorInvalidValue;  // tensor-core modes
   size_t smem = conv_simt_smem(a);
   static bool attr_set[64] = {};
   int dev = 0;

@@ -881,7 +881,7 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   const bool tc_path = tc_route(c, a);
   const double in_rows = a.in_up2 ? (double)((a.L_in + 1) / 2) : (double)a.L_in;
   // bf16 window planes in or out: 2 bytes per element
-  const double in_b = a.in_mode == IN_PRE ? 2.0 : 4.0,
+  const double in_b = a.in_mode == IN_PRE ? 2.0 : (a.x_b ? 12.0 : 4.0),
                out_b = (a.out_mode == OUT_GELU_PRE || a.out_mode == OUT_STORE_BF) ? 2.0 : 4.0;
   const double bytes = in_b * in_rows * a.cin + out_b * (double)a.L_out * a.cout + (res ? 4.0 * a.L_out * a.cout : 0.0) +
                        (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
@@ -891,11 +891,13 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       tr = ar.get<unsigned long long>(16);
       KK_CUDA(cudaMemsetAsync(tr, 0, 16 * sizeof(unsigned long long), st));
     }
-    if (tc_pre(c, a)) {
-      // several 128-channel output tiles share each input window: transform the input once into
-      // bf16 window planes instead of once per output tile
+    if (tc_pre(c, a) || (a.x_b && a.in_mode != IN_PRE)) {
+      // several 128-channel output tiles share each input window (or the input is the mean of three
+      // resblocks, formed here): transform the input once into bf16 window planes instead of once
+      // per output tile
       auto mk = ar.mark();
       ConvArgs ap = a;
+      ap.x_b = ap.x_c = nullptr;
       ap.pre_rows = PRE_PAD_FRONT + (long)a.L_in + PRE_PAD_BACK;
       void* xpre = ar.get<uint8_t>((size_t)((a.cin + 63) / 64) * 8 * ap.pre_rows * 16);
       check(launch_prologue_bf16(a, xpre, ap.pre_rows, st), "prologue_bf16");
@@ -928,6 +930,16 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
     } else {
       prof_end(e0, "conv_tcgen05", flops, bytes);
     }
+  } else if (a.x_b) {  // the three-input mean outside the tensor-core route: form it first
+    auto mk = ar.mark();
+    const long n = (long)(a.in_up2 ? (a.L_in + 1) / 2 : a.L_in) * a.ldx;
+    float* mean3 = ar.get<float>((size_t)n);
+    check(launch_sum3(a.x, a.x_b, a.x_c, mean3, n, st), "sum3");
+    ConvArgs a1 = a;
+    a1.x = mean3, a1.x_b = a1.x_c = nullptr;
+    run_conv(c, a1);
+    ar.rewind(mk);
+    return;
   } else if (rowproj_supported(a)) {  // projections to 1-4 channels: one warp per row
     check(launch_rowproj(a, st), "conv(row projection)");
     prof_end(e0, "rowproj", flops, bytes);
@@ -1178,7 +1190,15 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   stage_sync("source");
   // ---- generator stage 0 (2N -> 20N, C 256)
   float* y0 = ar.get<float>((size_t)L20 * 256);
-  float* x1 = ar.get<float>((size_t)L20 * 256);
+  // BF16 mode on the tensor cores: each stage's three resblock outputs stay alive and the next
+  // layer's input transform forms their mean (no separate mean pass over HBM); FP32 mode and
+  // stage dumps keep the mean kernel
+  const char* dump_dir = getenv("KK_DEBUG_DUMP_DIR");
+  const bool fuse_mean = precision == KK_PRECISION_BF16 && tc_ok && !(dump_dir && *dump_dir);
+  float* x1 = fuse_mean ? nullptr : ar.get<float>((size_t)L20 * 256);
+  float* r1[3] = {nullptr, nullptr, nullptr};  // stage-0 resblock outputs (fuse_mean)
+  if (fuse_mean)
+    for (int j = 0; j < 3; j++) r1[j] = ar.get<float>((size_t)L20 * 256);
   {
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L20 * 256);
@@ -1211,10 +1231,10 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     float *ym, *yr;  // statistics of y0, shared by the three parallel resblocks
     stats(y0, 256, 256, d20, items, B, max_n * d20.scale + d20.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
-      r[j] = ar.get<float>((size_t)L20 * 256);
+      r[j] = fuse_mean ? r1[j] : ar.get<float>((size_t)L20 * 256);
       snake(m.rb[j], y0, r[j], d20, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
-    check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
+    if (!fuse_mean) check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
     dump("r0_0", r[0], L20, 256, 256);
     dump("x1", x1, L20, 256, 256);
     ar.rewind(mk);
@@ -1222,7 +1242,10 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   stage_sync("generator stage 0");
   // ---- generator stage 1 (20N -> 120N + 1, C 128)
   float* y1 = ar.get<float>((size_t)L120 * 128);
-  float* x2 = ar.get<float>((size_t)L120 * 128);
+  float* x2 = fuse_mean ? nullptr : ar.get<float>((size_t)L120 * 128);
+  float* r2[3] = {nullptr, nullptr, nullptr};  // stage-1 resblock outputs (fuse_mean)
+  if (fuse_mean)
+    for (int j = 0; j < 3; j++) r2[j] = ar.get<float>((size_t)L120 * 128);
   {
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L120 * 128);
@@ -1235,7 +1258,8 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     snake(m.noise_res[1], xs, xsr, d120, gb_dec, ldgb, items, B, max_n, xm, xr);
     float* u1 = xs;  // noise-conv output no longer needed
     ConvArgs u = ca(m.ups[1]);
-    u.x = x1, u.ldx = 256, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d20, u.L_in = L20;
+    u.x = fuse_mean ? r1[0] : x1, u.ldx = 256, u.in_mode = IN_LEAKY_MASK, u.slope = 0.1f, u.din = d20, u.L_in = L20;
+    if (fuse_mean) u.x_b = r1[1], u.x_c = r1[2];
     u.y = u1, u.ldy = 768, u.L_out = L20;
     run_conv(m.ups[1], u);
     check(launch_reflect_add(u1, xsr, 128, items, d120, y1, st), "reflect_add");
@@ -1246,10 +1270,10 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     float *ym, *yr;  // statistics of y1, shared by the three parallel resblocks
     stats(y1, 128, 128, d120, items, B, max_n * d120.scale + d120.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
-      r[j] = ar.get<float>((size_t)L120 * 128);
+      r[j] = fuse_mean ? r2[j] : ar.get<float>((size_t)L120 * 128);
       snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
-    check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
+    if (!fuse_mean) check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
     dump("x2", x2, L120, 128, 128);
     ar.rewind(mk);
   }
@@ -1258,7 +1282,8 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   float* post = ar.get<float>((size_t)L120 * POST_LD);
   {
     ConvArgs a = ca(m.post);
-    a.x = x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
+    a.x = fuse_mean ? r2[0] : x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
+    if (fuse_mean) a.x_b = r2[1], a.x_c = r2[2];
     a.y = post, a.ldy = POST_LD, a.L_out = L120;
     run_conv(m.post, a);
   }

@@ -836,13 +836,24 @@ __global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, ui
     bm[m] = in ? (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)g)) : -1;
     v[m] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
     if (in && c0 < cin) {
-      const float* src = a.x + (long)(a.in_up2 ? (g >> 1) : g) * a.ldx + c0;
-      if (full) {
-        v[m] = __ldg(reinterpret_cast<const float4*>(src));
-      } else {
-        v[m].x = __ldg(src);
-        if (c0 + 1 < cin) v[m].y = __ldg(src + 1);
-        if (c0 + 2 < cin) v[m].z = __ldg(src + 2);
+      const long off = (long)(a.in_up2 ? (g >> 1) : g) * a.ldx + c0;
+      auto ld4 = [&](const float* base) {
+        const float* src = base + off;
+        float4 t = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (full) {
+          t = __ldg(reinterpret_cast<const float4*>(src));
+        } else {
+          t.x = __ldg(src);
+          if (c0 + 1 < cin) t.y = __ldg(src + 1);
+          if (c0 + 2 < cin) t.z = __ldg(src + 2);
+        }
+        return t;
+      };
+      v[m] = ld4(a.x);
+      if (a.x_b) {  // mean of three resblocks, in the resblock-mean kernel's order of operations
+        const float4 vb = ld4(a.x_b), vc = ld4(a.x_c);
+        v[m] = make_float4(((v[m].x + vb.x) + vc.x) / 3.0f, ((v[m].y + vb.y) + vc.y) / 3.0f,
+                           ((v[m].z + vb.z) + vc.z) / 3.0f, ((v[m].w + vb.w) + vc.w) / 3.0f);
       }
     }
   }
@@ -1113,6 +1124,7 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   const bool pre = a.in_mode == IN_PRE;
   if (pre && (!a.xpre || (((uintptr_t)a.xpre) & 15) != 0)) return cudaErrorInvalidValue;
   if (a.out_mode == OUT_STORE_BF && !pre) return cudaErrorInvalidValue;  // its one instance reads IN_PRE planes
+  if (a.x_b && !pre) return cudaErrorInvalidValue;  // the three-input mean is formed by the pre-transform
   const int box_rows = box_rows_of(a);
   bool maps = (pre || make_rows_map(&p.xmap, a.x, x_rows, a.cin, a.ldx, TC_KB, box_rows)) &&
               (a.out_mode == OUT_GELU_PRE ||
