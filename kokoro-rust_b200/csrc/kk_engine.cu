@@ -1190,9 +1190,12 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   stage_sync("source");
   // ---- generator stage 0 (2N -> 20N, C 256)
   float* y0 = ar.get<float>((size_t)L20 * 256);
-  // BF16 mode on the tensor cores: each stage's three resblock outputs stay alive and the next
-  // layer's input transform forms their mean (no separate mean pass over HBM); FP32 mode and
-  // stage dumps keep the mean kernel
+  // BF16 mode on the tensor cores: stage 0's three resblock outputs stay alive and the input
+  // transform of the stage-1 upsampling (the pre-transform route, which that layer takes anyway)
+  // forms their mean, saving the mean pass over HBM. Stage 1 keeps the mean kernel: its consumer,
+  // conv_post, runs on the fused route, and the pre-transform route with the three-input mean cost
+  // it more than the mean kernel (measured: +2.8 ms against 2.2 ms). FP32 mode and stage dumps keep
+  // the mean kernel for both stages
   const char* dump_dir = getenv("KK_DEBUG_DUMP_DIR");
   const bool fuse_mean = precision == KK_PRECISION_BF16 && tc_ok && !(dump_dir && *dump_dir);
   float* x1 = fuse_mean ? nullptr : ar.get<float>((size_t)L20 * 256);
@@ -1234,7 +1237,12 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
       r[j] = fuse_mean ? r1[j] : ar.get<float>((size_t)L20 * 256);
       snake(m.rb[j], y0, r[j], d20, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
-    if (!fuse_mean) check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
+    if (!fuse_mean) {
+      cudaEvent_t e0;
+      prof_begin(&e0);
+      check(launch_sum3(r[0], r[1], r[2], x1, (long)L20 * 256, st), "sum3");
+      prof_end(e0, "resblock_mean", 0.0, 16.0 * (double)L20 * 256);
+    }
     dump("r0_0", r[0], L20, 256, 256);
     dump("x1", x1, L20, 256, 256);
     ar.rewind(mk);
@@ -1242,10 +1250,7 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   stage_sync("generator stage 0");
   // ---- generator stage 1 (20N -> 120N + 1, C 128)
   float* y1 = ar.get<float>((size_t)L120 * 128);
-  float* x2 = fuse_mean ? nullptr : ar.get<float>((size_t)L120 * 128);
-  float* r2[3] = {nullptr, nullptr, nullptr};  // stage-1 resblock outputs (fuse_mean)
-  if (fuse_mean)
-    for (int j = 0; j < 3; j++) r2[j] = ar.get<float>((size_t)L120 * 128);
+  float* x2 = ar.get<float>((size_t)L120 * 128);
   {
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L120 * 128);
@@ -1270,10 +1275,15 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     float *ym, *yr;  // statistics of y1, shared by the three parallel resblocks
     stats(y1, 128, 128, d120, items, B, max_n * d120.scale + d120.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
-      r[j] = fuse_mean ? r2[j] : ar.get<float>((size_t)L120 * 128);
+      r[j] = ar.get<float>((size_t)L120 * 128);
       snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n, ym, yr);
     }
-    if (!fuse_mean) check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
+    {
+      cudaEvent_t e0;
+      prof_begin(&e0);
+      check(launch_sum3(r[0], r[1], r[2], x2, (long)L120 * 128, st), "sum3");
+      prof_end(e0, "resblock_mean", 0.0, 16.0 * (double)L120 * 128);
+    }
     dump("x2", x2, L120, 128, 128);
     ar.rewind(mk);
   }
@@ -1282,8 +1292,7 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   float* post = ar.get<float>((size_t)L120 * POST_LD);
   {
     ConvArgs a = ca(m.post);
-    a.x = fuse_mean ? r2[0] : x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
-    if (fuse_mean) a.x_b = r2[1], a.x_c = r2[2];
+    a.x = x2, a.ldx = 128, a.in_mode = IN_LEAKY_MASK, a.slope = 0.01f, a.din = d120, a.L_in = L120;
     a.y = post, a.ldy = POST_LD, a.L_out = L120;
     run_conv(m.post, a);
   }
