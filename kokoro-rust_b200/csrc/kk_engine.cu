@@ -1251,6 +1251,16 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
   // ---- generator stage 1 (20N -> 120N + 1, C 128)
   float* y1 = ar.get<float>((size_t)L120 * 128);
   float* x2 = ar.get<float>((size_t)L120 * 128);
+  // BF16 mode: the AdaIN statistics of y1 come out of the reflection-pad pass that writes it
+  // (plain f32 partial sums, as the tensor-core epilogues form theirs) instead of a second pass
+  const bool y1_fused_stats = precision == KK_PRECISION_BF16 && tc_ok;
+  float *ym1 = nullptr, *yr1 = nullptr;
+  double* part1 = nullptr;
+  if (y1_fused_stats) {
+    part1 = ar.get<double>((size_t)2 * B * 128);
+    ym1 = ar.get<float>((size_t)B * 128);
+    yr1 = ar.get<float>((size_t)B * 128);
+  }
   {
     auto mk = ar.mark();
     float* xs = ar.get<float>((size_t)L120 * 128);
@@ -1267,13 +1277,22 @@ float* Engine::decode_core(int B, int max_n, const ItemTab* items, const int* co
     if (fuse_mean) u.x_b = r1[1], u.x_c = r1[2];
     u.y = u1, u.ldy = 768, u.L_out = L20;
     run_conv(m.ups[1], u);
-    check(launch_reflect_add(u1, xsr, 128, items, d120, y1, st), "reflect_add");
+    if (y1_fused_stats) {
+      KK_CUDA(cudaMemsetAsync(part1, 0, sizeof(double) * 2 * B * 128, st));
+      check(launch_reflect_add_stats(u1, xsr, items, d120, y1, part1, st), "reflect_add_stats");
+      check(launch_stats_from_sums(part1, 128, items, B, d120.scale, d120.plus1, ym1, yr1, st), "stats_from_sums");
+    } else {
+      check(launch_reflect_add(u1, xsr, 128, items, d120, y1, st), "reflect_add");
+    }
     dump("xsr1", xsr, L120, 128, 128);
     dump("y1", y1, L120, 128, 128);
     ar.rewind(mk);
     float* r[3];
     float *ym, *yr;  // statistics of y1, shared by the three parallel resblocks
-    stats(y1, 128, 128, d120, items, B, max_n * d120.scale + d120.plus1, &ym, &yr);
+    if (y1_fused_stats)
+      ym = ym1, yr = yr1;
+    else
+      stats(y1, 128, 128, d120, items, B, max_n * d120.scale + d120.plus1, &ym, &yr);
     for (int j = 0; j < 3; j++) {
       r[j] = ar.get<float>((size_t)L120 * 128);
       snake(m.rb[3 + j], y1, r[j], d120, gb_dec, ldgb, items, B, max_n, ym, yr);

@@ -998,6 +998,60 @@ cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const Ite
   return cudaGetLastError();
 }
 
+// The same for C = 128 with the AdaIN sums of the result (BF16 mode: plain f32 partial sums, as the
+// tensor-core epilogue forms them, added into f64 part[(item * 128 + c) * 2 + {0, 1}]). Block =
+// 8 warps over RS_ROWS consecutive rows (warp w: rows w, w + 8, ...), lane = 4 channels; a lane
+// adds its partials when the row's item changes and at the end (items span thousands of rows).
+constexpr int RS_ROWS = 2048;
+__global__ void reflect_add_stats_kernel(const float* y, const float* xs, const ItemTab* items, Dom d120, float* x,
+                                         double* part) {
+  const int warp = threadIdx.x >> 5, c = 4 * (threadIdx.x & 31);
+  const int r0 = blockIdx.x * RS_ROWS, r1 = min(d120.L, r0 + RS_ROWS);
+  int cb = -1;
+  float s[4] = {0.0f, 0.0f, 0.0f, 0.0f}, q[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+  auto flush = [&]() {
+    if (cb >= 0)
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        atomicAdd(part + ((long)cb * 128 + c + e) * 2, (double)s[e]);
+        atomicAdd(part + ((long)cb * 128 + c + e) * 2 + 1, (double)q[e]);
+        s[e] = q[e] = 0.0f;
+      }
+  };
+  for (int o = r0 + warp; o < r1; o += 8) {
+    const int b = dom_item(d120, o);
+    long src = -1;
+    if (b >= 0) {
+      const int st = 120 * items[b].a;
+      src = (o == st) ? (long)(st + 1) : (long)(o - 1);
+    }
+    float4 v = src >= 0 ? __ldg(reinterpret_cast<const float4*>(y + src * 128 + c)) : make_float4(0, 0, 0, 0);
+    const float4 a = __ldg(reinterpret_cast<const float4*>(xs + (long)o * 128 + c));
+    v.x += a.x, v.y += a.y, v.z += a.z, v.w += a.w;
+    *reinterpret_cast<float4*>(x + (long)o * 128 + c) = v;
+    if (b != cb) {
+      flush();
+      cb = b;
+    }
+    if (b >= 0) {
+      const float e4[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+      for (int e = 0; e < 4; e++) {
+        s[e] += e4[e];
+        q[e] = fmaf(e4[e], e4[e], q[e]);
+      }
+    }
+  }
+  flush();
+}
+
+cudaError_t launch_reflect_add_stats(const float* y, const float* xs, const ItemTab* items, Dom d120, float* x,
+                                     double* part, cudaStream_t st) {
+  if (d120.L == 0) return cudaSuccess;
+  reflect_add_stats_kernel<<<(d120.L + RS_ROWS - 1) / RS_ROWS, 256, 0, st>>>(y, xs, items, d120, x, part);
+  return cudaGetLastError();
+}
+
 // PCM_16 of every sample of the batch (src/wav.rs:76-84: s * 32767 rounded half to even, values
 // outside [-32768, 32767] (and NaN, stored as 0) clamped and counted per item).
 __global__ void pcm16_kernel(const float* audio, long n, const int* col_item_n, int16_t* out,

@@ -139,6 +139,10 @@ cudaError_t launch_sum3(const float* r0, const float* r1, const float* r2, float
 // stage-1 reflection pad (1, 0) per item plus the noise branch: x[o] = pad(y)[o] + xs[o]
 cudaError_t launch_reflect_add(const float* y, const float* xs, int C, const ItemTab* items, Dom d120,
                                float* x, cudaStream_t st);
+// the same for C = 128, adding the result's per-(item, channel) sum and sum of squares into part
+// (f64 [B][128][2], zeroed by the caller): the AdaIN statistics of the stage-1 input (BF16 mode)
+cudaError_t launch_reflect_add_stats(const float* y, const float* xs, const ItemTab* items, Dom d120, float* x,
+                                     double* part, cudaStream_t st);
 // PCM_16 conversion of n samples (600 per N-domain column) with per-item clip counts (pre-zeroed)
 cudaError_t launch_pcm16(const float* audio, long n, const int* col_item_n, int16_t* out, unsigned long long* clipped,
                          cudaStream_t st);
