@@ -883,8 +883,9 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
   // bf16 window planes in or out: 2 bytes per element
   const double in_b = a.in_mode == IN_PRE ? 2.0 : (a.x_b ? 12.0 : 4.0),
                out_b = (a.out_mode == OUT_GELU_PRE || a.out_mode == OUT_STORE_BF) ? 2.0 : 4.0;
-  const double bytes = in_b * in_rows * a.cin + out_b * (double)a.L_out * a.cout + (res ? 4.0 * a.L_out * a.cout : 0.0) +
-                       (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
+  const double out_bytes = out_b * (double)a.L_out * a.cout + (res ? 4.0 * a.L_out * a.cout : 0.0) +
+                           (tc_path ? (double)c.tc.bytes : 4.0 * c.cin * c.cout * c.K);
+  double bytes = in_b * in_rows * a.cin + out_bytes;
   if (tc_path) {
     unsigned long long* tr = nullptr;
     if (tc_trace_dir) {
@@ -901,6 +902,12 @@ void Engine::run_conv(const Conv& c, ConvArgs& a) {
       ap.pre_rows = PRE_PAD_FRONT + (long)a.L_in + PRE_PAD_BACK;
       void* xpre = ar.get<uint8_t>((size_t)((a.cin + 63) / 64) * 8 * ap.pre_rows * 16);
       check(launch_prologue_bf16(a, xpre, ap.pre_rows, st), "prologue_bf16");
+      // the transform is its own (HBM-bound) kernel: profiled as its own class, so the conv class
+      // is the tcgen05 kernel alone (which reads the bf16 planes)
+      const double planes = 2.0 * (double)ap.pre_rows * ((a.cin + 63) / 64) * 64;
+      prof_end(e0, "input_transform", 0.0, in_b * in_rows * a.cin + planes);
+      prof_begin(&e0);
+      bytes = 2.0 * in_rows * a.cin + out_bytes;
       ap.xpre = xpre;
       ap.in_mode = IN_PRE;
       ap.in_up2 = 0;
