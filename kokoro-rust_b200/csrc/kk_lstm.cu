@@ -214,8 +214,9 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_clu
 // Wh x [Hh | Hl] (N 64, columns 0..63) and Wl x Hh (N 32, accumulated into columns 32..63);
 // G = columns 0..31 + columns 32..63 / 2^11. A rows are ordered unit * 4 + gate, so
 // the four gates of a unit sit in four neighbouring TMEM lanes; a 4-lane transpose through shared
-// memory hands each thread one unit's four gates for 4 items. The new h is split into bf16 hi / lo
-// and written into this CTA's 4 KB slice of its own next H image; one bulk copy per other CTA
+// memory hands each thread one unit's four gates for 4 items. Each thread writes its new h, split
+// into fp16 big / scaled small parts, straight into this CTA's 4 KB slice of its own next H image
+// (and to the output); one bulk copy per other CTA
 // then sends the slice, completing bytes of the receiver's own mbarrier: each CTA waits (bounded)
 // for the 7 slices of the next step, so steps need no cluster barrier.
 
@@ -232,7 +233,7 @@ constexpr float LT_LO_SCALE = 2048.0f;                          // small parts a
 constexpr float LT_LO_INV = 1.0f / 2048.0f;
 
 __host__ __device__ constexpr size_t lt_smem() {
-  return 2 * (size_t)LT_ABYTES + 2 * (size_t)LT_BBYTES + sizeof(float) * (LC_IPG * LC_TLD + 8 * 32 * LT_GXLD);
+  return 2 * (size_t)LT_ABYTES + 2 * (size_t)LT_BBYTES + sizeof(float) * (8 * 32 * LT_GXLD);
 }
 
 // The cell's sigmoid with the hardware exponential and divide (a few ulp of fp32), and tanh x =
@@ -251,8 +252,7 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
   uint8_t* Ahi = sm8;
   uint8_t* Alo = Ahi + LT_ABYTES;
   uint8_t* Bb = Alo + LT_ABYTES;                                  // [2 stages] H images
-  float* Tile = reinterpret_cast<float*>(Bb + 2 * LT_BBYTES);     // [32 items][LC_TLD] new h (f32)
-  float* Gx = Tile + LC_IPG * LC_TLD;                             // [8 warps][32 lanes][LT_GXLD]
+  float* Gx = reinterpret_cast<float*>(Bb + 2 * LT_BBYTES);       // [8 warps][32 lanes][LT_GXLD]
   __shared__ uint64_t bar;
   __shared__ uint64_t hbar[2];  // H image j complete: the 8 CTAs' slices of the next step have landed
   __shared__ uint32_t tslot;
@@ -291,9 +291,6 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
 #pragma unroll
   for (int gt = 0; gt < 4; gt++) bh[gt] = a.bhh[dir * 4 * LC_H + gt * LC_H + u];
   float c[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-  // push role: item pi, part (0 hi, 1 lo), 8-unit chunk kc4 of this CTA's 32 units
-  const int pi = tid >> 3, part = (tid >> 2) & 1, kc4 = tid & 3;
-  const int pst = gs[pi], pln = gl[pi];
   const int* act = a.gact + (long)g * a.Tmax;
   // bytes the other 7 CTAs send during step s (into H image (s + 1) & 1): each copies its whole
   // 4 KB slice (rows of finished items are stale and ignored)
@@ -301,9 +298,7 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
     const int n = s + 1 < a.Tmax ? act[s + 1] : 0;
     return n > 0 ? (uint32_t)((LC_CL - 1) * LT_SLICE) : 0u;
   };
-  // this thread's row of this CTA's slice (in image 0), and the cluster addresses of the slice and
-  // of the H-image barriers in each CTA
-  uint8_t* lslot = Bb + (4 * rank + kc4) * (LT_HROWS * 16) + (part * LC_IPG + pi) * 16;
+  // the cluster addresses of this CTA's slice and of the H-image barriers in each CTA
   uint32_t rblk[LC_CL], rbar0[LC_CL];
   {
     const uint32_t blk = smem_u32(Bb + 4 * rank * (LT_HROWS * 16));
@@ -358,6 +353,8 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
     const int na = act[s];
     if (na == 0) break;  // same for the whole group, so for every CTA of the cluster
     const int cur = s & 1;
+    // this thread's unit column in this CTA's slice of the next H image (image cur ^ 1)
+    uint8_t* hrow = Bb + (cur ^ 1) * LT_BBYTES + (4 * rank + (ul >> 3)) * (LT_HROWS * 16) + (ul & 7) * 2;
     if (s > 0) {  // this step's H image: all 8 CTAs' slices of step s - 1 have landed
       if (!bad && !mbar_wait(&hbar[cur], hph[cur], &abort_flag, a.err)) bad = 1;
       hph[cur] ^= 1;
@@ -404,41 +401,26 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
           const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
           const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
           c[m] = fg * c[m] + ig * cg;
-          Tile[(i0 + m) * LC_TLD + ul] = og * tanh_fast(c[m]);
+          const float hv = og * tanh_fast(c[m]);
+          // the new h goes straight into this CTA's slice of the next H image (fp16 big part in
+          // row item, scaled small part in row 32 + item, unit ul's two bytes) and to the output
+          const uint32_t hb = f16_bits(hv);
+          *reinterpret_cast<unsigned short*>(hrow + (i0 + m) * 16) = (unsigned short)hb;
+          *reinterpret_cast<unsigned short*>(hrow + (LC_IPG + i0 + m) * 16) = (unsigned short)f16_lo_bits(hv, hb);
+          const int t = dir == 0 ? s : ln_[m] - 1 - s;
+          a.out[(long)(st_[m] + t) * a.ldo + dir * LC_H + u] = hv;
         }
       }
     }
     // re-arm image `cur` (consumed this step) for the pushes of step s + 1, before the barrier that
     // releases this CTA's own step-s pushes: no CTA can push step s + 1 before it has received them
     if (tid == 0 && !bad && push_bytes(s + 1)) mbar_arrive_expect_tx(&hbar[cur], push_bytes(s + 1));
-    tc_fence_before();
-    __syncthreads();  // Tile complete; TMEM and staging reads done
     const int na_next = s + 1 < a.Tmax ? act[s + 1] : 0;
-    if (!bad && pi < na) {
-      const float* hp = Tile + pi * LC_TLD + 8 * kc4;
-      uint32_t w4[4];
-#pragma unroll
-      for (int e = 0; e < 8; e += 2) {
-        uint32_t b0 = f16_bits(hp[e]), b1 = f16_bits(hp[e + 1]);
-        if (part == 1) {
-          b0 = f16_lo_bits(hp[e], b0);
-          b1 = f16_lo_bits(hp[e + 1], b1);
-        }
-        w4[e >> 1] = b0 | (b1 << 16);
-      }
-      if (pi < na_next)  // only items still running at step s + 1 are needed there
-        *reinterpret_cast<uint4*>(lslot + (cur ^ 1) * LT_BBYTES) = make_uint4(w4[0], w4[1], w4[2], w4[3]);
-      if (part == 0) {
-        const int t = dir == 0 ? s : pln - 1 - s;
-        float* o = a.out + (long)(pst + t) * a.ldo + dir * LC_H + rank * 32 + 8 * kc4;
-        *reinterpret_cast<float4*>(o) = make_float4(hp[0], hp[1], hp[2], hp[3]);
-        *reinterpret_cast<float4*>(o + 4) = make_float4(hp[4], hp[5], hp[6], hp[7]);
-      }
-    }
     // this CTA's slice of the next H image is complete: one bulk copy sends it to each other CTA
     // of the cluster, completing bytes of that CTA's barrier for the image
+    tc_fence_before();
     fence_proxy_async();
-    __syncthreads();
+    __syncthreads();  // slice complete; TMEM and staging reads done
     if (tid == 0 && !bad && na_next > 0) {
       const uint32_t src = smem_u32(Bb + (cur ^ 1) * LT_BBYTES + 4 * rank * (LT_HROWS * 16));
       const uint32_t off = (uint32_t)((cur ^ 1) * LT_BBYTES), boff = (uint32_t)((cur ^ 1) * 8);
