@@ -329,6 +329,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    # the library's host-side audio fetch uses up to 16 threads: share the host's cores among the
+    # ranks of this node
+    local_world = int(os.environ.get("LOCAL_WORLD_SIZE", "1"))
+    os.environ.setdefault("KK_FETCH_THREADS", str(max(1, min(16, (os.cpu_count() or 8) // max(1, local_world)))))
     kk = import_package()
 
     ckpt_dir = os.environ.get("KK_CKPT_DIR", tempfile.gettempdir())

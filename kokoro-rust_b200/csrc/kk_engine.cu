@@ -31,7 +31,15 @@ static void parallel_copy(int count, void* const* dst, const void* const* src, c
   size_t total = 0;
   for (int i = 0; i < count; i++) total += n[i];
   const size_t per_thread = size_t(8) << 20;  // below 8 MiB a thread is not worth starting
-  int T = (int)std::min<size_t>({size_t(8), (size_t)std::max(1u, std::thread::hardware_concurrency()),
+  // up to 16 threads (the first touch of fresh destination pages dominates, and it scales with
+  // threads); KK_FETCH_THREADS caps it, e.g. to the cores per process when several engines share
+  // one host
+  static const size_t cap = [] {
+    const char* e = getenv("KK_FETCH_THREADS");
+    const long v = e ? strtol(e, nullptr, 10) : 16;
+    return (size_t)std::max(1L, std::min(64L, v));
+  }();
+  int T = (int)std::min<size_t>({cap, (size_t)std::max(1u, std::thread::hardware_concurrency()),
                                  std::max<size_t>(1, total / per_thread)});
   if (T <= 1 || count <= 1) {
     for (int i = 0; i < count; i++) memcpy(dst[i], src[i], n[i]);
