@@ -95,6 +95,7 @@ struct TcArgs {
   int win_pad;    // window rows rounded to 8, + 1 (bank-conflict-free producer stores)
   int rst;        // input-box ring stages (0 on the pre-transform route)
   int xst;        // activation-window stages
+  int red;        // OUT_ADD without statistics: the TMA unit adds the staged result into y
   int epb;        // shared-memory bytes per epilogue warp
   int tab;        // AdaIN coefficients and Snake alphas come from shared-memory tables (cin <= TC_TAB)
   int* err;
@@ -429,7 +430,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
     const int ew = warp - 4;
     const int q = warp & 3;
     const int hrow = (ew >> 2) * TC_EROWS;
-    const bool need_res = out_mode_k == OUT_ADD || out_mode_k == OUT_PLUS;
+    // OUT_ADD without statistics needs no residual rows here: the staged acc + bias is added into
+    // y by a TMA reduce (the same single f32 addition, done in L2)
+    const bool red = out_mode_k == OUT_ADD && p.red;
+    const bool need_res = (out_mode_k == OUT_ADD && !red) || out_mode_k == OUT_PLUS;
     float* stg = (float*)(epi + ew * p.epb);                      // [2][16][32]
     float* rsb = stg + 2 * TC_EC * 32;                            // [TC_RES_DEPTH][16][32] (need_res)
     int* eit = (int*)(rsb + (need_res ? TC_RES_DEPTH : 0) * TC_EC * 32);  // [128]
@@ -579,7 +583,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
 #pragma unroll
           for (int jj = 0; jj < TC_EC; jj++) {
             float r = v[sub * TC_EC + jj] + bias;
-            if (out_mode == OUT_ADD) r = lds_f32(rrl + 128u * jj) + r;
+            if (out_mode == OUT_ADD && !red) r = lds_f32(rrl + 128u * jj) + r;
             else if (out_mode == OUT_PLUS) r = (r + lds_f32(rrl + 128u * jj)) * oscale;
             else if (out_mode == OUT_GELU) r = gelu_new(r);
             vals[jj] = r;
@@ -606,7 +610,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           fence_proxy_async();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
+            if (red)
+              tma_reduce_add_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
+            else
+              tma_store_2d(&p.ymap, co0, t0 + c * TC_EC, sb);
             bulk_commit();
           }
           if (need_res) {  // every lane has read this residual slot: refill it
@@ -1048,7 +1055,11 @@ static int ring_stages(int win_pad, int box_rows, int epb, bool tab) {
   return 0;
 }
 
-static int epb_of(const ConvArgs& a) { return tc_epi_warp_bytes(a.out_mode == OUT_ADD || a.out_mode == OUT_PLUS); }
+// OUT_ADD layers without fused statistics accumulate by TMA reduce (no residual boxes)
+static bool add_by_reduce(const ConvArgs& a) { return a.out_mode == OUT_ADD && !a.stat; }
+static int epb_of(const ConvArgs& a) {
+  return tc_epi_warp_bytes((a.out_mode == OUT_ADD && !add_by_reduce(a)) || a.out_mode == OUT_PLUS);
+}
 
 // The shared-memory coefficient tables serve affine prologues of up to TC_TAB input channels.
 static bool tab_of(const ConvArgs& a, int cin_pad) {
@@ -1147,6 +1158,7 @@ cudaError_t tc_conv(const ConvArgs& a, const TcWeights& t, int* err, cudaStream_
   p.win_pad = win_pad_of(a.K, a.dil);
   p.err = err;
   p.epb = epb_of(a);
+  p.red = add_by_reduce(a) ? 1 : 0;
   p.tab = !pre && tab_of(a, t.cin_pad);
   p.rst = pre ? 0 : ring_stages(p.win_pad, box_rows, p.epb, p.tab);
   p.xst = 2;
