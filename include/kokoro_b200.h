@@ -125,7 +125,8 @@ KK_API kk_status kk_fetch_audio(kk_engine* e, int item, float* dst, int64_t cap)
  * Copy every item's audio of the last forward at once: item i into dst[i] (capacity cap[i] floats),
  * on several host threads (the reference's forward_batch returns owned per-item Vec<f32>,
  * src/gpu_batch.rs:408-420; filling fresh caller buffers is page-fault bound, so the copies of
- * different items run in parallel). No counterpart in the reference.
+ * different items run in parallel: up to 16 threads, fewer when the environment variable
+ * KK_FETCH_THREADS, read once per process, says so). No counterpart in the reference.
  */
 KK_API kk_status kk_fetch_audio_all(kk_engine* e, float* const* dst, const int64_t* cap);
 
