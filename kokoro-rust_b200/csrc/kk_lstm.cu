@@ -390,25 +390,32 @@ __global__ void __cluster_dims__(LC_CL, 1, 1) __launch_bounds__(256, 1) lstm_tc_
 #pragma unroll
       for (int j = 0; j < 16; j++) gw[lane * LT_GXLD + j] = fmaf(w[j], LT_LO_INV, v[j]);
       __syncwarp();
+      // all four cells are computed unconditionally, so their chains interleave (the cell of an
+      // item that has finished, whose gate inputs are zeros, is discarded); only the stores depend
+      // on the item still running
+      float hv[4];
+#pragma unroll
+      for (int m = 0; m < 4; m++) {
+        float d[4];
+#pragma unroll
+        for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
+        const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
+        const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
+        const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
+        const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
+        c[m] = fg * c[m] + ig * cg;
+        hv[m] = og * tanh_fast(c[m]);
+      }
 #pragma unroll
       for (int m = 0; m < 4; m++) {
         if (i0 + m < na) {
-          float d[4];
-#pragma unroll
-          for (int gt = 0; gt < 4; gt++) d[gt] = gw[((lane & ~3) + gt) * LT_GXLD + 4 * (lane & 3) + m];
-          const float ig = sigm_fast(gxv[m][0] + (d[0] + bh[0]));
-          const float fg = sigm_fast(gxv[m][1] + (d[1] + bh[1]));
-          const float cg = tanh_fast(gxv[m][2] + (d[2] + bh[2]));
-          const float og = sigm_fast(gxv[m][3] + (d[3] + bh[3]));
-          c[m] = fg * c[m] + ig * cg;
-          const float hv = og * tanh_fast(c[m]);
           // the new h goes straight into this CTA's slice of the next H image (fp16 big part in
           // row item, scaled small part in row 32 + item, unit ul's two bytes) and to the output
-          const uint32_t hb = f16_bits(hv);
+          const uint32_t hb = f16_bits(hv[m]);
           *reinterpret_cast<unsigned short*>(hrow + (i0 + m) * 16) = (unsigned short)hb;
-          *reinterpret_cast<unsigned short*>(hrow + (LC_IPG + i0 + m) * 16) = (unsigned short)f16_lo_bits(hv, hb);
+          *reinterpret_cast<unsigned short*>(hrow + (LC_IPG + i0 + m) * 16) = (unsigned short)f16_lo_bits(hv[m], hb);
           const int t = dir == 0 ? s : ln_[m] - 1 - s;
-          a.out[(long)(st_[m] + t) * a.ldo + dir * LC_H + u] = hv;
+          a.out[(long)(st_[m] + t) * a.ldo + dir * LC_H + u] = hv[m];
         }
       }
     }
