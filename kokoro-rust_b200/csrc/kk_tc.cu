@@ -687,7 +687,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
 #pragma unroll
         for (int e = 0; e < 8; e++) chs[e] = chA + (e < 4 ? e : 28 + e);
         // channel pairs q = 0 .. 3: (chA, chA + 1), (chA + 2, chA + 3), (chA + 32, chA + 33), (chA + 34, chA + 35)
-        float2 al[4], ial[4], ca[4], cbb[4];
+        float2 al[4], ial[4], ca[4] = {}, cbb[4] = {};
         int cached = -1;
         if (snake) {
           if (tab) {  // (alpha, 1 / alpha) of the four pairs: 4 x 16 bytes
@@ -779,8 +779,64 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
           }
           if (++in_sl == RST) in_sl = 0, in_ph ^= 1;
           const uint32_t box = smem_u32(inring + sl * INBOX) + (uint32_t)(prow * TC_KB + 4 * j) * 4u;
+          constexpr int NH = BOXR / TC_PROWS;
+          bool done_fast = false;
+          if (!up2 && affine) {
+            // this thread's rows of the box at once: when every row is a gap or belongs to the
+            // cached item, compute all of them unconditionally (interleaved chains) and store with
+            // predicates; otherwise fall back to row-by-row emits
+            float vv[NH][8];
+            int rw[NH], bw[NH];
+            bool fast = true;
 #pragma unroll
-          for (int hh = 0; hh < BOXR / TC_PROWS; hh++) {
+            for (int hh = 0; hh < NH; hh++) {
+              const float4 lo = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB) * 4u);
+              const float4 hi = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB + 32) * 4u);
+              vv[hh][0] = lo.x, vv[hh][1] = lo.y, vv[hh][2] = lo.z, vv[hh][3] = lo.w;
+              vv[hh][4] = hi.x, vv[hh][5] = hi.y, vv[hh][6] = hi.z, vv[hh][7] = hi.w;
+              rw[hh] = i * BOXR + prow + TC_PROWS * hh;
+              bw[hh] = rw[hh] < win_rows ? lds_s32(ri + 4u * (uint32_t)rw[hh]) : -1;
+              fast = fast && (bw[hh] < 0 || bw[hh] == cached);
+            }
+            if (fast) {
+              uint4 pk[NH];
+#pragma unroll
+              for (int hh = 0; hh < NH; hh++) {
+                float o[8];
+#pragma unroll
+                for (int e = 0; e < 8; e += 2) {
+                  float2 t = __ffma2_rn(make_float2(vv[hh][e], vv[hh][e + 1]), ca[e >> 1], cbb[e >> 1]);
+                  if (snake) {
+                    const float2 arg = __fmul2_rn(al[e >> 1], t);
+                    const float2 sn = make_float2(__sinf(arg.x), __sinf(arg.y));
+                    t = __ffma2_rn(ial[e >> 1], __fmul2_rn(sn, sn), t);
+                  } else {
+                    t.x = leaky(t.x, slope);
+                    t.y = leaky(t.y, slope);
+                  }
+                  o[e] = t.x;
+                  o[e + 1] = t.y;
+                }
+                __nv_bfloat162 h0 = __floats2bfloat162_rn(o[0], o[1]), h1 = __floats2bfloat162_rn(o[2], o[3]);
+                __nv_bfloat162 h2 = __floats2bfloat162_rn(o[4], o[5]), h3 = __floats2bfloat162_rn(o[6], o[7]);
+                memcpy(&pk[hh].x, &h0, 4);
+                memcpy(&pk[hh].y, &h1, 4);
+                memcpy(&pk[hh].z, &h2, 4);
+                memcpy(&pk[hh].w, &h3, 4);
+                if (bw[hh] < 0) pk[hh] = make_uint4(0u, 0u, 0u, 0u);
+              }
+#pragma unroll
+              for (int hh = 0; hh < NH; hh++)
+                if (rw[hh] < win_rows) sts_u4(xb + (uint32_t)rw[hh] * 16u, pk[hh]);
+            } else {
+#pragma unroll
+              for (int hh = 0; hh < NH; hh++)
+                if (rw[hh] < win_rows) emit(rw[hh], vv[hh]);
+            }
+            done_fast = true;
+          }
+#pragma unroll
+          for (int hh = 0; hh < NH && !done_fast; hh++) {
             const int br = prow + TC_PROWS * hh;
             const float4 lo = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB) * 4u);
             const float4 hi = lds_f4(box + (uint32_t)(TC_PROWS * hh * TC_KB + 32) * 4u);
