@@ -878,33 +878,43 @@ __global__ void __launch_bounds__(TC_THREADS, 1) tc_conv_kernel(const __grid_con
 
 // ------------------------------------------------------------------------------ IN_PRE prologue
 
-// Block = 32 plane rows x 128 input channels (two 64-channel blocks), 8 warps. Warp w reads rows
-// 4w .. 4w + 3 of the tile as whole 512-byte row segments (lane l: channels 4l .. 4l + 3; all four
+// Block = 64 plane rows x 128 input channels (two 64-channel blocks), 8 warps. Warp w reads rows
+// 8w .. 8w + 7 of the tile as whole 512-byte row segments (lane l: channels 4l .. 4l + 3; all eight
 // rows' loads issued before any is used), applies the layer's prologue with the item's
 // coefficients cached across rows, and leaves bf16 values in a plane-major shared-memory tile
-// (plane stride padded to 33 rows: conflict-free 8-byte stores). Warp w then writes planes 2w and
-// 2w + 1: 32 consecutive 16-byte plane rows, 512 contiguous bytes each. Reads and writes of HBM
-// are both fully coalesced.
-__global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, uint4* __restrict__ out, long pre_rows,
+// (plane stride padded to 65 rows: conflict-free 8-byte stores). Warp w then writes planes 2w and
+// 2w + 1: 64 consecutive 16-byte plane rows, 1 KB contiguous each. Reads and writes of HBM
+// are both fully coalesced. The kernel issues about as many instructions as the SM can (ncu: issue
+// active 75%, DRAM 47% on the 256-channel layers), so per-row work is kept off the lanes: the
+// prologue is a template parameter, lane m < 8 looks up the item of row m (a frame-domain lookup
+// divides by the domain's scale) and the warp takes it by shuffle, and the AdaIN + Snake arithmetic
+// runs on channel pairs in packed f32x2 instructions (each lane rounds like the scalar fmaf /
+// multiply, so the planes are bit-identical to the scalar form). Four blocks of 64 rows per SM (64
+// registers) keep 256 rows in flight; 32-row blocks held 160-192 and ran the Snake layers 3% slower.
+template <int IM>
+__global__ void __launch_bounds__(256, 4) prologue_bf16_kernel(const ConvArgs a, uint4* __restrict__ out, long pre_rows,
                                                             int n_planes) {
-  __shared__ uint4 tile[16][33];
-  constexpr int RW = 4;  // rows per warp
+  __shared__ uint4 tile[16][65];
+  constexpr int RW = 8;  // rows per warp
+  constexpr bool affine = IM == IN_ADAIN_LEAKY || IM == IN_ADAIN_SNAKE;
+  constexpr bool snake = IM == IN_ADAIN_SNAKE;
+  constexpr bool leaky_on = IM == IN_ADAIN_LEAKY || IM == IN_LEAKY_MASK;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const long r0 = blockIdx.x * 32L;
+  const long r0 = blockIdx.x * 64L + warp * RW;  // this warp's first plane row
   const int cin = a.cin, c0 = blockIdx.y * 128 + 4 * lane;
-  const bool affine = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_ADAIN_SNAKE;
-  const bool snake = a.in_mode == IN_ADAIN_SNAKE;
-  const bool leaky_on = a.in_mode == IN_ADAIN_LEAKY || a.in_mode == IN_LEAKY_MASK;
   const bool full = c0 + 3 < cin;
-  int bm[RW];
+  auto row_in = [&](long r) {
+    const long g = r - PRE_PAD_FRONT;
+    return g >= 0 && g < a.L_in && r < pre_rows;
+  };
+  int bl = -1;  // lane m < RW: item of row r0 + m
+  if (lane < RW && row_in(r0 + lane)) bl = IM == IN_NOMASK ? 0 : dom_item(a.din, (int)(r0 + lane - PRE_PAD_FRONT));
   float4 v[RW];
 #pragma unroll
   for (int m = 0; m < RW; m++) {
-    const long r = r0 + warp * RW + m, g = r - PRE_PAD_FRONT;
-    const bool in = g >= 0 && g < a.L_in && r < pre_rows;
-    bm[m] = in ? (a.in_mode == IN_NOMASK ? 0 : dom_item(a.din, (int)g)) : -1;
+    const long r = r0 + m, g = r - PRE_PAD_FRONT;
     v[m] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-    if (in && c0 < cin) {
+    if (row_in(r) && c0 < cin) {
       const long off = (long)(a.in_up2 ? (g >> 1) : g) * a.ldx + c0;
       auto ld4 = [&](const float* base) {
         const float* src = base + off;
@@ -926,48 +936,54 @@ __global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, ui
       }
     }
   }
-  float al[4], ial[4];
+  // channel pairs (c0, c0 + 1) and (c0 + 2, c0 + 3)
+  float2 al[2], ial[2];
   if (snake) {
 #pragma unroll
     for (int e = 0; e < 4; e++) {
-      al[e] = c0 + e < cin ? __ldg(a.alpha + c0 + e) : 1.0f;
-      ial[e] = 1.0f / al[e];
+      const float av = c0 + e < cin ? __ldg(a.alpha + c0 + e) : 1.0f;
+      (e & 1 ? al[e >> 1].y : al[e >> 1].x) = av;
+      (e & 1 ? ial[e >> 1].y : ial[e >> 1].x) = __frcp_rn(av);  // = 1.0f / av (both correctly rounded)
     }
   }
   // plane of lane l's channels within the tile: block l / 16, chunk l % 8, half (l / 8) % 2
   const int tp = (lane >> 4) * 8 + (lane & 7), th = (lane >> 3) & 1;
-  float2 q[4];
+  float2 qs[2], qh[2];  // AdaIN (scale, shift) of the two channel pairs
   int cached = -1;
 #pragma unroll
   for (int m = 0; m < RW; m++) {
-    const int b = bm[m];
-    float o[4] = {v[m].x, v[m].y, v[m].z, v[m].w};
+    const int b = __shfl_sync(0xffffffffu, bl, m);
+    float2 o[2] = {make_float2(v[m].x, v[m].y), make_float2(v[m].z, v[m].w)};
     if (b < 0) {
-#pragma unroll
-      for (int e = 0; e < 4; e++) o[e] = 0.0f;
+      o[0] = o[1] = make_float2(0.0f, 0.0f);
     } else if (affine) {
       if (b != cached) {
         cached = b;
 #pragma unroll
-        for (int e = 0; e < 4; e++)
-          q[e] = c0 + e < cin ? __ldg(a.coef + (long)b * cin + c0 + e) : make_float2(0.0f, 0.0f);
+        for (int e = 0; e < 4; e++) {
+          const float2 q = c0 + e < cin ? __ldg(a.coef + (long)b * cin + c0 + e) : make_float2(0.0f, 0.0f);
+          (e & 1 ? qs[e >> 1].y : qs[e >> 1].x) = q.x;
+          (e & 1 ? qh[e >> 1].y : qh[e >> 1].x) = q.y;
+        }
       }
 #pragma unroll
-      for (int e = 0; e < 4; e++) {
-        float t = fmaf(o[e], q[e].x, q[e].y);
+      for (int h = 0; h < 2; h++) {
+        float2 t = __ffma2_rn(o[h], qs[h], qh[h]);
         if (snake) {
-          const float sn = __sinf(al[e] * t);
-          t = fmaf(ial[e], sn * sn, t);
+          const float2 arg = __fmul2_rn(al[h], t);
+          const float2 sn = make_float2(__sinf(arg.x), __sinf(arg.y));
+          t = __ffma2_rn(ial[h], __fmul2_rn(sn, sn), t);
         } else {
-          t = leaky(t, a.slope);
+          t.x = leaky(t.x, a.slope);
+          t.y = leaky(t.y, a.slope);
         }
-        o[e] = t;
+        o[h] = t;
       }
     } else if (leaky_on) {
 #pragma unroll
-      for (int e = 0; e < 4; e++) o[e] = leaky(o[e], a.slope);
+      for (int h = 0; h < 2; h++) o[h] = make_float2(leaky(o[h].x, a.slope), leaky(o[h].y, a.slope));
     }
-    __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0], o[1]), p1 = __floats2bfloat162_rn(o[2], o[3]);
+    __nv_bfloat162 p0 = __floats2bfloat162_rn(o[0].x, o[0].y), p1 = __floats2bfloat162_rn(o[1].x, o[1].y);
     uint2 u;
     memcpy(&u.x, &p0, 4);
     memcpy(&u.y, &p1, 4);
@@ -975,18 +991,31 @@ __global__ void __launch_bounds__(256) prologue_bf16_kernel(const ConvArgs a, ui
   }
   __syncthreads();
 #pragma unroll
-  for (int k = 0; k < 2; k++) {
-    const int p = 2 * warp + k, plane = blockIdx.y * 16 + p;
-    const long r = r0 + lane;
-    if (plane < n_planes && r < pre_rows) out[(long)plane * pre_rows + r] = tile[p][lane];
+  for (int k = 0; k < 4; k++) {
+    const int p = 2 * warp + (k >> 1), plane = blockIdx.y * 16 + p, rr = (k & 1) * 32 + lane;
+    const long r = blockIdx.x * 64L + rr;
+    if (plane < n_planes && r < pre_rows) out[(long)plane * pre_rows + r] = tile[p][rr];
   }
 }
 
 cudaError_t launch_prologue_bf16(const ConvArgs& a, void* xpre, long pre_rows, cudaStream_t st) {
   const int ncb = (a.cin + TC_KB - 1) / TC_KB;
   if (a.ldx % 4 != 0 || (((uintptr_t)a.x) & 15) != 0) return cudaErrorInvalidValue;
-  prologue_bf16_kernel<<<dim3((unsigned)((pre_rows + 31) / 32), (ncb + 1) / 2), 256, 0, st>>>(a, (uint4*)xpre,
-                                                                                             pre_rows, ncb * 8);
+  const dim3 grid((unsigned)((pre_rows + 63) / 64), (ncb + 1) / 2);
+  switch (a.in_mode) {
+    case IN_NOMASK: prologue_bf16_kernel<IN_NOMASK><<<grid, 256, 0, st>>>(a, (uint4*)xpre, pre_rows, ncb * 8); break;
+    case IN_MASK: prologue_bf16_kernel<IN_MASK><<<grid, 256, 0, st>>>(a, (uint4*)xpre, pre_rows, ncb * 8); break;
+    case IN_ADAIN_LEAKY:
+      prologue_bf16_kernel<IN_ADAIN_LEAKY><<<grid, 256, 0, st>>>(a, (uint4*)xpre, pre_rows, ncb * 8);
+      break;
+    case IN_ADAIN_SNAKE:
+      prologue_bf16_kernel<IN_ADAIN_SNAKE><<<grid, 256, 0, st>>>(a, (uint4*)xpre, pre_rows, ncb * 8);
+      break;
+    case IN_LEAKY_MASK:
+      prologue_bf16_kernel<IN_LEAKY_MASK><<<grid, 256, 0, st>>>(a, (uint4*)xpre, pre_rows, ncb * 8);
+      break;
+    default: return cudaErrorInvalidValue;
+  }
   return cudaGetLastError();
 }
 
