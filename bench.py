@@ -314,7 +314,7 @@ def main():
     ap.add_argument("--precision", default=os.environ.get("KK_PRECISION", "bf16"), choices=["bf16", "fp32"])
     ap.add_argument("--cpu-lines", type=int, default=3, help="lines in the CPU-baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--launch-log", default=None, help="write every profiled launch (class, ms, FLOPs, bytes) as CSV")
+    ap.add_argument("--launch-log", default=None, help="write every profiled launch (class, ms, FLOPs, bytes) of the PROF_STEPS profiled steps as CSV")
     ap.add_argument("--items", type=int, default=32, help="config2: utterances per batch")
     ap.add_argument("--frames", type=int, default=400, help="config2: frames per utterance")
     ap.add_argument("--lines", type=int, default=20000, help="config5: lines of the book")
